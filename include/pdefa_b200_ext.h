@@ -1,0 +1,98 @@
+/* pdefa_b200_ext.h - additive entry points of the B200 build of libpdefa_native.so.
+ *
+ * These have no counterpart in the reference ABI (pdefa/pdefa.def); they are extra
+ * exports, so the reference ctypes layer is unaffected. They expose what a GPU
+ * engine needs beyond the CPU engine's surface: precision and device selection,
+ * device-pointer execution, the batched YOLO decode/NMS that replaces the
+ * reference's pure-Python decode_yolo (pdefa/python/src/pdefa/_bindings.py:1095-1212),
+ * and the multi-GPU batch runner behind BatchInference (pdefa/python/src/pdefa/batch.py:13-70).
+ * All pointers are plain host or device pointers; no framework types cross the ABI.
+ */
+#ifndef PDEFA_B200_EXT_H
+#define PDEFA_B200_EXT_H
+
+#include <stdint.h>
+#include "engine_c_api.h"
+#include "pdefa_c_api.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Arithmetic used by sessions created from a context.
+ * FP32: strict fp32 SIMT kernels (parity <= 1e-5 with the reference engine).
+ * TF32 / BF16: tcgen05 tensor-core kernels with fp32 accumulation (<= 1e-2). */
+typedef enum {
+    PDEFA_PREC_FP32 = 0,
+    PDEFA_PREC_TF32 = 1,
+    PDEFA_PREC_BF16 = 2
+} PdefaPrecision;
+
+ENGINE_API EngineStatus engine_context_set_precision(EngineContext* ctx, int32_t precision);
+ENGINE_API int32_t      engine_context_get_precision(const EngineContext* ctx);
+ENGINE_API EngineStatus engine_context_set_device(EngineContext* ctx, int32_t device);
+ENGINE_API int32_t      engine_context_get_device(const EngineContext* ctx);
+/* Number of visible CUDA devices (0 without a GPU). */
+ENGINE_API int32_t      engine_device_count(void);
+/* Sticky device-side error word set by bounded waits that timed out (0 = none). */
+ENGINE_API int32_t      engine_device_error(int32_t device);
+
+/* Run a session on device buffers already resident on the session's GPU.
+ * d_input: [batch, C, H, W] fp32 NCHW; d_output: graph output 0 for `batch` images
+ * (shape from engine_session_output_shape). stream: cudaStream_t or NULL for the
+ * session's own stream. Returns after the work is enqueued (asynchronous). */
+ENGINE_API EngineStatus engine_session_run_device(EngineSession* sess, const float* d_input,
+                                                  int64_t batch, float* d_output, void* stream);
+ENGINE_API EngineStatus engine_session_output_shape(const EngineSession* sess, int32_t index,
+                                                    int64_t batch, int64_t* out_shape,
+                                                    int32_t* out_ndim);
+/* Number of kernel launches one engine_session_run_device call issues. */
+ENGINE_API int64_t      engine_session_launch_count(const EngineSession* sess, int64_t batch);
+
+/* C[M,N] = A[M,K] * B[K,N], row-major fp32 device pointers on the current device. */
+ENGINE_API EngineStatus engine_gemm_f32_device(const float* d_a, const float* d_b, float* d_c,
+                                               int64_t m, int64_t n, int64_t k,
+                                               int32_t precision, void* stream);
+/* engine_ops_matmul with an explicit precision (PdefaPrecision). */
+ENGINE_API EngineStatus engine_ops_matmul_ex(const EngineTensor* a, const EngineTensor* b,
+                                             EngineTensor* out, int32_t precision);
+
+/* One kept detection; boxes are float64 exactly as the reference decode computes them. */
+typedef struct {
+    double  x1, y1, x2, y2;
+    float   conf;
+    int32_t cls;
+    int32_t anchor;
+    int32_t reserved;
+} PdefaDetection;
+
+/* Batched decode_yolo + class-wise NMS on the GPU.
+ * preds: [batch, channels, anchors] fp32 (host pointer, or device pointer on
+ * `device` when preds_on_device != 0). metas: NULL or `batch` letterbox records.
+ * out_counts[batch] and out_dets[batch * max_det] are host arrays. */
+ENGINE_API EngineStatus pdefa_decode_yolo(const float* preds, int32_t preds_on_device,
+                                          int64_t batch, int64_t channels, int64_t anchors,
+                                          const PdefaPreprocessMeta* metas,
+                                          double conf_thres, double iou_thres, int32_t max_det,
+                                          int32_t* out_counts, PdefaDetection* out_dets,
+                                          int32_t device);
+
+/* Multi-GPU batch runner: one replica of `model` per device, contiguous shards, no
+ * collective. Each device runs its shard's inference and decode and returns only
+ * detections. */
+typedef struct PdefaBatchRunner PdefaBatchRunner;
+ENGINE_API EngineStatus pdefa_batch_create(EngineModel* model, int32_t n_devices,
+                                           const int32_t* devices, int32_t precision,
+                                           int64_t max_images_per_device,
+                                           PdefaBatchRunner** out_runner);
+/* images: [n_images, C, H, W] fp32 host array. */
+ENGINE_API EngineStatus pdefa_batch_run(PdefaBatchRunner* runner, const float* images,
+                                        int64_t n_images, const PdefaPreprocessMeta* metas,
+                                        double conf_thres, double iou_thres, int32_t max_det,
+                                        int32_t* out_counts, PdefaDetection* out_dets);
+ENGINE_API void         pdefa_batch_destroy(PdefaBatchRunner* runner);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* PDEFA_B200_EXT_H */

@@ -1,0 +1,302 @@
+// Additive entry points (include/pdefa_b200_ext.h): precision/device selection,
+// device-pointer execution, tensor-core GEMM, batched GPU decode/NMS and the
+// multi-GPU batch runner (one replica per device, contiguous shards, no collective).
+#include <thread>
+
+#include "../../include/pdefa_b200_ext.h"
+#include "kernels.h"
+#include "runtime.h"
+
+using namespace pb;
+
+namespace {
+
+// Per-device scratch kept across calls (GEMM operand staging).
+struct Scratch {
+    void* p = nullptr;
+    size_t n = 0;
+};
+std::mutex g_scratch_mu;
+Scratch g_scratch[64];
+
+void* scratch(int dev, size_t n) {
+    std::lock_guard<std::mutex> lk(g_scratch_mu);
+    Scratch& s = g_scratch[dev];
+    if (s.n < n) {
+        if (s.p) cudaFree(s.p);
+        s.p = nullptr;
+        s.n = 0;
+        if (cudaMalloc(&s.p, n) != cudaSuccess) { cudaGetLastError(); fail(ENGINE_ERR_OUT_OF_MEMORY, "scratch allocation failed"); }
+        s.n = n;
+    }
+    return s.p;
+}
+
+struct DeviceBuffer {
+    void* p = nullptr;
+    explicit DeviceBuffer(size_t n) {
+        if (cudaMalloc(&p, std::max<size_t>(n, 16)) != cudaSuccess) {
+            cudaGetLastError();
+            fail(ENGINE_ERR_OUT_OF_MEMORY, "device allocation failed");
+        }
+    }
+    ~DeviceBuffer() { if (p) cudaFree(p); }
+};
+
+void decode_on_device(const float* d_preds, int64_t batch, int64_t channels, int64_t anchors,
+                      const PdefaPreprocessMeta* metas, double conf, double iou, int32_t max_det,
+                      int32_t* d_counts, void* d_dets, void* d_work, int32_t* d_meta, int* err, cudaStream_t s) {
+    if (metas) PB_CUDA(cudaMemcpyAsync(d_meta, metas, (size_t)batch * sizeof(PdefaPreprocessMeta), cudaMemcpyHostToDevice, s));
+    DecodeArgs a;
+    a.preds = d_preds;
+    a.batch = batch; a.channels = channels; a.anchors = anchors;
+    a.meta = metas ? d_meta : nullptr;
+    a.conf = conf; a.iou = iou; a.max_det = max_det;
+    a.counts = d_counts; a.dets = d_dets; a.work = d_work; a.err = err;
+    launch_decode_nms(a, s);
+}
+
+}  // namespace
+
+struct PdefaBatchRunner {
+    struct Replica {
+        int device = 0;
+        cudaStream_t stream = nullptr;
+        std::map<int64_t, std::unique_ptr<Plan>> plans;
+        void* counts = nullptr;
+        void* dets = nullptr;
+        void* work = nullptr;
+        void* meta = nullptr;
+        size_t dets_cap = 0;
+    };
+    std::shared_ptr<const Graph> graph;
+    int precision = PREC_BF16;
+    int64_t max_per_device = 1;
+    std::vector<Replica> reps;
+};
+
+extern "C" {
+
+ENGINE_API EngineStatus engine_context_set_precision(EngineContext* ctx, int32_t precision) {
+    if (!ctx || ctx->magic != kMagicContext) return ENGINE_ERR_INVALID_HANDLE;
+    if (precision < PREC_FP32 || precision > PREC_BF16) return ENGINE_ERR_INVALID_ARG;
+    ctx->precision = precision;
+    return ENGINE_OK;
+}
+ENGINE_API int32_t engine_context_get_precision(const EngineContext* ctx) {
+    return (ctx && ctx->magic == kMagicContext) ? ctx->precision : -1;
+}
+ENGINE_API EngineStatus engine_context_set_device(EngineContext* ctx, int32_t device) {
+    if (!ctx || ctx->magic != kMagicContext) return ENGINE_ERR_INVALID_HANDLE;
+    if (device < 0) return ENGINE_ERR_INVALID_ARG;
+    ctx->device = device;
+    return ENGINE_OK;
+}
+ENGINE_API int32_t engine_context_get_device(const EngineContext* ctx) {
+    return (ctx && ctx->magic == kMagicContext) ? ctx->device : -1;
+}
+ENGINE_API int32_t engine_device_count(void) { return pb::device_count(); }
+ENGINE_API int32_t engine_device_error(int32_t device) {
+    try { return read_device_error(device); } catch (...) { return -1; }
+}
+
+ENGINE_API EngineStatus engine_session_run_device(EngineSession* sess, const float* d_input, int64_t batch,
+                                                  float* d_output, void* stream) {
+    if (!sess || sess->magic != kMagicSession) return ENGINE_ERR_INVALID_HANDLE;
+    if (!d_input) return ENGINE_ERR_NULL_PTR;
+    return guarded([&]() -> EngineStatus {
+        std::lock_guard<std::mutex> lk(sess->mu);
+        clear_error();
+        PB_CUDA(cudaSetDevice(sess->device));
+        cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : sess->stream;
+        Plan& p = sess->plan_for(batch);
+        p.run(s, d_input, nullptr);
+        if (d_output && d_output != p.output_buffer(0))
+            PB_CUDA(cudaMemcpyAsync(d_output, p.output_buffer(0), p.output_bytes(0), cudaMemcpyDeviceToDevice, s));
+        return ENGINE_OK;
+    });
+}
+ENGINE_API EngineStatus engine_session_output_shape(const EngineSession* sess, int32_t index, int64_t batch,
+                                                    int64_t* out_shape, int32_t* out_ndim) {
+    if (!sess || sess->magic != kMagicSession) return ENGINE_ERR_INVALID_HANDLE;
+    return guarded([&]() -> EngineStatus {
+        Plan& p = const_cast<EngineSession*>(sess)->plan_for(batch);
+        if (index < 0 || index >= p.num_outputs()) return ENGINE_ERR_INVALID_ARG;
+        const auto& s = p.output_shape(index);
+        if (out_shape) for (size_t i = 0; i < s.size(); ++i) out_shape[i] = s[i];
+        if (out_ndim) *out_ndim = (int32_t)s.size();
+        return ENGINE_OK;
+    });
+}
+ENGINE_API int64_t engine_session_launch_count(const EngineSession* sess, int64_t batch) {
+    if (!sess || sess->magic != kMagicSession) return -1;
+    try {
+        return const_cast<EngineSession*>(sess)->plan_for(batch).launch_count();
+    } catch (...) {
+        return -1;
+    }
+}
+
+ENGINE_API EngineStatus engine_gemm_f32_device(const float* d_a, const float* d_b, float* d_c, int64_t m, int64_t n,
+                                               int64_t k, int32_t precision, void* stream) {
+    if (!d_a || !d_b || !d_c) return ENGINE_ERR_NULL_PTR;
+    return guarded([&]() -> EngineStatus {
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        int dev = 0;
+        PB_CUDA(cudaGetDevice(&dev));
+        if (precision != PREC_FP32) {
+            const int op_dt = precision == PREC_BF16 ? BF16 : F32;
+            const int esz = op_dt == BF16 ? 2 : 4;
+            const bool ok = n % 16 == 0 && k % (op_dt == BF16 ? 16 : 8) == 0 && ((uintptr_t)d_c % 16) == 0;
+            if (ok) {
+                void* sc = scratch(dev, ((size_t)m * k + (size_t)n * k) * esz + 256);
+                launch_gemm_tc(d_a, d_b, d_c, m, n, k, op_dt, sc, device_error_word(dev), s);
+                return ENGINE_OK;
+            }
+        }
+        launch_gemm_f32(d_a, d_b, d_c, nullptr, m, n, k, k, n, n, 1, 0, 0, 0, s);
+        return ENGINE_OK;
+    });
+}
+
+ENGINE_API EngineStatus pdefa_decode_yolo(const float* preds, int32_t preds_on_device, int64_t batch, int64_t channels,
+                                          int64_t anchors, const PdefaPreprocessMeta* metas, double conf_thres,
+                                          double iou_thres, int32_t max_det, int32_t* out_counts,
+                                          PdefaDetection* out_dets, int32_t device) {
+    if (!preds || !out_counts || (!out_dets && max_det > 0)) return ENGINE_ERR_NULL_PTR;
+    return guarded([&]() -> EngineStatus {
+        clear_error();
+        if (batch < 0 || channels < 5 || anchors < 0) { set_error("decode: bad shape"); return ENGINE_ERR_INVALID_SHAPE; }
+        if (max_det < 0) { set_error("decode: max_det must be >= 0"); return ENGINE_ERR_INVALID_ARG; }
+        if (batch == 0) return ENGINE_OK;
+        require_device(device);
+        PB_CUDA(cudaSetDevice(device));
+        cudaStream_t s;
+        PB_CUDA(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
+        struct SG { cudaStream_t s; ~SG() { cudaStreamSynchronize(s); cudaStreamDestroy(s); } } sg{s};
+        const size_t pbytes = (size_t)batch * channels * anchors * 4;
+        std::unique_ptr<DeviceBuffer> dpred;
+        const float* dp = preds;
+        if (!preds_on_device) {
+            dpred = std::make_unique<DeviceBuffer>(pbytes);
+            PB_CUDA(cudaMemcpyAsync(dpred->p, preds, pbytes, cudaMemcpyHostToDevice, s));
+            dp = static_cast<const float*>(dpred->p);
+        }
+        DeviceBuffer counts((size_t)batch * 4), dets((size_t)batch * std::max(1, max_det) * sizeof(PdefaDetection));
+        DeviceBuffer work(decode_work_bytes(batch, anchors)), meta((size_t)batch * sizeof(PdefaPreprocessMeta));
+        int* err = device_error_word(device);
+        decode_on_device(dp, batch, channels, anchors, metas, conf_thres, iou_thres, max_det,
+                         static_cast<int32_t*>(counts.p), dets.p, work.p, static_cast<int32_t*>(meta.p), err, s);
+        PB_CUDA(cudaMemcpyAsync(out_counts, counts.p, (size_t)batch * 4, cudaMemcpyDeviceToHost, s));
+        if (max_det > 0)
+            PB_CUDA(cudaMemcpyAsync(out_dets, dets.p, (size_t)batch * max_det * sizeof(PdefaDetection),
+                                    cudaMemcpyDeviceToHost, s));
+        PB_CUDA(cudaStreamSynchronize(s));
+        for (int64_t b = 0; b < batch; ++b)
+            if (out_counts[b] < 0) { set_error("decode: more than 16384 candidates in one image"); return ENGINE_ERR_NOT_IMPL; }
+        return ENGINE_OK;
+    });
+}
+
+ENGINE_API EngineStatus pdefa_batch_create(EngineModel* model, int32_t n_devices, const int32_t* devices,
+                                           int32_t precision, int64_t max_images_per_device,
+                                           PdefaBatchRunner** out_runner) {
+    if (!out_runner) return ENGINE_ERR_NULL_PTR;
+    *out_runner = nullptr;
+    if (!model || model->magic != kMagicModel) return ENGINE_ERR_INVALID_HANDLE;
+    return guarded([&]() -> EngineStatus {
+        clear_error();
+        if (n_devices < 1 || max_images_per_device < 1) return ENGINE_ERR_INVALID_ARG;
+        auto r = std::make_unique<PdefaBatchRunner>();
+        r->graph = model->graph;
+        r->precision = precision;
+        r->max_per_device = max_images_per_device;
+        r->reps.resize(n_devices);
+        for (int i = 0; i < n_devices; ++i) {
+            auto& rp = r->reps[i];
+            rp.device = devices ? devices[i] : i;
+            require_device(rp.device);
+            PB_CUDA(cudaSetDevice(rp.device));
+            PB_CUDA(cudaStreamCreateWithFlags(&rp.stream, cudaStreamNonBlocking));
+        }
+        *out_runner = r.release();
+        return ENGINE_OK;
+    });
+}
+
+ENGINE_API EngineStatus pdefa_batch_run(PdefaBatchRunner* r, const float* images, int64_t n_images,
+                                        const PdefaPreprocessMeta* metas, double conf_thres, double iou_thres,
+                                        int32_t max_det, int32_t* out_counts, PdefaDetection* out_dets) {
+    if (!r || !images || !out_counts || (!out_dets && max_det > 0)) return ENGINE_ERR_NULL_PTR;
+    return guarded([&]() -> EngineStatus {
+        clear_error();
+        if (max_det < 0) return ENGINE_ERR_INVALID_ARG;
+        const int nd = (int)r->reps.size();
+        const int64_t per = (n_images + nd - 1) / nd;
+        std::vector<std::string> errs(nd);
+        std::vector<std::thread> th;
+        for (int d = 0; d < nd; ++d) {
+            th.emplace_back([&, d] {
+                try {
+                    auto& rp = r->reps[d];
+                    PB_CUDA(cudaSetDevice(rp.device));
+                    const int64_t lo = std::min(n_images, d * per), hi = std::min(n_images, lo + per);
+                    for (int64_t c0 = lo; c0 < hi; c0 += r->max_per_device) {
+                        const int64_t nb = std::min(r->max_per_device, hi - c0);
+                        auto it = rp.plans.find(nb);
+                        if (it == rp.plans.end())
+                            it = rp.plans.emplace(nb, std::make_unique<Plan>(r->graph, nb, r->precision, rp.device)).first;
+                        Plan& p = *it->second;
+                        const auto& os = p.output_shape(0);
+                        if (os.size() != 3) fail(ENGINE_ERR_INVALID_SHAPE, "batch runner expects a [B, 4+nc, A] output");
+                        const int64_t ch = os[1], A = os[2];
+                        const size_t need = (size_t)nb * std::max(1, max_det) * sizeof(PdefaDetection);
+                        if (rp.dets_cap < need || !rp.work) {
+                            if (rp.counts) { cudaFree(rp.counts); cudaFree(rp.dets); cudaFree(rp.work); cudaFree(rp.meta); }
+                            const int64_t cap_imgs = r->max_per_device;
+                            PB_CUDA(cudaMalloc(&rp.counts, cap_imgs * 4));
+                            const size_t dc = (size_t)cap_imgs * std::max(1, max_det) * sizeof(PdefaDetection);
+                            PB_CUDA(cudaMalloc(&rp.dets, dc));
+                            PB_CUDA(cudaMalloc(&rp.work, decode_work_bytes(cap_imgs, A)));
+                            PB_CUDA(cudaMalloc(&rp.meta, cap_imgs * sizeof(PdefaPreprocessMeta)));
+                            rp.dets_cap = dc;
+                        }
+                        const size_t ibytes = p.input_bytes(0);
+                        PB_CUDA(cudaMemcpyAsync(p.input_buffer(0), images + c0 * (ibytes / 4 / nb), ibytes,
+                                                cudaMemcpyHostToDevice, rp.stream));
+                        p.run(rp.stream);
+                        decode_on_device(p.output_buffer(0), nb, ch, A, metas ? metas + c0 : nullptr, conf_thres,
+                                         iou_thres, max_det, static_cast<int32_t*>(rp.counts), rp.dets, rp.work,
+                                         static_cast<int32_t*>(rp.meta), device_error_word(rp.device), rp.stream);
+                        PB_CUDA(cudaMemcpyAsync(out_counts + c0, rp.counts, nb * 4, cudaMemcpyDeviceToHost, rp.stream));
+                        if (max_det > 0)
+                            PB_CUDA(cudaMemcpyAsync(out_dets + c0 * max_det, rp.dets, (size_t)nb * max_det * sizeof(PdefaDetection),
+                                                    cudaMemcpyDeviceToHost, rp.stream));
+                        PB_CUDA(cudaStreamSynchronize(rp.stream));
+                    }
+                    if (read_device_error(rp.device)) fail(ENGINE_ERR_RUNTIME, "device-side wait timed out");
+                } catch (const std::exception& e) {
+                    errs[d] = e.what();
+                }
+            });
+        }
+        for (auto& t : th) t.join();
+        for (int d = 0; d < nd; ++d)
+            if (!errs[d].empty()) { set_error("device " + std::to_string(r->reps[d].device) + ": " + errs[d]); return ENGINE_ERR_RUNTIME; }
+        return ENGINE_OK;
+    });
+}
+
+ENGINE_API void pdefa_batch_destroy(PdefaBatchRunner* r) {
+    if (!r) return;
+    for (auto& rp : r->reps) {
+        cudaSetDevice(rp.device);
+        if (rp.stream) cudaStreamSynchronize(rp.stream);
+        rp.plans.clear();
+        if (rp.counts) { cudaFree(rp.counts); cudaFree(rp.dets); cudaFree(rp.work); cudaFree(rp.meta); }
+        if (rp.stream) cudaStreamDestroy(rp.stream);
+    }
+    delete r;
+}
+
+}  // extern "C"

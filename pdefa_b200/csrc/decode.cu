@@ -1,0 +1,271 @@
+// Batched YOLO decode + class-wise greedy NMS, bit-exact with the reference's
+// pure-Python decode_yolo / _nms / _iou (pdefa/python/src/pdefa/_bindings.py:1095-1212).
+//
+// One CTA (1024 threads) per image:
+//  1. candidates in anchor order: class argmax (strict '>', first maximum wins),
+//     skip when best < conf; box (cx - w*0.5, cy - h*0.5, cx + w*0.5, cy + h*0.5) in
+//     float64; optional letterbox unmap (v - pad) * (1.0 / ratio) clamped to
+//     [0, orig] -- all with round-to-nearest float64 intrinsics, no contraction.
+//     Order-preserving compaction uses warp ballots and a block scan.
+//  2. class groups are ranked by the position of their first candidate (the
+//     insertion order of the reference's defaultdict).
+//  3. keys (group, conf desc, candidate index) are bitonic-sorted in shared memory,
+//     which reproduces the reference's stable sort by confidence inside each group.
+//  4. one warp per class group runs the greedy scan: keep the next unsuppressed box,
+//     suppress later boxes whose IoU is not <= iou_thres (IoU = inter /
+//     (area_a + area_b - inter + 1e-9), 0 when the overlap is empty).
+//  5. kept boxes are re-sorted by (conf desc, group, index) -- the reference's final
+//     stable sort of keep_all -- and the first max_det are written out.
+// Limit: at most 16384 anchors per image (keys live in shared memory).
+#include <cfloat>
+#include <climits>
+
+#include "common.h"
+#include "device_common.cuh"
+
+namespace pb {
+
+namespace {
+
+constexpr int kThreads = 1024;
+constexpr int kMaxKeys = 16384;
+constexpr int kMaxClasses = 1024;
+
+struct Det {
+    double x1, y1, x2, y2;
+    float conf;
+    int32_t cls;
+    int32_t anchor;
+    int32_t reserved;
+};
+static_assert(sizeof(Det) == 48, "Det must match PdefaDetection");
+
+__device__ __forceinline__ uint32_t desc_key(float f) {
+    uint32_t u = __float_as_uint(f == 0.0f ? 0.0f : f);       // -0.0 orders as +0.0
+    const uint32_t asc = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    return ~asc;
+}
+
+__device__ __forceinline__ double iou_ref(const Det& a, const Det& b) {
+    const double x1 = a.x1 > b.x1 ? a.x1 : b.x1;
+    const double y1 = a.y1 > b.y1 ? a.y1 : b.y1;
+    const double x2 = a.x2 < b.x2 ? a.x2 : b.x2;
+    const double y2 = a.y2 < b.y2 ? a.y2 : b.y2;
+    const double w = __dsub_rn(x2, x1);
+    const double h = __dsub_rn(y2, y1);
+    if (w <= 0.0 || h <= 0.0) return 0.0;
+    const double inter = __dmul_rn(w, h);
+    const double area_a = __dmul_rn(__dsub_rn(a.x2, a.x1), __dsub_rn(a.y2, a.y1));
+    const double area_b = __dmul_rn(__dsub_rn(b.x2, b.x1), __dsub_rn(b.y2, b.y1));
+    return __ddiv_rn(inter, __dadd_rn(__dsub_rn(__dadd_rn(area_a, area_b), inter), 1e-9));
+}
+
+__device__ __forceinline__ double clamp_ref(double v, double hi) {
+    return v < 0.0 ? 0.0 : (v > hi ? hi : v);
+}
+
+__device__ void bitonic_sort(unsigned long long* keys, int np) {
+    for (int k = 2; k <= np; k <<= 1) {
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            for (int i = threadIdx.x; i < np; i += kThreads) {
+                const int ixj = i ^ j;
+                if (ixj > i) {
+                    const unsigned long long a = keys[i], b = keys[ixj];
+                    const bool asc = (i & k) == 0;
+                    if ((a > b) == asc) { keys[i] = b; keys[ixj] = a; }
+                }
+            }
+            __syncthreads();
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kThreads, 1) decode_nms_kernel(DecodeArgs p) {
+    extern __shared__ unsigned long long keys[];                       // kMaxKeys
+    uint8_t* removed = reinterpret_cast<uint8_t*>(keys + kMaxKeys);    // kMaxKeys
+    int* first = reinterpret_cast<int*>(removed + kMaxKeys);           // kMaxClasses
+    int* grp = first + kMaxClasses;                                    // kMaxClasses
+    int* seg = grp + kMaxClasses;                                      // kMaxClasses + 1 starts
+    __shared__ int warp_tot[32];
+    __shared__ int s_n, s_kept, s_groups;
+
+    const int b = blockIdx.x;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int64_t A = p.anchors;
+    const int nc = (int)p.channels - 4;
+    const float* pr = p.preds + (int64_t)b * p.channels * A;
+    Det* cand = reinterpret_cast<Det*>(p.work) + (int64_t)b * A;
+    Det* out = reinterpret_cast<Det*>(p.dets) + (int64_t)b * p.max_det;
+
+    bool has_meta = p.meta != nullptr;
+    double px = 0, py = 0, ow = 0, oh = 0, scale = 1.0;
+    if (has_meta) {
+        const int32_t* m = p.meta + (int64_t)b * 9;
+        ow = (double)m[2]; oh = (double)m[3];
+        px = (double)m[4]; py = (double)m[5];
+        scale = __ddiv_rn(1.0, (double)__int_as_float(m[8]));
+    }
+    for (int c = tid; c < kMaxClasses; c += kThreads) first[c] = INT_MAX;
+    if (tid == 0) { s_n = 0; s_kept = 0; }
+    __syncthreads();
+
+    // ---- 1. ordered candidate extraction ----
+    for (int64_t a0 = 0; a0 < A; a0 += kThreads) {
+        const int64_t a = a0 + tid;
+        bool flag = false;
+        float best = 0.0f;
+        int best_c = 0;
+        if (a < A) {
+            best = pr[4 * A + a];
+            for (int c = 1; c < nc; ++c) {
+                const float s = pr[(4 + c) * A + a];
+                if (s > best) { best = s; best_c = c; }
+            }
+            flag = !((double)best < p.conf);
+        }
+        const unsigned bal = __ballot_sync(0xffffffffu, flag);
+        if (lane == 0) warp_tot[warp] = __popc(bal);
+        __syncthreads();
+        if (warp == 0) {
+            int v = warp_tot[lane];
+            for (int o = 1; o < 32; o <<= 1) {
+                const int t = __shfl_up_sync(0xffffffffu, v, o);
+                if (lane >= o) v += t;
+            }
+            warp_tot[lane] = v;  // inclusive
+        }
+        __syncthreads();
+        if (flag) {
+            const int k = s_n + (warp ? warp_tot[warp - 1] : 0) + __popc(bal & ((1u << lane) - 1u));
+            if (k < kMaxKeys) {
+                const double cx = pr[a], cy = pr[A + a], w = pr[2 * A + a], h = pr[3 * A + a];
+                const double hw = __dmul_rn(w, 0.5), hh = __dmul_rn(h, 0.5);
+                Det d;
+                d.x1 = __dsub_rn(cx, hw); d.y1 = __dsub_rn(cy, hh);
+                d.x2 = __dadd_rn(cx, hw); d.y2 = __dadd_rn(cy, hh);
+                if (has_meta) {
+                    d.x1 = clamp_ref(__dmul_rn(__dsub_rn(d.x1, px), scale), ow);
+                    d.y1 = clamp_ref(__dmul_rn(__dsub_rn(d.y1, py), scale), oh);
+                    d.x2 = clamp_ref(__dmul_rn(__dsub_rn(d.x2, px), scale), ow);
+                    d.y2 = clamp_ref(__dmul_rn(__dsub_rn(d.y2, py), scale), oh);
+                }
+                d.conf = best; d.cls = best_c; d.anchor = (int32_t)a; d.reserved = 0;
+                cand[k] = d;
+                atomicMin(&first[best_c], k);
+            }
+        }
+        __syncthreads();
+        if (tid == 0) s_n += warp_tot[31];
+        __syncthreads();
+    }
+    const int n = s_n;
+    if (n > kMaxKeys) {
+        if (tid == 0) p.counts[b] = -1;
+        return;
+    }
+
+    // ---- 2. class group rank = order of first appearance ----
+    for (int c = tid; c < nc; c += kThreads) {
+        int g = -1;
+        const int f = first[c];
+        if (f != INT_MAX) {
+            g = 0;
+            for (int c2 = 0; c2 < nc; ++c2) g += first[c2] < f;
+        }
+        grp[c] = g;
+    }
+    __syncthreads();
+
+    // ---- 3. sort by (group, conf desc, index) ----
+    int np = 1;
+    while (np < n) np <<= 1;
+    for (int i = tid; i < np; i += kThreads) {
+        if (i < n) {
+            const Det& d = cand[i];
+            keys[i] = ((unsigned long long)grp[d.cls] << 48) | ((unsigned long long)desc_key(d.conf) << 16) |
+                      (unsigned long long)i;
+            removed[i] = 0;
+        } else {
+            keys[i] = ~0ull;
+        }
+    }
+    __syncthreads();
+    bitonic_sort(keys, np);
+
+    // group segment starts
+    for (int i = tid; i < n; i += kThreads) {
+        const int g = (int)(keys[i] >> 48);
+        if (i == 0 || (int)(keys[i - 1] >> 48) != g) seg[g] = i;
+        if (i == n - 1) s_groups = g + 1;
+    }
+    if (n == 0 && tid == 0) s_groups = 0;
+    __syncthreads();
+    const int G = s_groups;
+    if (tid == 0) seg[G] = n;
+    __syncthreads();
+
+    // ---- 4. greedy NMS, one warp per class group ----
+    for (int g = warp; g < G; g += kThreads / 32) {
+        const int s0 = seg[g], s1 = seg[g + 1];
+        for (int i = s0; i < s1; ++i) {
+            __syncwarp();
+            if (removed[i]) continue;
+            const Det bi = cand[keys[i] & 0xFFFF];
+            for (int j = i + 1 + lane; j < s1; j += 32) {
+                if (removed[j]) continue;
+                const Det bj = cand[keys[j] & 0xFFFF];
+                if (!(iou_ref(bi, bj) <= p.iou)) removed[j] = 1;
+            }
+        }
+        __syncwarp();
+    }
+    __syncthreads();
+
+    // ---- 5. final stable order: (conf desc, group, index) ----
+    unsigned long long mine[kMaxKeys / kThreads];
+    int cnt = 0;
+    for (int i = tid; i < np; i += kThreads) {
+        unsigned long long nk = ~0ull;
+        if (i < n && !removed[i]) {
+            const uint32_t idx = (uint32_t)(keys[i] & 0xFFFF);
+            const unsigned long long g = keys[i] >> 48;
+            nk = ((unsigned long long)desc_key(cand[idx].conf) << 26) | (g << 16) | idx;
+            atomicAdd(&s_kept, 1);
+        }
+        mine[cnt++] = nk;
+    }
+    __syncthreads();
+    cnt = 0;
+    for (int i = tid; i < np; i += kThreads) keys[i] = mine[cnt++];
+    __syncthreads();
+    bitonic_sort(keys, np);
+
+    // ---- 6. emit ----
+    const int kept = s_kept;
+    const int count = kept < p.max_det ? kept : p.max_det;
+    for (int r = tid; r < count; r += kThreads) out[r] = cand[keys[r] & 0xFFFF];
+    if (tid == 0) p.counts[b] = count;
+}
+
+}  // namespace
+
+size_t decode_work_bytes(int64_t batch, int64_t anchors) { return (size_t)batch * (size_t)anchors * sizeof(Det); }
+
+void launch_decode_nms(const DecodeArgs& a, cudaStream_t s) {
+    if (a.anchors > kMaxKeys) fail(ENGINE_ERR_NOT_IMPL, "decode: more than 16384 anchors per image");
+    if (a.channels - 4 > kMaxClasses || a.channels < 5) fail(ENGINE_ERR_INVALID_SHAPE, "decode: bad channel count");
+    if (a.max_det < 0) fail(ENGINE_ERR_INVALID_ARG, "decode: max_det must be >= 0");
+    if (a.batch == 0) return;
+    const size_t smem = kMaxKeys * 8 + kMaxKeys + 3 * kMaxClasses * 4 + 16;
+    int dev = 0;
+    PB_CUDA(cudaGetDevice(&dev));
+    static bool set[64] = {};
+    if (!set[dev]) {
+        PB_CUDA(cudaFuncSetAttribute(decode_nms_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        set[dev] = true;
+    }
+    decode_nms_kernel<<<(unsigned)a.batch, kThreads, smem, s>>>(a);
+    PB_CUDA(cudaGetLastError());
+}
+
+}  // namespace pb

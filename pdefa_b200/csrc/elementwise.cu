@@ -1,0 +1,311 @@
+// Layout and memory-bound kernels: strided copy/convert, broadcast binary ops,
+// unary activations, softmax, 2-D pooling and nearest resize. All operate on
+// strided per-image views (TView) so the planner can express NHWC channel slices,
+// NCHW<->NHWC conversions, permutations and broadcasts without extra copies.
+#include <cfloat>
+
+#include "common.h"
+#include "device_common.cuh"
+
+namespace pb {
+
+namespace {
+
+inline int grid_for(int64_t n, int threads) {
+    int64_t b = (n + threads - 1) / threads;
+    if (b > 148 * 32) b = 148 * 32;
+    return (int)(b < 1 ? 1 : b);
+}
+
+int64_t view_numel(const TView& v) {
+    int64_t n = 1;
+    for (int d = 0; d < v.rank; ++d) n *= v.shape[d];
+    return n;
+}
+
+__global__ void strided_copy_kernel(TView in, TView out, int64_t per_img, int64_t total) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t b = i / per_img, e = i - b * per_img;
+        const float v = ld_elem(in.ptr, in.dt, b * in.img_stride + view_offset(in, e));
+        st_elem(const_cast<void*>(out.ptr), out.dt, b * out.img_stride + view_offset(out, e), v);
+    }
+}
+
+// Fast path: both views are a set of contiguous rows of `row` elements (the inner
+// dimension has stride 1 on both sides), fp32 or bf16, copied 4 elements at a time.
+__global__ void row_copy_kernel(TView in, TView out, int64_t row, int64_t rows_per_img, int64_t total_rows) {
+    const int64_t vec = row / 4;
+    const int64_t total = total_rows * vec;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = i / vec, q = i - r * vec;
+        const int64_t b = r / rows_per_img, rr = r - b * rows_per_img;
+        // offset of the row start: index rr*row over the view shape
+        const int64_t oi = b * in.img_stride + view_offset(in, rr * row) + q * 4;
+        const int64_t oo = b * out.img_stride + view_offset(out, rr * row) + q * 4;
+        float v[4];
+        if (in.dt == F32) {
+            const float4 t = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(in.ptr) + oi);
+            v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+        } else {
+            const uint2 t = *reinterpret_cast<const uint2*>(reinterpret_cast<const __nv_bfloat16*>(in.ptr) + oi);
+            const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&t.x);
+            const __nv_bfloat162 c = *reinterpret_cast<const __nv_bfloat162*>(&t.y);
+            v[0] = __low2float(a); v[1] = __high2float(a); v[2] = __low2float(c); v[3] = __high2float(c);
+        }
+        if (out.dt == F32) {
+            *reinterpret_cast<float4*>(reinterpret_cast<float*>(const_cast<void*>(out.ptr)) + oo) =
+                make_float4(v[0], v[1], v[2], v[3]);
+        } else {
+            __nv_bfloat162 a = __floats2bfloat162_rn(v[0], v[1]);
+            __nv_bfloat162 c = __floats2bfloat162_rn(v[2], v[3]);
+            uint2 t;
+            t.x = *reinterpret_cast<uint32_t*>(&a);
+            t.y = *reinterpret_cast<uint32_t*>(&c);
+            *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(const_cast<void*>(out.ptr)) + oo) = t;
+        }
+    }
+}
+
+__global__ void binary_kernel(int op, TView a, TView b, TView out, int64_t per_img, int64_t total) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t n = i / per_img, e = i - n * per_img;
+        const float x = ld_elem(a.ptr, a.dt, n * a.img_stride + view_offset(a, e));
+        const float y = ld_elem(b.ptr, b.dt, n * b.img_stride + view_offset(b, e));
+        float r;
+        switch (op) {
+            case BIN_ADD: r = __fadd_rn(x, y); break;
+            case BIN_SUB: r = __fsub_rn(x, y); break;
+            case BIN_MUL: r = __fmul_rn(x, y); break;
+            default: r = __fdiv_rn(x, y); break;
+        }
+        st_elem(const_cast<void*>(out.ptr), out.dt, n * out.img_stride + view_offset(out, e), r);
+    }
+}
+
+__global__ void unary_kernel(int kind, TView in, TView out, int64_t per_img, int64_t total, float p0, float p1) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t n = i / per_img, e = i - n * per_img;
+        const float x = ld_elem(in.ptr, in.dt, n * in.img_stride + view_offset(in, e));
+        st_elem(const_cast<void*>(out.ptr), out.dt, n * out.img_stride + view_offset(out, e),
+                apply_act(x, kind, p0, p1));
+    }
+}
+
+// One thread per (image, outer, inner) column: max, exp-sum, normalise.
+__global__ void softmax_kernel(const float* in, float* out, int64_t outer, int64_t axis_len,
+                               int64_t inner, int64_t img_elems, int64_t total) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t per = outer * inner;
+        const int64_t b = i / per, r = i - b * per;
+        const int64_t o = r / inner, k = r - o * inner;
+        const float* src = in + b * img_elems + o * axis_len * inner + k;
+        float* dst = out + b * img_elems + o * axis_len * inner + k;
+        float mx = -1e30f;
+        for (int64_t a = 0; a < axis_len; ++a) mx = fmaxf(mx, src[a * inner]);
+        float sum = 0.0f;
+        for (int64_t a = 0; a < axis_len; ++a) {
+            const float e = expf(src[a * inner] - mx);
+            dst[a * inner] = e;
+            sum += e;
+        }
+        const float inv = sum > 0.0f ? 1.0f / sum : 0.0f;
+        for (int64_t a = 0; a < axis_len; ++a) dst[a * inner] *= inv;
+    }
+}
+
+// NHWC pooling, one thread per output element. Max pooling skips padded taps
+// (pooling.cpp:35-101: init -FLT_MAX, out-of-range taps ignored).
+__global__ void pool2d_kernel(Pool2dArgs a, int64_t total) {
+    const int64_t H = a.in.shape[1], W = a.in.shape[2], C = a.in.shape[3];
+    const int64_t Ho = a.out.shape[1], Wo = a.out.shape[2];
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        int64_t t = i;
+        const int64_t c = t % C; t /= C;
+        const int64_t wo = t % Wo; t /= Wo;
+        const int64_t ho = t % Ho;
+        const int64_t b = t / Ho;
+        const int64_t base = b * a.in.img_stride + c * a.in.stride[3];
+        float acc;
+        if (a.mode >= 2) {
+            acc = a.mode == 2 ? -FLT_MAX : 0.0f;
+            for (int64_t h = 0; h < H; ++h)
+                for (int64_t w = 0; w < W; ++w) {
+                    const float v = ld_elem(a.in.ptr, a.in.dt, base + h * a.in.stride[1] + w * a.in.stride[2]);
+                    acc = a.mode == 2 ? (v > acc ? v : acc) : acc + v;
+                }
+            if (a.mode == 3) acc = acc / (float)(H * W);
+        } else {
+            const int64_t h0 = ho * a.sh - a.ph, w0 = wo * a.sw - a.pw;
+            acc = a.mode == 0 ? -FLT_MAX : 0.0f;
+            int cnt = 0;
+            for (int kh = 0; kh < a.kh; ++kh) {
+                const int64_t h = h0 + kh;
+                if (h < 0 || h >= H) continue;
+                for (int kw = 0; kw < a.kw; ++kw) {
+                    const int64_t w = w0 + kw;
+                    if (w < 0 || w >= W) continue;
+                    const float v = ld_elem(a.in.ptr, a.in.dt, base + h * a.in.stride[1] + w * a.in.stride[2]);
+                    if (a.mode == 0) { if (v > acc) acc = v; }
+                    else { acc += v; ++cnt; }
+                }
+            }
+            if (a.mode == 1) acc = cnt ? acc / (float)cnt : 0.0f;
+        }
+        st_elem(const_cast<void*>(a.out.ptr), a.out.dt,
+                b * a.out.img_stride + ho * a.out.stride[1] + wo * a.out.stride[2] + c * a.out.stride[3], acc);
+    }
+}
+
+__global__ void resize_nearest_kernel(TView in, TView out, int64_t total, float sy, float sx) {
+    const int64_t Hi = in.shape[1], Wi = in.shape[2], C = in.shape[3];
+    const int64_t Ho = out.shape[1], Wo = out.shape[2];
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        int64_t t = i;
+        const int64_t c = t % C; t /= C;
+        const int64_t wo = t % Wo; t /= Wo;
+        const int64_t ho = t % Ho;
+        const int64_t b = t / Ho;
+        int64_t hi = (int64_t)((float)ho * sy); if (hi > Hi - 1) hi = Hi - 1;
+        int64_t wi = (int64_t)((float)wo * sx); if (wi > Wi - 1) wi = Wi - 1;
+        const float v = ld_elem(in.ptr, in.dt, b * in.img_stride + hi * in.stride[1] + wi * in.stride[2] + c * in.stride[3]);
+        st_elem(const_cast<void*>(out.ptr), out.dt,
+                b * out.img_stride + ho * out.stride[1] + wo * out.stride[2] + c * out.stride[3], v);
+    }
+}
+
+__global__ void reduce_kernel(int mode, const float* in, void* out, int64_t outer, int64_t axis_len,
+                              int64_t inner) {
+    const int64_t total = outer * inner;
+    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total;
+         t += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t o = t / inner, i = t - o * inner;
+        const float* base = in + o * axis_len * inner + i;
+        if (mode == 3) {
+            float best = base[0];
+            int32_t bi = 0;
+            for (int64_t k = 1; k < axis_len; ++k)
+                if (base[k * inner] > best) { best = base[k * inner]; bi = (int32_t)k; }
+            reinterpret_cast<int32_t*>(out)[t] = bi;
+        } else if (mode == 0) {
+            float mx = -3.4e38f;
+            for (int64_t k = 0; k < axis_len; ++k) if (base[k * inner] > mx) mx = base[k * inner];
+            reinterpret_cast<float*>(out)[t] = mx;
+        } else {
+            float s = 0.0f;
+            for (int64_t k = 0; k < axis_len; ++k) s += base[k * inner];
+            if (mode == 2) s = s / (float)axis_len;
+            reinterpret_cast<float*>(out)[t] = s;
+        }
+    }
+}
+
+__global__ void gather_kernel(const float* data, const int64_t* idx, float* out, int64_t outer, int64_t ax_dim,
+                              int64_t n_idx, int64_t inner) {
+    const int64_t total = outer * n_idx * inner;
+    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total;
+         t += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t i = t % inner;
+        const int64_t j = (t / inner) % n_idx;
+        const int64_t o = t / (inner * n_idx);
+        int64_t g = idx[j];
+        if (g < 0) g += ax_dim;
+        if (g < 0 || g >= ax_dim) g = 0;
+        out[t] = data[(o * ax_dim + g) * inner + i];
+    }
+}
+
+bool rows_vectorisable(const TView& in, const TView& out, int64_t* row) {
+    if (in.rank < 1 || in.stride[in.rank - 1] != 1 || out.stride[out.rank - 1] != 1) return false;
+    const int64_t r = in.shape[in.rank - 1];
+    if (r % 4) return false;
+    auto aligned = [](const TView& v) {
+        const int esz = v.dt == F32 ? 4 : 2;
+        if (((uintptr_t)v.ptr) % (4 * esz)) return false;
+        if (v.img_stride % 4) return false;
+        for (int d = 0; d < v.rank - 1; ++d) if (v.stride[d] % 4) return false;
+        return true;
+    };
+    if (!aligned(in) || !aligned(out)) return false;
+    *row = r;
+    return true;
+}
+
+}  // namespace
+
+void launch_strided_copy(const TView& in, const TView& out, int64_t batch, cudaStream_t s) {
+    const int64_t per = view_numel(out);
+    const int64_t total = per * batch;
+    if (total == 0) return;
+    int64_t row = 0;
+    if (rows_vectorisable(in, out, &row)) {
+        const int64_t rows_per_img = per / row;
+        const int64_t n = rows_per_img * batch * (row / 4);
+        row_copy_kernel<<<grid_for(n, 256), 256, 0, s>>>(in, out, row, rows_per_img, rows_per_img * batch);
+    } else {
+        strided_copy_kernel<<<grid_for(total, 256), 256, 0, s>>>(in, out, per, total);
+    }
+    PB_CUDA(cudaGetLastError());
+}
+
+void launch_binary(int op, const TView& a, const TView& b, const TView& out, int64_t batch, cudaStream_t s) {
+    const int64_t per = view_numel(out), total = per * batch;
+    if (!total) return;
+    binary_kernel<<<grid_for(total, 256), 256, 0, s>>>(op, a, b, out, per, total);
+    PB_CUDA(cudaGetLastError());
+}
+
+void launch_unary(int kind, const TView& in, const TView& out, int64_t batch, float p0, float p1, cudaStream_t s) {
+    const int64_t per = view_numel(out), total = per * batch;
+    if (!total) return;
+    unary_kernel<<<grid_for(total, 256), 256, 0, s>>>(kind, in, out, per, total, p0, p1);
+    PB_CUDA(cudaGetLastError());
+}
+
+void launch_softmax(const float* in, float* out, int64_t outer, int64_t axis_len, int64_t inner,
+                    int64_t img_elems, int64_t batch, cudaStream_t s) {
+    const int64_t total = outer * inner * batch;
+    if (!total) return;
+    softmax_kernel<<<grid_for(total, 256), 256, 0, s>>>(in, out, outer, axis_len, inner, img_elems, total);
+    PB_CUDA(cudaGetLastError());
+}
+
+void launch_reduce(int mode, const float* in, void* out, int64_t outer, int64_t axis_len, int64_t inner,
+                   cudaStream_t s) {
+    const int64_t total = outer * inner;
+    if (!total) return;
+    reduce_kernel<<<grid_for(total, 256), 256, 0, s>>>(mode, in, out, outer, axis_len, inner);
+    PB_CUDA(cudaGetLastError());
+}
+
+void launch_gather(const float* data, const int64_t* idx, float* out, int64_t outer, int64_t ax_dim,
+                   int64_t n_idx, int64_t inner, cudaStream_t s) {
+    const int64_t total = outer * n_idx * inner;
+    if (!total) return;
+    gather_kernel<<<grid_for(total, 256), 256, 0, s>>>(data, idx, out, outer, ax_dim, n_idx, inner);
+    PB_CUDA(cudaGetLastError());
+}
+
+void launch_pool2d(const Pool2dArgs& a, cudaStream_t s) {
+    const int64_t total = a.out.shape[1] * a.out.shape[2] * a.out.shape[3] * a.batch;
+    if (!total) return;
+    pool2d_kernel<<<grid_for(total, 256), 256, 0, s>>>(a, total);
+    PB_CUDA(cudaGetLastError());
+}
+
+void launch_resize_nearest(const TView& in, const TView& out, int64_t batch, cudaStream_t s) {
+    const int64_t total = out.shape[1] * out.shape[2] * out.shape[3] * batch;
+    if (!total) return;
+    const float sy = (float)in.shape[1] / (float)out.shape[1];
+    const float sx = (float)in.shape[2] / (float)out.shape[2];
+    resize_nearest_kernel<<<grid_for(total, 256), 256, 0, s>>>(in, out, total, sy, sx);
+    PB_CUDA(cudaGetLastError());
+}
+
+}  // namespace pb

@@ -1,0 +1,97 @@
+// Lowering of a .engine graph into a fixed sequence of GPU launches for a given
+// batch size and precision ("plan"), and its execution on a CUDA stream.
+//
+// Semantics follow the reference CPU interpreter (PDEFA1.0/src/core/session.cpp
+// and session_parts/*.inc): rank-4 activations are NHWC ("motor" shapes), ONNX axes
+// are remapped exactly as the reference does, conv+activation fusion uses the
+// reference's rule, and a batch of B images computes B independent batch-1 passes.
+#pragma once
+
+#include <functional>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "common.h"
+#include "kernels.h"
+
+namespace pb {
+
+enum Precision : int { PREC_FP32 = 0, PREC_TF32 = 1, PREC_BF16 = 2 };
+
+// Physical description of one graph value for the whole batch.
+struct Value {
+    std::vector<int64_t> shape;      // per-image motor shape (as the reference sees it at N = 1)
+    std::vector<int64_t> stride;     // per-image strides, elements
+    int64_t img_stride = 0;          // elements between images (0 = shared across images)
+    int dt = F32;
+    int buf = -1;                    // owning buffer (after allocation)
+    int64_t off = 0;                 // element offset inside the buffer
+    bool known = false;              // shape inferred
+    // placement (decided before allocation)
+    int alias_of = -1;               // value id this one views (slice / reshape views)
+    int64_t alias_off = 0;           // element offset added to the aliased value's offset
+    int place_in = -1;               // concat value this one is stored inside
+    int64_t place_ch = 0;            // channel offset inside that concat
+    bool dense_required = false;
+    int weight = -1;                 // weight index when this value is a constant
+    bool external = false;           // graph input
+    int producer = -1;               // node index
+};
+
+struct PlanStep {
+    std::string name;
+    std::function<void(cudaStream_t)> run;
+    int launches = 1;
+};
+
+class Plan {
+public:
+    Plan(std::shared_ptr<const Graph> g, int64_t batch, int precision, int device);
+    ~Plan();
+    Plan(const Plan&) = delete;
+    Plan& operator=(const Plan&) = delete;
+
+    // Input i: device buffer the caller fills with [batch, C, H, W] (NCHW fp32) data.
+    float* input_buffer(int i) const { return inputs_.at(i); }
+    size_t input_bytes(int i) const { return input_bytes_.at(i); }
+    // Output i: dense fp32 device buffer in the reference's output layout.
+    float* output_buffer(int i) const { return outputs_.at(i); }
+    const std::vector<int64_t>& output_shape(int i) const { return out_shapes_.at(i); }
+    size_t output_bytes(int i) const { return out_bytes_.at(i); }
+    int num_outputs() const { return (int)outputs_.size(); }
+
+    // Enqueue all steps on `s` (optionally redirecting input/output buffers).
+    void run(cudaStream_t s, const float* in_override = nullptr, float* out_override = nullptr);
+    const std::vector<PlanStep>& steps() const { return steps_; }
+    int64_t launch_count() const;
+    int64_t batch() const { return batch_; }
+    int precision() const { return prec_; }
+    int device() const { return device_; }
+
+private:
+    void build();
+    void* alloc(size_t bytes);
+
+    std::shared_ptr<const Graph> g_;
+    int64_t batch_;
+    int prec_;
+    int device_;
+    std::vector<void*> allocs_;
+    std::vector<float*> inputs_;
+    std::vector<size_t> input_bytes_;
+    std::vector<float*> outputs_;
+    std::vector<size_t> out_bytes_;
+    std::vector<std::vector<int64_t>> out_shapes_;
+    std::vector<PlanStep> steps_;
+    const float* cur_in_ = nullptr;   // overrides valid during run()
+    float* cur_out_ = nullptr;
+    friend struct PlanBuilder;
+};
+
+// Kernel the reference dispatcher picks for a batch-1 NHWC conv
+// (PDEFA1.0/src/ops/conv2d.cpp:602-642): 0 direct (Cin <= 16, not pure 1x1),
+// 1 Winograd F(2,3) (3x3 s1 d1, Cin <= 512), 2 GEMM. Decides the SiLU flavour.
+int reference_conv_path(int64_t cin, int64_t kh, int64_t kw, const OpParams& p);
+
+}  // namespace pb

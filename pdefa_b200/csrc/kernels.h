@@ -1,0 +1,132 @@
+// Host-callable launchers for every device kernel of the engine. All kernels run
+// on the caller's stream; none allocates memory.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace pb {
+
+enum DType : int { F32 = 0, BF16 = 1 };
+
+// Activation codes used in conv epilogues and unary kernels. 1-5 follow the
+// reference's fused_activation numbering (session_fusion.inc:76-98 and
+// Conv2dConfig::FusedActivation); 6 is SiLU evaluated the way the reference's
+// Winograd kernel does (conv2d_winograd.cpp:81-101); >= 10 are unary-op kinds.
+enum Act : int {
+    ACT_NONE = 0, ACT_RELU = 1, ACT_LEAKY = 2, ACT_SIGMOID = 3, ACT_GELU_TANH = 4,
+    ACT_SILU = 5, ACT_SILU_WINO = 6,
+    UN_TANH = 10, UN_GELU = 11, UN_HARDSWISH = 12, UN_HARDSIGMOID = 13, UN_CLIP = 14,
+    UN_COPY = 15,
+};
+
+enum BinOp : int { BIN_ADD = 0, BIN_SUB = 1, BIN_MUL = 2, BIN_DIV = 3 };
+
+constexpr int kMaxRank = 8;
+
+// A strided view of one image's worth of a tensor; `img_stride` advances to the
+// next image (0 broadcasts one tensor over the batch). Strides are in elements.
+struct TView {
+    const void* ptr = nullptr;
+    int dt = F32;
+    int rank = 0;
+    int64_t shape[kMaxRank] = {};
+    int64_t stride[kMaxRank] = {};
+    int64_t img_stride = 0;
+};
+
+// out[b, i...] = convert(in[b, i...]); shapes of in and out must match.
+void launch_strided_copy(const TView& in, const TView& out, int64_t batch, cudaStream_t s);
+// out = a (op) b with broadcasting expressed by zero strides; all views have out's rank.
+void launch_binary(int op, const TView& a, const TView& b, const TView& out, int64_t batch, cudaStream_t s);
+// out = act(in) for the unary kinds above (p0/p1: leaky slope or clip bounds).
+void launch_unary(int kind, const TView& in, const TView& out, int64_t batch, float p0, float p1, cudaStream_t s);
+// Softmax over `axis_len` elements spaced `inner` apart; dense fp32 in/out per image.
+void launch_softmax(const float* in, float* out, int64_t outer, int64_t axis_len, int64_t inner,
+                    int64_t img_elems, int64_t batch, cudaStream_t s);
+
+// Reduction along one axis of a dense fp32 tensor laid out as [outer, axis_len, inner].
+// mode: 0 max (init -3.4e38), 1 sum, 2 mean, 3 argmax (int32 out, strict '>' keeps the first).
+void launch_reduce(int mode, const float* in, void* out, int64_t outer, int64_t axis_len, int64_t inner,
+                   cudaStream_t s);
+// out[o, j, i] = data[o, clamp(idx[j]), i] with negative indices wrapped and
+// out-of-range ones mapped to 0 (engine_api.cpp gather semantics).
+void launch_gather(const float* data, const int64_t* idx, float* out, int64_t outer, int64_t ax_dim,
+                   int64_t n_idx, int64_t inner, cudaStream_t s);
+
+struct Pool2dArgs {
+    TView in, out;      // rank-4 NHWC views [1,H,W,C]
+    int kh, kw, sh, sw, ph, pw;
+    int mode;           // 0 max, 1 avg (count excludes padding), 2 global max, 3 global avg
+    int64_t batch;
+};
+void launch_pool2d(const Pool2dArgs& a, cudaStream_t s);
+// Nearest resize: out(h,w) = in(min(floor(h*Hin/H), Hin-1), ...) (session_ops_shape.inc:182-196).
+void launch_resize_nearest(const TView& in, const TView& out, int64_t batch, cudaStream_t s);
+
+// ---------------------------------------------------------------------------
+// Convolution (NHWC implicit GEMM). Input/output/residual are strided rank-4 views.
+// ---------------------------------------------------------------------------
+struct ConvArgs {
+    TView in;                 // [1,H,W,Cin]
+    TView out;                // [1,Ho,Wo,Cout]
+    TView res;                // optional residual added after the activation (ptr null = none)
+    const void* weight = nullptr;   // packed per kernel family (see conv_*.cu)
+    const float* bias = nullptr;
+    int cin = 0, cout = 0, kh = 1, kw = 1, sh = 1, sw = 1, ph = 0, pw = 0, dh = 1, dw = 1;
+    int act = ACT_NONE;
+    float slope = 0.01f;
+    int64_t batch = 1;
+};
+// Strict fp32 SIMT implicit GEMM. weight: fp32 [kh][kw][cin][cout].
+void launch_conv_simt(const ConvArgs& a, cudaStream_t s);
+
+// tcgen05 / TMA implicit GEMM. weight: [cout][kh][kw][cin] in the operand type
+// (bf16 for BF16, fp32 for TF32). Requires channel stride 1, 16-byte aligned pixel
+// strides and channel offsets, cin % chunk == 0 and cout % 16 == 0 (checked by
+// conv_tc_supported). err: device error word for bounded waits.
+bool conv_tc_supported(const ConvArgs& a, int op_dt, const char** why);
+void launch_conv_tc(const ConvArgs& a, int op_dt, int* err, cudaStream_t s);
+
+// Strict fp32 GEMM: C[b] = A[b] (M x K, lda) * B[b] (K x N, ldb) (+ bias[N]); row-major.
+void launch_gemm_f32(const float* A, const float* B, float* C, const float* bias,
+                     int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc,
+                     int64_t batch, int64_t sA, int64_t sB, int64_t sC, cudaStream_t s);
+// Tensor-core GEMM for ops_matmul (TF32 or BF16 operands, fp32 accumulate/output).
+// scratch must hold M*K + N*K operand-sized elements.
+void launch_gemm_tc(const float* A, const float* B, float* C, int64_t M, int64_t N, int64_t K,
+                    int op_dt, void* scratch, int* err, cudaStream_t s);
+
+// ---------------------------------------------------------------------------
+// YOLO head and decode.
+// ---------------------------------------------------------------------------
+struct YoloHeadArgs {
+    TView level[3];           // rank-4 NHWC [1,H,W,4*reg+nc] views, one per stride level
+    int nlevels = 3;
+    int64_t level_anchors[3] = {};
+    int reg_max = 16, nc = 80;
+    const float* anchors = nullptr;    // [2, A] anchor points (x row then y row)
+    const float* strides = nullptr;    // [A]
+    const float* dfl_w = nullptr;      // [reg_max] DFL conv weights
+    float* out = nullptr;              // [batch, 4+nc, A] fp32
+    int64_t A = 0;
+    int64_t batch = 1;
+};
+void launch_yolo_head(const YoloHeadArgs& a, cudaStream_t s);
+
+struct DecodeArgs {
+    const float* preds;         // [batch, channels, anchors]
+    int64_t batch, channels, anchors;
+    const int32_t* meta;        // [batch, 9] PdefaPreprocessMeta words or null
+    double conf, iou;
+    int max_det;
+    // device outputs
+    int32_t* counts;            // [batch]
+    void* dets;                 // [batch, max_det] PdefaDetection records
+    void* work;                 // scratch: decode_work_bytes(batch, anchors)
+    int* err;
+};
+size_t decode_work_bytes(int64_t batch, int64_t anchors);
+void launch_decode_nms(const DecodeArgs& a, cudaStream_t s);
+
+}  // namespace pb
