@@ -1,0 +1,316 @@
+"""Throughput benchmark: YOLOv8n-640 images/s on 1..8 B200 (configs[3] of BASELINE.json).
+
+One step = one batched forward pass of a random-init YOLOv8n over `--batch` (256)
+synthetic 640x640 images per GPU with BF16 tcgen05 convolutions, followed by the GPU
+decode + class-wise NMS (conf 0.25, IoU 0.45, max_det 300). One process per GPU
+(torchrun); replicas are independent, so the work scales weakly and there is no
+collective on the data path (one all-reduce of the timings at the end).
+
+Printed JSON line (rank 0):
+* value: images/s over all GPUs with inputs resident in HBM (seeded torch.rand on the
+  device, 1.26 GB per GPU > L2, so no L2 flush is needed), device-timed with CUDA
+  events, max over ranks;
+* e2e: the same through the public batch API (pdefa_batch_run, what
+  BatchInference.detect calls) from pinned host images to host detections;
+* roofline: the tcgen05 convolution kernels of the step (the dominant kernel
+  family): conv FLOPs / their CUDA-event time measured inside the timed region,
+  against the measured sustained BF16 peak;
+* cpu_baseline: the reference CPU engine (oracle/_ref, built from the reference
+  sources) + the restated reference decode on a bounded sample, rank 0 only.
+`--impl reference` times that CPU path alone as the reference arm.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "YOLOv8n-640 images/sec at 1/2/4/8 B200; conv TFLOP/s vs tensor-core peak"
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d.get("hbm_gbs", 6650.0), d.get("bf16_tflops", 1590.0), d.get("bf16_tflops_sustained", 1400.0), "measured"
+    return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in self.lines:
+            f = [x.strip() for x in l.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        sm.sort()
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def cpu_reference(images: int, threads: int):
+    """Reference CPU path on `images` images: engine (oracle/_ref) batch-1 + decode restatement."""
+    import numpy as np
+    from oracle import decode_ref, ref_engine as R
+    from pdefa_b200.engine_file import write_engine
+    from pdefa_b200.yolo import build_yolov8
+    if not R.available():
+        return None
+    g, _ = build_yolov8("n", imgsz=640, seed=0)
+    p = os.path.join(tempfile.mkdtemp(), "y8n_ref.engine")
+    write_engine(p, g)
+    sess = R.RefSession(p, threads=threads)
+    x = np.random.default_rng(0).random((1, 3, 640, 640), dtype=np.float32)
+    sess.run(x)   # warm-up (weight caches)
+
+    def step(n):
+        t0 = time.perf_counter()
+        for i in range(n):
+            y = sess.run(x)
+            decode_ref.decode(y[0], None, 0.25, 0.45, 300)
+        return time.perf_counter() - t0
+    return step
+
+
+def run_reference_arm(args, rank):
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    step = cpu_reference(args.ref_images, threads)
+    if step is None:
+        print(json.dumps({"impl": "reference", "unavailable": "reference engine not built (oracle/_ref missing)"}))
+        return
+    for _ in range(args.warmup):
+        step(args.ref_images)
+    ts = [step(args.ref_images) for _ in range(args.steps)]
+    tot = sum(ts)
+    value = args.ref_images * args.steps / tot
+    sample = (f"{args.ref_images} images per step, batch-1 Session.run of the reference engine "
+              f"(oracle/_ref, AVX2) + reference decode/NMS restated in Python (oracle/decode_ref.py)")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "images/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": tot / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": config(args, 1),
+        "cpu_baseline": {"value": value, "unit": "images/s", "cores": threads, "kind": "reference", "sample": sample},
+        "e2e": {"value": value, "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }))
+
+
+def config(args, world):
+    return {"workload": "configs[3]: YOLOv8n-640 random-init, BF16 tcgen05 convs + GPU decode/NMS "
+                        "(conf 0.25, IoU 0.45, max_det 300), independent replicas",
+            "model": "yolov8n", "imgsz": args.imgsz, "per_gpu_batch": args.batch, "global_batch": args.batch * world,
+            "parallelism": f"replicas x{world}", "precision": args.precision,
+            "l2": "inputs larger than L2 (1.26 GB per GPU)"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--batch", type=int, default=256)
+    ap.add_argument("--imgsz", type=int, default=640)
+    ap.add_argument("--precision", default="bf16", choices=["bf16", "tf32", "fp32"])
+    ap.add_argument("--e2e-steps", type=int, default=0, help="steps for the e2e leg (default: --steps)")
+    ap.add_argument("--cpu-images", type=int, default=48, help="images in the bounded CPU baseline sample")
+    ap.add_argument("--ref-images", type=int, default=4, help="images per step of the reference arm")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        run_reference_arm(args, rank)
+        return
+
+    import datetime
+    import torch
+    import torch.distributed as dist
+
+    import pdefa_b200 as pb
+    from pdefa_b200 import _native as N
+    from pdefa_b200.engine_file import write_engine
+    from pdefa_b200.yolo import build_yolov8, conv_flops
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    L = N.lib()
+    prec = {"bf16": pb.BF16, "tf32": pb.TF32, "fp32": pb.FP32}[args.precision]
+    g, info = build_yolov8("n", imgsz=args.imgsz, seed=0)
+    tmp = tempfile.mkdtemp()
+    path = os.path.join(tmp, "yolov8n.engine")
+    write_engine(path, g)
+    ctx = pb.Context(precision=prec, device=local)
+    model = pb.Model(ctx, path)
+    sess = pb.Session(ctx, model)
+    B = args.batch
+    out_shape = sess.output_shape(B)
+    ch, A = out_shape[1], out_shape[2]
+    gen = torch.Generator(device="cuda").manual_seed(1234 + rank)
+    x = torch.rand((B, 3, args.imgsz, args.imgsz), device="cuda", generator=gen)
+    out_ptr = sess.device_output(B)          # decode reads the session's own output buffer
+    max_det = 300
+    counts = torch.empty(B, dtype=torch.int32, device="cuda")
+    dets = torch.empty(B * max_det * 48, dtype=torch.uint8, device="cuda")
+    wbytes = L.pdefa_decode_work_bytes(B, A)
+    work = torch.empty(wbytes, dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def step():
+        sess.run_device(x.data_ptr(), B, None, stream)
+        pb.api._check(L.pdefa_decode_yolo_device(out_ptr, B, ch, A, None, 0.25, 0.45, max_det,
+                                                 counts.data_ptr(), dets.data_ptr(), work.data_ptr(), wbytes,
+                                                 stream), "decode")
+
+    summary = model.plan_summary(prec, B)
+    launches_per_step = len(summary) + 1
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    sess.set_step_timing(B, True)
+
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+    phys = int(vis.split(",")[local]) if vis and vis.split(",")[local].strip().isdigit() else local
+    sampler = ClockSampler(phys)
+    sampler.start()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop()
+    ms = e0.elapsed_time(e1)
+    step_ms = sess.step_times(B)
+    sess.set_step_timing(B, False)
+    t = torch.tensor([ms], device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    value = B * world * args.steps / (ms_max / 1e3)
+
+    # roofline of the tensor-core conv family, measured inside the timed region
+    hbm, peak_burst, peak_sus, peak_src = load_peaks()
+    flops_img = conv_flops(info)
+    tc_ms = sum(step_ms[i] for i, (k, _) in enumerate(summary) if k.startswith("conv_tc")) / args.steps
+    conv_ms_all = sum(step_ms[i] for i, (k, _) in enumerate(summary) if k.startswith("conv")) / args.steps
+    by_kind = {}
+    for i, (k, _) in enumerate(summary):
+        by_kind[k] = by_kind.get(k, 0.0) + step_ms[i] / args.steps
+    tc_flops = (flops_img - 2 * 3 * 16 * 9 * (args.imgsz // 2) ** 2) * B
+    achieved = tc_flops / (tc_ms / 1e3) / 1e12 if tc_ms > 0 else None
+    roofline = {"bound": "tensor", "achieved": achieved, "peak": peak_sus, "unit": "TFLOP/s",
+                "frac": (achieved / peak_sus) if achieved else None, "traffic": None,
+                "kernel": "conv_tc_bf16 (62 launches/step)", "peak_source": f"{peak_src} bf16 sustained",
+                "conv_tflops_all_convs": flops_img * B / (conv_ms_all / 1e3) / 1e12 if conv_ms_all else None,
+                "ms_by_kernel_kind": {k: round(v, 4) for k, v in by_kind.items()},
+                "decode_ms": ms_max / args.steps - sum(by_kind.values())}
+
+    # e2e: pinned host images -> public batch API on this GPU -> host detections
+    e2e_steps = args.e2e_steps or args.steps
+    xh = torch.empty((B, 3, args.imgsz, args.imgsz), dtype=torch.float32, pin_memory=True)
+    xh.copy_(x)
+    bi = pb.BatchInference(ctx, model, batch_size=B, devices=[local], precision=prec)
+    xnp = xh.numpy()
+    bi.detect(xnp)
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        bi.detect(xnp, conf_thres=0.25, iou_thres=0.45, max_det=max_det)
+    e2e_s = time.perf_counter() - t0
+    bi.close()
+    te = torch.tensor([e2e_s], device="cuda")
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_value = B * world * e2e_steps / float(te.item())
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        stepf = cpu_reference(args.cpu_images, threads)
+        if stepf is not None:
+            secs = stepf(args.cpu_images)
+            cpu = {"value": args.cpu_images / secs, "unit": "images/s", "cores": threads, "kind": "reference",
+                   "sample": f"{args.cpu_images} images: reference engine (oracle/_ref) batch-1 Session.run "
+                             f"+ restated reference decode/NMS (oracle/decode_ref.py)"}
+
+    if world > 1:
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC, "value": value, "unit": "images/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16" if prec == pb.BF16 else ("tf32" if prec == pb.TF32 else "f32"),
+            "data": "synthetic (seeded uniform images, random-init weights)", "config": config(args, world),
+            "clocks": clocks, "gpu_launches": launches_per_step * args.steps,
+            "e2e": {"value": e2e_value, "unit": "images/s", "h2d_bytes_per_step": xh.numel() * 4,
+                    "d2h_bytes_per_step": B * 4 + B * max_det * 48},
+            "roofline": roofline, "cpu_baseline": cpu,
+            "conv_gflop_per_image": flops_img / 1e9,
+        }))
+
+
+if __name__ == "__main__":
+    main()

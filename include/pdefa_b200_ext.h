@@ -43,9 +43,26 @@ ENGINE_API int32_t      engine_device_error(int32_t device);
  * session's own stream. Returns after the work is enqueued (asynchronous). */
 ENGINE_API EngineStatus engine_session_run_device(EngineSession* sess, const float* d_input,
                                                   int64_t batch, float* d_output, void* stream);
+/* Device address of the session's own output buffer `index` for `batch` images
+ * (valid until the session is destroyed; engine_session_run_device with
+ * d_output == NULL leaves the result there without an extra copy). */
+ENGINE_API EngineStatus engine_session_device_output(EngineSession* sess, int32_t index, int64_t batch,
+                                                     void** out_ptr);
 ENGINE_API EngineStatus engine_session_output_shape(const EngineSession* sess, int32_t index,
                                                     int64_t batch, int64_t* out_shape,
                                                     int32_t* out_ndim);
+/* Lowers `model` for `batch` images at `precision` without touching a GPU and
+ * reports whether it is supported (status + message as usual). On success
+ * writes one line per launch ("<kernel kind> <node name>") into buf (truncated to
+ * buf_len, NUL-terminated) and the launch count into *out_launches. */
+ENGINE_API EngineStatus engine_model_plan_summary(const EngineModel* model, int32_t precision, int64_t batch,
+                                                  char* buf, size_t buf_len, int64_t* out_launches);
+/* Per-launch CUDA-event timing of the plan for `batch` (enable != 0 turns it on).
+ * engine_session_step_times waits for the recorded events and writes, per launch in
+ * engine_model_plan_summary order, the total milliseconds accumulated since timing
+ * was enabled (n_steps entries at most); returns the number of launches. */
+ENGINE_API EngineStatus engine_session_step_timing(EngineSession* sess, int64_t batch, int32_t enable);
+ENGINE_API int64_t      engine_session_step_times(EngineSession* sess, int64_t batch, double* out_ms, int64_t n_steps);
 /* Number of kernel launches one engine_session_run_device call issues. */
 ENGINE_API int64_t      engine_session_launch_count(const EngineSession* sess, int64_t batch);
 
@@ -76,6 +93,17 @@ ENGINE_API EngineStatus pdefa_decode_yolo(const float* preds, int32_t preds_on_d
                                           double conf_thres, double iou_thres, int32_t max_det,
                                           int32_t* out_counts, PdefaDetection* out_dets,
                                           int32_t device);
+
+/* Device-side variant of pdefa_decode_yolo for callers that manage memory: all
+ * pointers are device pointers on the current device (d_metas may be NULL), work is
+ * caller-provided scratch of pdefa_decode_work_bytes(batch, anchors) bytes, and the
+ * call only enqueues one kernel on `stream` (no allocation, no synchronisation). */
+ENGINE_API size_t       pdefa_decode_work_bytes(int64_t batch, int64_t anchors);
+ENGINE_API EngineStatus pdefa_decode_yolo_device(const float* d_preds, int64_t batch, int64_t channels,
+                                                 int64_t anchors, const PdefaPreprocessMeta* d_metas,
+                                                 double conf_thres, double iou_thres, int32_t max_det,
+                                                 int32_t* d_counts, PdefaDetection* d_dets, void* d_work,
+                                                 size_t work_bytes, void* stream);
 
 /* Multi-GPU batch runner: one replica of `model` per device, contiguous shards, no
  * collective. Each device runs its shard's inference and decode and returns only

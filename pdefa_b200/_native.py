@@ -75,6 +75,12 @@ _SIGS = {
     "engine_session_run_device": ([vp, vp, i64, vp, vp], C.c_int),
     "engine_session_output_shape": ([vp, i32, i64, P(i64), P(i32)], C.c_int),
     "engine_session_launch_count": ([vp, i64], i64),
+    "engine_session_device_output": ([vp, i32, i64, P(vp)], C.c_int),
+    "engine_session_step_timing": ([vp, i64, i32], C.c_int),
+    "engine_session_step_times": ([vp, i64, P(f64), i64], i64),
+    "pdefa_decode_work_bytes": ([i64, i64], sz),
+    "pdefa_decode_yolo_device": ([vp, i64, i64, i64, vp, f64, f64, i32, vp, vp, vp, sz, vp], C.c_int),
+    "engine_model_plan_summary": ([vp, i32, i64, C.c_char_p, sz, P(i64)], C.c_int),
     # ops
     "engine_ops_add": ([vp, vp, P(vp)], C.c_int), "engine_ops_sub": ([vp, vp, P(vp)], C.c_int),
     "engine_ops_mul": ([vp, vp, P(vp)], C.c_int), "engine_ops_div": ([vp, vp, P(vp)], C.c_int),

@@ -459,6 +459,15 @@ class Model:
     def input_info(self, idx: int) -> TensorInfo:
         return _info(self._handle, idx, N.lib().engine_model_input_info)
 
+    def plan_summary(self, precision: int = FP32, batch: int = 1) -> List[Tuple[str, str]]:
+        """(kernel kind, node name) per launch, from a device-free lowering."""
+        buf = C.create_string_buffer(1 << 20)
+        n = N.i64()
+        _check(N.lib().engine_model_plan_summary(self._handle, int(precision), int(batch), buf, len(buf),
+                                                 C.byref(n)), "plan_summary")
+        lines = [l for l in buf.value.decode().splitlines() if l]
+        return [tuple(l.split(" ", 1)) for l in lines]
+
     def output_info(self, idx: int) -> TensorInfo:
         return _info(self._handle, idx, N.lib().engine_model_output_info)
 
@@ -526,6 +535,23 @@ class Session:
 
     def run_device(self, d_input: int, batch: int, d_output: Optional[int] = None, stream: Optional[int] = None):
         _check(N.lib().engine_session_run_device(self._handle, d_input, batch, d_output, stream), "run_device")
+
+    def device_output(self, batch: int, index: int = 0) -> int:
+        """Device address of the session-owned output buffer for `batch` images."""
+        ptr = C.c_void_p()
+        _check(N.lib().engine_session_device_output(self._handle, index, batch, C.byref(ptr)), "device_output")
+        return int(ptr.value)
+
+    def set_step_timing(self, batch: int, enable: bool = True):
+        _check(N.lib().engine_session_step_timing(self._handle, batch, 1 if enable else 0), "step_timing")
+
+    def step_times(self, batch: int) -> List[float]:
+        n = self.launch_count(batch)
+        buf = (C.c_double * max(n, 1))()
+        got = N.lib().engine_session_step_times(self._handle, batch, buf, n)
+        if got < 0:
+            _check(8, "step_times")
+        return [buf[i] for i in range(got)]
 
     def launch_count(self, batch: int) -> int:
         return int(N.lib().engine_session_launch_count(self._handle, batch))

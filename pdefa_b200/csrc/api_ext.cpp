@@ -116,6 +116,18 @@ ENGINE_API EngineStatus engine_session_run_device(EngineSession* sess, const flo
         return ENGINE_OK;
     });
 }
+ENGINE_API EngineStatus engine_session_device_output(EngineSession* sess, int32_t index, int64_t batch, void** out_ptr) {
+    if (!sess || sess->magic != kMagicSession) return ENGINE_ERR_INVALID_HANDLE;
+    if (!out_ptr) return ENGINE_ERR_NULL_PTR;
+    return guarded([&]() -> EngineStatus {
+        std::lock_guard<std::mutex> lk(sess->mu);
+        PB_CUDA(cudaSetDevice(sess->device));
+        Plan& p = sess->plan_for(batch);
+        if (index < 0 || index >= p.num_outputs()) return ENGINE_ERR_INVALID_ARG;
+        *out_ptr = p.output_buffer(index);
+        return ENGINE_OK;
+    });
+}
 ENGINE_API EngineStatus engine_session_output_shape(const EngineSession* sess, int32_t index, int64_t batch,
                                                     int64_t* out_shape, int32_t* out_ndim) {
     if (!sess || sess->magic != kMagicSession) return ENGINE_ERR_INVALID_HANDLE;
@@ -128,6 +140,74 @@ ENGINE_API EngineStatus engine_session_output_shape(const EngineSession* sess, i
         return ENGINE_OK;
     });
 }
+ENGINE_API EngineStatus engine_model_plan_summary(const EngineModel* model, int32_t precision, int64_t batch,
+                                                  char* buf, size_t buf_len, int64_t* out_launches) {
+    if (!model || model->magic != kMagicModel) return ENGINE_ERR_INVALID_HANDLE;
+    return guarded([&]() -> EngineStatus {
+        clear_error();
+        auto plan = Plan::dry_run(model->graph, batch, precision);
+        const std::string s = plan->summary();
+        if (buf && buf_len) {
+            const size_t n = std::min(buf_len - 1, s.size());
+            std::memcpy(buf, s.data(), n);
+            buf[n] = 0;
+        }
+        if (out_launches) *out_launches = plan->launch_count();
+        return ENGINE_OK;
+    });
+}
+
+ENGINE_API EngineStatus engine_session_step_timing(EngineSession* sess, int64_t batch, int32_t enable) {
+    if (!sess || sess->magic != kMagicSession) return ENGINE_ERR_INVALID_HANDLE;
+    return guarded([&]() -> EngineStatus {
+        std::lock_guard<std::mutex> lk(sess->mu);
+        PB_CUDA(cudaSetDevice(sess->device));
+        Plan& p = sess->plan_for(batch);
+        p.collect_step_ms();
+        p.set_step_timing(enable != 0);
+        return ENGINE_OK;
+    });
+}
+ENGINE_API int64_t engine_session_step_times(EngineSession* sess, int64_t batch, double* out_ms, int64_t n_steps) {
+    if (!sess || sess->magic != kMagicSession) return -1;
+    try {
+        std::lock_guard<std::mutex> lk(sess->mu);
+        PB_CUDA(cudaSetDevice(sess->device));
+        Plan& p = sess->plan_for(batch);
+        const auto ms = p.collect_step_ms();
+        for (int64_t i = 0; i < n_steps && i < (int64_t)ms.size(); ++i) out_ms[i] = ms[i];
+        return (int64_t)ms.size();
+    } catch (const std::exception& e) {
+        set_error(e.what());
+        return -1;
+    }
+}
+
+ENGINE_API size_t pdefa_decode_work_bytes(int64_t batch, int64_t anchors) { return decode_work_bytes(batch, anchors); }
+
+ENGINE_API EngineStatus pdefa_decode_yolo_device(const float* d_preds, int64_t batch, int64_t channels, int64_t anchors,
+                                                 const PdefaPreprocessMeta* d_metas, double conf_thres, double iou_thres,
+                                                 int32_t max_det, int32_t* d_counts, PdefaDetection* d_dets, void* d_work,
+                                                 size_t work_bytes, void* stream) {
+    if (!d_preds || !d_counts || !d_work || (!d_dets && max_det > 0)) return ENGINE_ERR_NULL_PTR;
+    return guarded([&]() -> EngineStatus {
+        clear_error();
+        if (batch < 0 || channels < 5 || anchors < 0) { set_error("decode: bad shape"); return ENGINE_ERR_INVALID_SHAPE; }
+        if (max_det < 0) { set_error("decode: max_det must be >= 0"); return ENGINE_ERR_INVALID_ARG; }
+        if (work_bytes < decode_work_bytes(batch, anchors)) { set_error("decode: work buffer too small"); return ENGINE_ERR_INVALID_ARG; }
+        int dev = 0;
+        PB_CUDA(cudaGetDevice(&dev));
+        DecodeArgs a;
+        a.preds = d_preds;
+        a.batch = batch; a.channels = channels; a.anchors = anchors;
+        a.meta = reinterpret_cast<const int32_t*>(d_metas);
+        a.conf = conf_thres; a.iou = iou_thres; a.max_det = max_det;
+        a.counts = d_counts; a.dets = d_dets; a.work = d_work; a.err = device_error_word(dev);
+        launch_decode_nms(a, static_cast<cudaStream_t>(stream));
+        return ENGINE_OK;
+    });
+}
+
 ENGINE_API int64_t engine_session_launch_count(const EngineSession* sess, int64_t batch) {
     if (!sess || sess->magic != kMagicSession) return -1;
     try {

@@ -260,7 +260,7 @@ struct PlanBuilder {
             need(2);
             const int x = input_vid(n, 0), w = input_vid(n, 1);
             auto is = V[x].shape;
-            const auto& ws = V[w].shape;
+            const auto ws = V[w].shape;
             if (is.size() != 4 || ws.size() != 4) fail(ENGINE_ERR_INVALID_SHAPE, "conv '" + n.name + "': rank != 4");
             const int64_t ci_w = ws[1];
             if (is[3] != ci_w && is[2] == ci_w) {   // session_ops_nn.inc:10-33
@@ -286,8 +286,8 @@ struct PlanBuilder {
         }
         case Op::MatMul: {
             need(2);
-            const auto& a = V[input_vid(n, 0)].shape;
-            const auto& b = V[input_vid(n, 1)].shape;
+            const auto a = V[input_vid(n, 0)].shape;
+            const auto b = V[input_vid(n, 1)].shape;
             if (a.size() == 4 && b.size() == 2 && a[3] == b[0]) {
                 nt.mode = 1;
                 set_out(n, 0, {a[0], a[1], a[2], b[1]}, act_dt, ni);
@@ -302,14 +302,14 @@ struct PlanBuilder {
         case Op::ReLU: case Op::LeakyReLU: case Op::Sigmoid: case Op::Tanh: case Op::SiLU: case Op::GELU:
         case Op::HardSwish: case Op::HardSigmoid: case Op::Clip: {
             need(1);
-            const auto& s = V[input_vid(n, 0)].shape;
+            const auto s = V[input_vid(n, 0)].shape;
             set_out(n, 0, s, dt_for(s), ni);
             return;
         }
         case Op::Add: case Op::Sub: case Op::Mul: case Op::Div: {
             need(2);
-            const auto& a = V[input_vid(n, 0)].shape;
-            const auto& b = V[input_vid(n, 1)].shape;
+            const auto a = V[input_vid(n, 0)].shape;
+            const auto b = V[input_vid(n, 1)].shape;
             const size_t r = std::max(a.size(), b.size());
             std::vector<int64_t> o(r);
             for (size_t d = 0; d < r; ++d) {
@@ -327,11 +327,13 @@ struct PlanBuilder {
             const int r = (int)s0.size();
             int ax = n.params.axis < 0 ? n.params.axis + r : n.params.axis;
             if (r == 4 && ax == 1) ax = 3;   // session_ops_shape.inc:73-75
-            if (ax < 0 || ax >= r) fail(ENGINE_ERR_INVALID_SHAPE, "concat axis out of range");
+            if (ax < 0 || ax >= r)
+                fail(ENGINE_ERR_INVALID_SHAPE, "concat '" + n.name + "': axis " + std::to_string(n.params.axis) +
+                                                   " out of range for input shape " + shape_str(s0));
             auto o = s0;
             o[ax] = 0;
             for (size_t k = 0; k < nin; ++k) {
-                const auto& s = V[input_vid(n, k)].shape;
+                const auto s = V[input_vid(n, k)].shape;
                 if ((int)s.size() != r) fail(ENGINE_ERR_INVALID_SHAPE, "concat rank mismatch");
                 o[ax] += s[ax];
             }
@@ -341,7 +343,7 @@ struct PlanBuilder {
         }
         case Op::Upsample: case Op::Resize: {
             need(1);
-            const auto& s = V[input_vid(n, 0)].shape;
+            const auto s = V[input_vid(n, 0)].shape;
             if (s.size() != 4) fail(ENGINE_ERR_INVALID_SHAPE, "resize needs a rank-4 input");
             int64_t H = 0, W = 0;
             const OpParams& p = n.params;
@@ -370,7 +372,7 @@ struct PlanBuilder {
         }
         case Op::MaxPool2d: case Op::AvgPool2d: {
             need(1);
-            const auto& s = V[input_vid(n, 0)].shape;
+            const auto s = V[input_vid(n, 0)].shape;
             if (s.size() != 4) fail(ENGINE_ERR_INVALID_SHAPE, "pool needs a rank-4 input");
             const OpParams& p = n.params;
             if (p.kernel_h <= 0 || p.kernel_w <= 0) { nt.mode = 1; set_out(n, 0, {s[0], 1, 1, s[3]}, act_dt, ni); return; }
@@ -384,7 +386,7 @@ struct PlanBuilder {
         case Op::Slice: infer_slice(ni); return;
         case Op::Softmax: {
             need(1);
-            const auto& s = V[input_vid(n, 0)].shape;
+            const auto s = V[input_vid(n, 0)].shape;
             int64_t ax = n.params.axis < 0 ? n.params.axis + (int64_t)s.size() : n.params.axis;
             if (s.size() == 4) { static const int64_t remap[4] = {0, 2, 3, 1}; if (ax >= 0 && ax < 4) ax = remap[ax]; }
             if (ax < 0 || ax >= (int64_t)s.size()) fail(ENGINE_ERR_INVALID_SHAPE, "softmax axis");
@@ -404,7 +406,7 @@ struct PlanBuilder {
         const Node& n = nodes[ni];
         Note& nt = note[ni];
         const int x = input_vid(n, 0);
-        const auto& in = V[x].shape;
+        const auto in = V[x].shape;
         const size_t nin = n.inputs.size();
         if (in.size() == 4 && nin >= 2 && numel_of(V[input_vid(n, 1)].shape) == 5) {
             const int t = input_vid(n, 1);
@@ -474,7 +476,7 @@ struct PlanBuilder {
         Note& nt = note[ni];
         if (n.inputs.size() < 2) fail(ENGINE_ERR_INVALID_FORMAT, "transpose without perm");
         const int x = input_vid(n, 0), pt = input_vid(n, 1);
-        const auto& s = V[x].shape;
+        const auto s = V[x].shape;
         const int64_t r = (int64_t)s.size();
         if (numel_of(V[pt].shape) != r) fail(ENGINE_ERR_INVALID_SHAPE, "transpose perm length");
         std::vector<int64_t> perm(r);
@@ -510,7 +512,7 @@ struct PlanBuilder {
         int ax_v = -1, sp_v = -1;
         if (n.inputs.size() > 3) { ax_v = input_vid(n, 3); if (numel_of(V[ax_v].shape) == 0) ax_v = -1; }
         if (n.inputs.size() > 4) { sp_v = input_vid(n, 4); if (numel_of(V[sp_v].shape) == 0) sp_v = -1; }
-        const auto& s = V[x].shape;
+        const auto s = V[x].shape;
         const int64_t r = (int64_t)s.size();
         const int64_t ns = numel_of(V[st].shape);
         std::vector<int64_t> od = s, sv(r, 0), stv(r, 1);
@@ -820,7 +822,7 @@ struct PlanBuilder {
         std::vector<float> h(W.numel());
         for (int64_t i = 0; i < W.numel(); ++i) h[i] = (float)W.value(i);
         void* d = P.alloc(std::max<size_t>(h.size() * 4, 16));
-        PB_CUDA(cudaMemcpy(d, h.data(), h.size() * 4, cudaMemcpyHostToDevice));
+        if (!P.dry_) PB_CUDA(cudaMemcpy(d, h.data(), h.size() * 4, cudaMemcpyHostToDevice));
         wdev[w] = d;
         return d;
     }
@@ -864,14 +866,18 @@ struct PlanBuilder {
         return -1;
     }
 
+    std::string next_kind = "kernel";
     void add_step(const std::string& name, std::function<void(cudaStream_t)> fn, int launches = 1) {
-        P.steps_.push_back(PlanStep{name, std::move(fn), launches});
+        P.steps_.push_back(PlanStep{name, std::move(fn), launches, next_kind});
+        next_kind = "kernel";
     }
+    void kind(const char* k) { next_kind = k; }
 
     void add_copy(TView src, TView dst, const std::string& name) {
         const int64_t b = B;
         const bool ext = external_of(src) == 0;
         Plan* pp = &P;
+        kind("copy");
         add_step(name, [src, dst, b, ext, pp](cudaStream_t s) mutable {
             if (ext && pp->cur_in_) src.ptr = pp->cur_in_;
             launch_strided_copy(src, dst, b, s);
@@ -956,6 +962,7 @@ struct PlanBuilder {
         a.out = static_cast<float*>(const_cast<void*>(o.ptr));
         a.A = V[head_out].shape[2];
         a.batch = B;
+        kind("yolo_head");
         add_step("yolo_head", [a](cudaStream_t s) { launch_yolo_head(a, s); });
     }
 
@@ -983,6 +990,7 @@ struct PlanBuilder {
             const int64_t b = B;
             const bool ext = external_of(in) == 0;
             Plan* pp = &P;
+            this->kind("unary");
             add_step(n.name, [=](cudaStream_t s) mutable {
                 if (ext && pp->cur_in_) in.ptr = pp->cur_in_;
                 launch_unary(kind, in, out, b, p0, p1, s);
@@ -1007,6 +1015,7 @@ struct PlanBuilder {
             };
             TView a = aligned(input_vid(n, 0)), bb = aligned(input_vid(n, 1));
             const int64_t b = B;
+            kind("binary");
             add_step(n.name, [=](cudaStream_t s) { launch_binary(op, a, bb, out, b, s); });
             return;
         }
@@ -1035,6 +1044,7 @@ struct PlanBuilder {
         case Op::Upsample: case Op::Resize: {
             TView in = view(input_vid(n, 0)), out = view(vid[n.outputs[0]]);
             const int64_t b = B;
+            kind("resize");
             add_step(n.name, [=](cudaStream_t s) { launch_resize_nearest(in, out, b, s); });
             return;
         }
@@ -1047,6 +1057,7 @@ struct PlanBuilder {
             a.ph = (int)n.params.pad_h; a.pw = (int)n.params.pad_w;
             a.mode = (n.op == Op::MaxPool2d ? 0 : 1) + (nt.mode == 1 ? 2 : 0);
             a.batch = B;
+            kind("pool");
             add_step(n.name, [a](cudaStream_t s) { launch_pool2d(a, s); });
             return;
         }
@@ -1081,7 +1092,7 @@ struct PlanBuilder {
             const int x = input_vid(n, 0), o = vid[n.outputs[0]];
             TView in = dense_f32(x, n.name);
             TView out = view(o);
-            const auto& s = V[x].shape;
+            const auto s = V[x].shape;
             const int ax = nt.mode;
             int64_t outer = 1, inner = 1;
             for (int d = 0; d < ax; ++d) outer *= s[d];
@@ -1089,6 +1100,7 @@ struct PlanBuilder {
             const int64_t axl = s[ax], per = numel_of(s), b = B;
             const float* ip = static_cast<const float*>(in.ptr);
             float* op = static_cast<float*>(const_cast<void*>(out.ptr));
+            kind("softmax");
             add_step(n.name, [=](cudaStream_t st) { launch_softmax(ip, op, outer, axl, inner, per, b, st); });
             return;
         }
@@ -1101,7 +1113,7 @@ struct PlanBuilder {
         const Node& n = nodes[ni];
         const int x = input_vid(n, 0), o = vid[n.outputs[0]];
         const int mode = note[ni].mode;
-        const auto& is = V[x].shape;
+        const auto is = V[x].shape;
         if (mode == 0) {
             TView src = view(x);
             // flat reinterpretation: copy the logical row-major order into the new shape
@@ -1155,7 +1167,7 @@ struct PlanBuilder {
         stage.img_stride = N * C * H * W;
         stage.ptr = P.alloc(std::max<size_t>((size_t)stage.img_stride * B * (src.dt == BF16 ? 2 : 4), 16));
         add_copy(nchw, stage, n.name + "/nchw");
-        const auto& od = V[o].shape;   // motor [N', H', W', C'] of ONNX target [N', C', H', W']
+        const auto od = V[o].shape;   // motor [N', H', W', C'] of ONNX target [N', C', H', W']
         TView in2 = stage;
         in2.shape[0] = od[0]; in2.shape[1] = od[1]; in2.shape[2] = od[2]; in2.shape[3] = od[3];
         const int64_t Ho = od[1], Wo = od[2], Co = od[3];
@@ -1200,6 +1212,7 @@ struct PlanBuilder {
             float* op = static_cast<float*>(const_cast<void*>(out.ptr));
             const float* ip = static_cast<const float*>(src.ptr);
             const int64_t b = B, per_in = numel_of(V[x].shape), per_out = numel_of(V[o].shape);
+            kind("gemm_f32");
             add_step(n.name, [=](cudaStream_t s) {
                 launch_gemm_f32(wp, ip, op, nullptr, Co, HWt, Ci, Ci, HWt, HWt, b, 0, per_in, per_out, s);
             });
@@ -1246,7 +1259,7 @@ struct PlanBuilder {
                         for (int64_t s = 0; s < KW; ++s)
                             for (int64_t ci = 0; ci < Ci; ++ci)
                                 h[(size_t)co * K + (r * KW + s) * Ci + ci] = f2bf(wf[((co * Ci + ci) * KH + r) * KW + s]);
-                PB_CUDA(cudaMemcpy(d, h.data(), h.size() * 2, cudaMemcpyHostToDevice));
+                if (!P.dry_) PB_CUDA(cudaMemcpy(d, h.data(), h.size() * 2, cudaMemcpyHostToDevice));
             } else {
                 std::vector<float> h((size_t)Co * K);
                 for (int64_t co = 0; co < Co; ++co)
@@ -1254,10 +1267,11 @@ struct PlanBuilder {
                         for (int64_t s = 0; s < KW; ++s)
                             for (int64_t ci = 0; ci < Ci; ++ci)
                                 h[(size_t)co * K + (r * KW + s) * Ci + ci] = wf[((co * Ci + ci) * KH + r) * KW + s];
-                PB_CUDA(cudaMemcpy(d, h.data(), h.size() * 4, cudaMemcpyHostToDevice));
+                if (!P.dry_) PB_CUDA(cudaMemcpy(d, h.data(), h.size() * 4, cudaMemcpyHostToDevice));
             }
             a.weight = d;
-            int* err = device_error_word(P.device_);
+            int* err = P.dry_ ? nullptr : device_error_word(P.device_);
+            kind(op_dt == BF16 ? "conv_tc_bf16" : "conv_tc_tf32");
             add_step(n.name, [a, op_dt, err](cudaStream_t s) { launch_conv_tc(a, op_dt, err, s); });
         } else {
             if (verbose() && prec != PREC_FP32)
@@ -1269,8 +1283,9 @@ struct PlanBuilder {
                         for (int64_t s = 0; s < KW; ++s)
                             h[((size_t)(r * KW + s) * Ci + ci) * Co + co] = wf[((co * Ci + ci) * KH + r) * KW + s];
             void* d = P.alloc(h.size() * 4);
-            PB_CUDA(cudaMemcpy(d, h.data(), h.size() * 4, cudaMemcpyHostToDevice));
+            if (!P.dry_) PB_CUDA(cudaMemcpy(d, h.data(), h.size() * 4, cudaMemcpyHostToDevice));
             a.weight = d;
+            kind("conv_simt");
             add_step(n.name, [a, ext, pp](cudaStream_t s) mutable {
                 if (ext && pp->cur_in_) a.in.ptr = pp->cur_in_;
                 launch_conv_simt(a, s);
@@ -1289,8 +1304,8 @@ struct PlanBuilder {
         TView A = dense_f32(a, n.name + "/a");
         TView Wt = dense_f32(w, n.name + "/b");
         TView O = view(o);
-        const auto& as = V[a].shape;
-        const auto& wsh = V[w].shape;
+        const auto as = V[a].shape;
+        const auto wsh = V[w].shape;
         int64_t M, K = wsh[0], N = wsh[1];
         if (note[ni].mode == 1) M = as[0] * as[1] * as[2]; else M = as[0];
         const float* bias = nullptr;
@@ -1302,6 +1317,7 @@ struct PlanBuilder {
         const float* ap = static_cast<const float*>(A.ptr);
         const float* bp = static_cast<const float*>(Wt.ptr);
         const int64_t b = B, sa = A.img_stride, sb = Wt.img_stride;
+        kind("gemm_f32");
         add_step(n.name, [=](cudaStream_t s) { launch_gemm_f32(ap, bp, tmp, bias, M, N, K, K, N, N, b, sa, sb, M * N, s); });
         if (!odense) {
             TView src = O;
@@ -1314,6 +1330,11 @@ struct PlanBuilder {
     }
 
     void build() {
+        // Value slots are reserved up front: references into V must stay valid while
+        // later values are created.
+        size_t slots = g.weights.size() + g.inputs.size() + 16;
+        for (const Node& n : g.nodes) slots += n.outputs.size() + n.inputs.size();
+        V.reserve(slots);
         fuse();
         infer();
         match_head();
@@ -1346,15 +1367,39 @@ Plan::Plan(std::shared_ptr<const Graph> g, int64_t batch, int precision, int dev
     }
 }
 
+Plan::Plan(DryTag, std::shared_ptr<const Graph> g, int64_t batch, int precision)
+    : g_(std::move(g)), dry_(true), batch_(batch), prec_(precision), device_(0) {
+    if (batch < 1) fail(ENGINE_ERR_INVALID_ARG, "batch must be >= 1");
+    build();
+}
+
+std::unique_ptr<Plan> Plan::dry_run(std::shared_ptr<const Graph> g, int64_t batch, int precision) {
+    return std::unique_ptr<Plan>(new Plan(DryTag{}, std::move(g), batch, precision));
+}
+
+std::string Plan::summary() const {
+    std::string r;
+    for (const auto& s : steps_) r += s.kind + " " + s.name + "\n";
+    return r;
+}
+
 Plan::~Plan() {
+    if (dry_) return;
     int prev = 0;
     cudaGetDevice(&prev);
     cudaSetDevice(device_);
+    for (auto& p : pending_) { cudaEventDestroy(p.second.first); cudaEventDestroy(p.second.second); }
+    for (auto e : ev_pool_) cudaEventDestroy(e);
     for (void* p : allocs_) cudaFree(p);
     cudaSetDevice(prev);
 }
 
 void* Plan::alloc(size_t bytes) {
+    if (dry_) {
+        void* p = reinterpret_cast<void*>(dry_next_);
+        dry_next_ += (bytes + 1023) & ~size_t(1023);
+        return p;
+    }
     void* p = nullptr;
     const cudaError_t e = cudaMalloc(&p, (bytes + 255) & ~size_t(255));
     if (e != cudaSuccess) {
@@ -1373,8 +1418,43 @@ void Plan::build() {
 void Plan::run(cudaStream_t s, const float* in_override, float* out_override) {
     (void)out_override;
     cur_in_ = in_override;
-    for (auto& st : steps_) st.run(s);
+    for (size_t i = 0; i < steps_.size(); ++i) {
+        if (timing_) {
+            cudaEvent_t a = take_event(), b = take_event();
+            PB_CUDA(cudaEventRecord(a, s));
+            steps_[i].run(s);
+            PB_CUDA(cudaEventRecord(b, s));
+            pending_.push_back({(int)i, {a, b}});
+        } else {
+            steps_[i].run(s);
+        }
+    }
     cur_in_ = nullptr;
+}
+
+cudaEvent_t Plan::take_event() {
+    if (ev_pool_.empty()) {
+        cudaEvent_t e;
+        PB_CUDA(cudaEventCreate(&e));
+        return e;
+    }
+    cudaEvent_t e = ev_pool_.back();
+    ev_pool_.pop_back();
+    return e;
+}
+
+std::vector<double> Plan::collect_step_ms() {
+    step_ms_.resize(steps_.size(), 0.0);
+    for (auto& p : pending_) {
+        PB_CUDA(cudaEventSynchronize(p.second.second));
+        float ms = 0.0f;
+        PB_CUDA(cudaEventElapsedTime(&ms, p.second.first, p.second.second));
+        step_ms_[p.first] += ms;
+        ev_pool_.push_back(p.second.first);
+        ev_pool_.push_back(p.second.second);
+    }
+    pending_.clear();
+    return step_ms_;
 }
 
 int64_t Plan::launch_count() const {

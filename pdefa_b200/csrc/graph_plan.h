@@ -43,11 +43,18 @@ struct PlanStep {
     std::string name;
     std::function<void(cudaStream_t)> run;
     int launches = 1;
+    std::string kind;                // kernel family, for plan summaries
 };
 
 class Plan {
 public:
     Plan(std::shared_ptr<const Graph> g, int64_t batch, int precision, int device);
+    // Device-free lowering: every pass runs and every launch is recorded, but nothing
+    // is allocated or copied (addresses are placeholders). Used to validate a model
+    // and to inspect its launch list without a GPU.
+    static std::unique_ptr<Plan> dry_run(std::shared_ptr<const Graph> g, int64_t batch, int precision);
+    // One line per launch: "<kind> <name>".
+    std::string summary() const;
     ~Plan();
     Plan(const Plan&) = delete;
     Plan& operator=(const Plan&) = delete;
@@ -65,6 +72,11 @@ public:
     void run(cudaStream_t s, const float* in_override = nullptr, float* out_override = nullptr);
     const std::vector<PlanStep>& steps() const { return steps_; }
     int64_t launch_count() const;
+    // Per-step CUDA-event timing: while enabled, run() brackets every step with
+    // events on the launching stream; collect_step_ms() waits for them and adds the
+    // elapsed times to per-step totals (one entry per step, summary() order).
+    void set_step_timing(bool on) { timing_ = on; }
+    std::vector<double> collect_step_ms();
     int64_t batch() const { return batch_; }
     int precision() const { return prec_; }
     int device() const { return device_; }
@@ -73,7 +85,11 @@ private:
     void build();
     void* alloc(size_t bytes);
 
+    struct DryTag {};
+    Plan(DryTag, std::shared_ptr<const Graph> g, int64_t batch, int precision);
     std::shared_ptr<const Graph> g_;
+    bool dry_ = false;
+    uintptr_t dry_next_ = 0x10000000;
     int64_t batch_;
     int prec_;
     int device_;
@@ -84,6 +100,11 @@ private:
     std::vector<size_t> out_bytes_;
     std::vector<std::vector<int64_t>> out_shapes_;
     std::vector<PlanStep> steps_;
+    bool timing_ = false;
+    std::vector<cudaEvent_t> ev_pool_;
+    std::vector<std::pair<int, std::pair<cudaEvent_t, cudaEvent_t>>> pending_;
+    std::vector<double> step_ms_;
+    cudaEvent_t take_event();
     const float* cur_in_ = nullptr;   // overrides valid during run()
     float* cur_out_ = nullptr;
     friend struct PlanBuilder;

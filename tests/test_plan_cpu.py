@@ -1,0 +1,58 @@
+"""Device-free lowering of the synthetic YOLOv8 graphs (engine_model_plan_summary):
+which kernel each layer gets and which reference ops disappear into fusions."""
+from collections import Counter
+
+import pytest
+
+import pdefa_b200 as pb
+from pdefa_b200.engine_file import write_engine
+from pdefa_b200.yolo import build_single_conv, build_yolov8
+
+
+@pytest.fixture(scope="module")
+def y8n(tmp_path_factory):
+    g, info = build_yolov8("n", imgsz=640)
+    p = str(tmp_path_factory.mktemp("plan") / "y8n.engine")
+    write_engine(p, g)
+    return pb.Model(pb.Context(), p), info
+
+
+def test_bf16_plan_is_all_tensor_core_and_copy_free(y8n):
+    m, info = y8n
+    steps = m.plan_summary(pb.BF16, batch=256)
+    kinds = Counter(k for k, _ in steps)
+    # 63 convs: stem on the SIMT direct path (Cin=3, NCHW fp32 input), 62 on tcgen05
+    assert kinds["conv_simt"] == 1 and kinds["conv_tc_bf16"] == 62
+    assert kinds["yolo_head"] == 1
+    assert kinds["pool"] == 3 and kinds["resize"] == 2
+    # C2f splits are views, concats are zero-copy, residual Adds live in conv epilogues
+    assert kinds["copy"] == 0 and kinds["binary"] == 0 and kinds["unary"] == 0
+    assert len(steps) == 69
+    assert steps[0] == ("conv_simt", "/model.0/conv/Conv")
+
+
+def test_fp32_plan_uses_strict_kernels_only(y8n):
+    m, _ = y8n
+    kinds = Counter(k for k, _ in m.plan_summary(pb.FP32, batch=1))
+    assert kinds["conv_simt"] == 63 and not any(k.startswith("conv_tc") for k in kinds)
+
+
+def test_tf32_plan(y8n):
+    m, _ = y8n
+    kinds = Counter(k for k, _ in m.plan_summary(pb.TF32, batch=4))
+    assert kinds["conv_tc_tf32"] == 62
+
+
+def test_unfused_head_lowers_generic_ops(y8n, monkeypatch):
+    m, _ = y8n
+    monkeypatch.setenv("PDEFA_NO_HEAD_FUSION", "1")
+    kinds = Counter(k for k, _ in m.plan_summary(pb.FP32, batch=1))
+    assert kinds["yolo_head"] == 0 and kinds["softmax"] == 1 and kinds["binary"] >= 6
+
+
+def test_stem_plan(tmp_path):
+    g, _ = build_single_conv(hw=640)
+    p = str(tmp_path / "stem.engine")
+    write_engine(p, g)
+    steps = pb.Model(pb.Context(), p).plan_summary(pb.BF16, 1)
+    assert [k for k, _ in steps] == ["conv_simt", "copy"]      # conv + NHWC->NCHW output
