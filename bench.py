@@ -167,6 +167,7 @@ def main():
     ap.add_argument("--cpu-images", type=int, default=48, help="images in the bounded CPU baseline sample")
     ap.add_argument("--ref-images", type=int, default=4, help="images per step of the reference arm")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", action="store_true", help="print per-launch milliseconds to stderr")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -210,7 +211,11 @@ def main():
     dets = torch.empty(B * max_det * 48, dtype=torch.uint8, device="cuda")
     wbytes = L.pdefa_decode_work_bytes(B, A)
     work = torch.empty(wbytes, dtype=torch.uint8, device="cuda")
-    stream = torch.cuda.current_stream().cuda_stream
+    # An explicit (non-default) stream: every launch of the step, and the CUDA events
+    # that time it, are ordered on this one stream.
+    ts = torch.cuda.Stream()
+    torch.cuda.set_stream(ts)
+    stream = ts.cuda_stream
 
     def step():
         sess.run_device(x.data_ptr(), B, None, stream)
@@ -244,6 +249,9 @@ def main():
     ms = e0.elapsed_time(e1)
     step_ms = sess.step_times(B)
     sess.set_step_timing(B, False)
+    if args.layers and rank == 0:
+        for (k, name), v in zip(summary, step_ms):
+            print(f"{v / args.steps:9.4f} ms  {k:14s} {name}", file=sys.stderr)
     t = torch.tensor([ms], device="cuda")
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
