@@ -253,7 +253,8 @@ size_t decode_work_bytes(int64_t batch, int64_t anchors) { return (size_t)batch 
 
 void launch_decode_nms(const DecodeArgs& a, cudaStream_t s) {
     if (a.anchors > kMaxKeys) fail(ENGINE_ERR_NOT_IMPL, "decode: more than 16384 anchors per image");
-    if (a.channels - 4 > kMaxClasses || a.channels < 5) fail(ENGINE_ERR_INVALID_SHAPE, "decode: bad channel count");
+    // nc <= kMaxClasses - 1: the segment table holds one entry past the last group.
+    if (a.channels - 4 > kMaxClasses - 1 || a.channels < 5) fail(ENGINE_ERR_INVALID_SHAPE, "decode: bad channel count");
     if (a.max_det < 0) fail(ENGINE_ERR_INVALID_ARG, "decode: max_det must be >= 0");
     if (a.batch == 0) return;
     const size_t smem = kMaxKeys * 8 + kMaxKeys + 3 * kMaxClasses * 4 + 16;
