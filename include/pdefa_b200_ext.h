@@ -105,6 +105,22 @@ ENGINE_API EngineStatus pdefa_decode_yolo_device(const float* d_preds, int64_t b
                                                  int32_t* d_counts, PdefaDetection* d_dets, void* d_work,
                                                  size_t work_bytes, void* stream);
 
+/* Allocation-free decode. No counterpart in the reference (its decode is Python).
+ * For callers that cannot allocate device memory when they decode (a caching
+ * allocator they must not bypass, a server that forbids cudaMalloc after start-up,
+ * a plugin host that only provides input/output buffers): same inputs, outputs and
+ * results as pdefa_decode_yolo_device, but the candidate scratch is a built-in
+ * 8 MiB device array per GPU (kept until the process exits), so at most
+ * batch * anchors <= 174762 per call (e.g. 20 images of 8400 anchors); larger calls
+ * fail with ENGINE_ERR_INVALID_ARG. The first call on a device looks up the array's
+ * device address (make it before any stream capture). Calls share the array: calls
+ * that overlap on the GPU (other streams, other threads) race and must be ordered
+ * by the caller. Allocates nothing, no cudaMalloc or cudaFree. */
+ENGINE_API EngineStatus pdefa_decode_yolo_noalloc(const float* d_preds, int64_t batch, int64_t channels,
+                                                  int64_t anchors, const PdefaPreprocessMeta* d_metas,
+                                                  double conf_thres, double iou_thres, int32_t max_det,
+                                                  int32_t* d_counts, PdefaDetection* d_dets, void* stream);
+
 /* Multi-GPU batch runner: one replica of `model` per device, contiguous shards, no
  * collective. Each device runs its shard's inference and decode and returns only
  * detections. */

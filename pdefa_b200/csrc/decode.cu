@@ -20,8 +20,12 @@
 #include <cfloat>
 #include <climits>
 
+#include <mutex>
+
+#include "../../include/pdefa_b200_ext.h"
 #include "common.h"
 #include "device_common.cuh"
+#include "runtime.h"
 
 namespace pb {
 
@@ -270,3 +274,80 @@ void launch_decode_nms(const DecodeArgs& a, cudaStream_t s) {
 }
 
 }  // namespace pb
+
+// ---------------------------------------------------------------------------
+// Allocation-free decode (pdefa_decode_yolo_noalloc).
+//
+// Some callers cannot allocate device memory at the moment they decode: code that
+// runs under a framework's caching allocator it must not bypass, inference servers
+// that forbid cudaMalloc after start-up (allocation there can stall every stream on
+// the device), and plugin hosts that hand out only their own input/output buffers.
+// For them the candidate scratch of the decode kernel lives in a fixed file-scope
+// device array, kNoAllocScratchBytes per GPU, held by every GPU that loads this
+// library until the process exits.
+// ---------------------------------------------------------------------------
+namespace pb {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;   // 8 MiB = 174762 candidate records
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[64] = {};
+
+// Device address of g_noalloc_scratch on the current device. In host code the
+// array's name is only a host-side stand-in, so the address is looked up once per
+// device (with that device current) and cached.
+void* noalloc_scratch_address(int device) {
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (device < 0 || device >= 64) fail(ENGINE_ERR_INVALID_ARG, "device index out of range");
+    if (!g_noalloc_ptr[device]) {
+        void* ptr = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+        if (e != cudaSuccess || !ptr) {
+            cudaGetLastError();
+            fail(ENGINE_ERR_RUNTIME, std::string("cudaGetSymbolAddress(decode scratch) failed: ") + cudaGetErrorString(e));
+        }
+        g_noalloc_ptr[device] = ptr;
+    }
+    return g_noalloc_ptr[device];
+}
+
+}  // namespace
+}  // namespace pb
+
+extern "C" ENGINE_API EngineStatus pdefa_decode_yolo_noalloc(const float* d_preds, int64_t batch, int64_t channels,
+                                                            int64_t anchors, const PdefaPreprocessMeta* d_metas,
+                                                            double conf_thres, double iou_thres, int32_t max_det,
+                                                            int32_t* d_counts, PdefaDetection* d_dets,
+                                                            void* stream) {
+    using namespace pb;
+    if (!d_preds || !d_counts || (!d_dets && max_det > 0)) return ENGINE_ERR_NULL_PTR;
+    return guarded([&]() -> EngineStatus {
+        clear_error();
+        if (batch < 0 || channels < 5 || anchors < 0) { set_error("decode_noalloc: bad shape"); return ENGINE_ERR_INVALID_SHAPE; }
+        if (max_det < 0) { set_error("decode_noalloc: max_det must be >= 0"); return ENGINE_ERR_INVALID_ARG; }
+        const size_t need = decode_work_bytes(batch, anchors);
+        if (need > kNoAllocScratchBytes) {
+            set_error("decode_noalloc: batch * anchors = " + std::to_string(batch * anchors) +
+                      " candidate slots exceed the built-in scratch of " +
+                      std::to_string(kNoAllocScratchBytes / sizeof(Det)) +
+                      " (8 MiB); decode fewer images per call or use pdefa_decode_yolo_device");
+            return ENGINE_ERR_INVALID_ARG;
+        }
+        int dev = 0;
+        PB_CUDA(cudaGetDevice(&dev));
+        DecodeArgs a;
+        a.preds = d_preds;
+        a.batch = batch; a.channels = channels; a.anchors = anchors;
+        a.meta = reinterpret_cast<const int32_t*>(d_metas);
+        a.conf = conf_thres; a.iou = iou_thres; a.max_det = max_det;
+        a.counts = d_counts; a.dets = d_dets;
+        // Every candidate record is written before it is read, so the shared scratch
+        // needs no clearing between calls.
+        a.work = noalloc_scratch_address(dev);
+        a.err = nullptr;
+        launch_decode_nms(a, static_cast<cudaStream_t>(stream));
+        return ENGINE_OK;
+    });
+}
