@@ -224,7 +224,7 @@ def main():
                                                  stream), "decode")
 
     summary = model.plan_summary(prec, B)
-    launches_per_step = len(summary) + 1
+    launches_per_step = len(summary) + 2          # + decode: candidate pass and per-image NMS
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()

@@ -391,8 +391,12 @@ void launch_conv_tc(const ConvArgs& a, int op_dt, int* err, cudaStream_t s) {
     p.stage_a_bytes = BM * swb;
     p.stage_b_bytes = bn * swb;
     const uint32_t stage = p.stage_a_bytes + p.stage_b_bytes;
-    int stages = (int)((200u * 1024u) / stage);
-    stages = stages < 2 ? 2 : (stages > 8 ? 8 : stages);
+    // A short ring (<= 4 slots, <= ~110 KB) keeps several CTAs resident per SM, so one
+    // CTA's epilogue and pipeline fill overlap other CTAs' loads and MMAs.
+    const int nk_total = a.kh * a.kw * (a.cin / ch);
+    int stages = nk_total < 4 ? nk_total : 4;
+    if (stages < 2) stages = 2;
+    while (stages > 2 && (size_t)stages * stage > 110u * 1024u) --stages;
     p.stages = stages;
     const uint32_t fmt = op_dt == BF16 ? 1u : 2u;
     p.idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(bn >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);

@@ -1,7 +1,7 @@
 // Batched YOLO decode + class-wise greedy NMS, bit-exact with the reference's
 // pure-Python decode_yolo / _nms / _iou (pdefa/python/src/pdefa/_bindings.py:1095-1212).
 //
-// One CTA (1024 threads) per image:
+// A grid-wide pass evaluates every anchor, then one CTA (1024 threads) per image:
 //  1. candidates in anchor order: class argmax (strict '>', first maximum wins),
 //     skip when best < conf; box (cx - w*0.5, cy - h*0.5, cx + w*0.5, cy + h*0.5) in
 //     float64; optional letterbox unmap (v - pad) * (1.0 / ratio) clamped to
@@ -84,6 +84,45 @@ __device__ void bitonic_sort(unsigned long long* keys, int np) {
     }
 }
 
+// Per anchor (all images, whole grid): class argmax (strict '>', first maximum),
+// the conf test, the float64 box and the optional letterbox unmap. The record goes
+// to the anchor's slot of the work area with `reserved` = 1 when it is a candidate.
+__global__ void decode_candidates_kernel(DecodeArgs p) {
+    const int64_t A = p.anchors, total = p.batch * A;
+    const int nc = (int)p.channels - 4;
+    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total;
+         t += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t b = t / A, a = t - b * A;
+        const float* pr = p.preds + b * p.channels * A;
+        float best = pr[4 * A + a];
+        int best_c = 0;
+        for (int c = 1; c < nc; ++c) {
+            const float s = pr[(4 + c) * A + a];
+            if (s > best) { best = s; best_c = c; }
+        }
+        Det d;
+        d.x1 = d.y1 = d.x2 = d.y2 = 0.0;
+        const bool flag = !((double)best < p.conf);
+        if (flag) {
+            const double cx = pr[a], cy = pr[A + a], w = pr[2 * A + a], h = pr[3 * A + a];
+            const double hw = __dmul_rn(w, 0.5), hh = __dmul_rn(h, 0.5);
+            d.x1 = __dsub_rn(cx, hw); d.y1 = __dsub_rn(cy, hh);
+            d.x2 = __dadd_rn(cx, hw); d.y2 = __dadd_rn(cy, hh);
+            if (p.meta) {
+                const int32_t* m = p.meta + b * 9;
+                const double ow = (double)m[2], oh = (double)m[3], px = (double)m[4], py = (double)m[5];
+                const double scale = __ddiv_rn(1.0, (double)__int_as_float(m[8]));
+                d.x1 = clamp_ref(__dmul_rn(__dsub_rn(d.x1, px), scale), ow);
+                d.y1 = clamp_ref(__dmul_rn(__dsub_rn(d.y1, py), scale), oh);
+                d.x2 = clamp_ref(__dmul_rn(__dsub_rn(d.x2, px), scale), ow);
+                d.y2 = clamp_ref(__dmul_rn(__dsub_rn(d.y2, py), scale), oh);
+            }
+        }
+        d.conf = best; d.cls = best_c; d.anchor = (int32_t)a; d.reserved = flag ? 1 : 0;
+        reinterpret_cast<Det*>(p.work)[t] = d;
+    }
+}
+
 __global__ void __launch_bounds__(kThreads, 1) decode_nms_kernel(DecodeArgs p) {
     extern __shared__ unsigned long long keys[];                       // kMaxKeys
     uint8_t* removed = reinterpret_cast<uint8_t*>(keys + kMaxKeys);    // kMaxKeys
@@ -97,35 +136,24 @@ __global__ void __launch_bounds__(kThreads, 1) decode_nms_kernel(DecodeArgs p) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int64_t A = p.anchors;
     const int nc = (int)p.channels - 4;
-    const float* pr = p.preds + (int64_t)b * p.channels * A;
     Det* cand = reinterpret_cast<Det*>(p.work) + (int64_t)b * A;
     Det* out = reinterpret_cast<Det*>(p.dets) + (int64_t)b * p.max_det;
 
-    bool has_meta = p.meta != nullptr;
-    double px = 0, py = 0, ow = 0, oh = 0, scale = 1.0;
-    if (has_meta) {
-        const int32_t* m = p.meta + (int64_t)b * 9;
-        ow = (double)m[2]; oh = (double)m[3];
-        px = (double)m[4]; py = (double)m[5];
-        scale = __ddiv_rn(1.0, (double)__int_as_float(m[8]));
-    }
     for (int c = tid; c < kMaxClasses; c += kThreads) first[c] = INT_MAX;
     if (tid == 0) { s_n = 0; s_kept = 0; }
     __syncthreads();
 
-    // ---- 1. ordered candidate extraction ----
+    // ---- 1. ordered compaction of the candidates marked by decode_candidates_kernel ----
+    // Records sit at their anchor slot; candidate k moves to slot k <= its anchor. Each
+    // chunk reads all its records before the scan's barriers and writes after them,
+    // and later chunks only read slots beyond every slot written so far.
     for (int64_t a0 = 0; a0 < A; a0 += kThreads) {
         const int64_t a = a0 + tid;
         bool flag = false;
-        float best = 0.0f;
-        int best_c = 0;
+        Det d;
         if (a < A) {
-            best = pr[4 * A + a];
-            for (int c = 1; c < nc; ++c) {
-                const float s = pr[(4 + c) * A + a];
-                if (s > best) { best = s; best_c = c; }
-            }
-            flag = !((double)best < p.conf);
+            d = cand[a];
+            flag = d.reserved != 0;
         }
         const unsigned bal = __ballot_sync(0xffffffffu, flag);
         if (lane == 0) warp_tot[warp] = __popc(bal);
@@ -142,20 +170,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_nms_kernel(DecodeArgs p) {
         if (flag) {
             const int k = s_n + (warp ? warp_tot[warp - 1] : 0) + __popc(bal & ((1u << lane) - 1u));
             if (k < kMaxKeys) {
-                const double cx = pr[a], cy = pr[A + a], w = pr[2 * A + a], h = pr[3 * A + a];
-                const double hw = __dmul_rn(w, 0.5), hh = __dmul_rn(h, 0.5);
-                Det d;
-                d.x1 = __dsub_rn(cx, hw); d.y1 = __dsub_rn(cy, hh);
-                d.x2 = __dadd_rn(cx, hw); d.y2 = __dadd_rn(cy, hh);
-                if (has_meta) {
-                    d.x1 = clamp_ref(__dmul_rn(__dsub_rn(d.x1, px), scale), ow);
-                    d.y1 = clamp_ref(__dmul_rn(__dsub_rn(d.y1, py), scale), oh);
-                    d.x2 = clamp_ref(__dmul_rn(__dsub_rn(d.x2, px), scale), ow);
-                    d.y2 = clamp_ref(__dmul_rn(__dsub_rn(d.y2, py), scale), oh);
-                }
-                d.conf = best; d.cls = best_c; d.anchor = (int32_t)a; d.reserved = 0;
+                d.reserved = 0;
                 cand[k] = d;
-                atomicMin(&first[best_c], k);
+                atomicMin(&first[d.cls], k);
             }
         }
         __syncthreads();
@@ -269,6 +286,9 @@ void launch_decode_nms(const DecodeArgs& a, cudaStream_t s) {
         PB_CUDA(cudaFuncSetAttribute(decode_nms_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
         set[dev] = true;
     }
+    int64_t cblocks = (a.batch * a.anchors + 255) / 256;
+    if (cblocks > 148 * 16) cblocks = 148 * 16;
+    if (cblocks > 0) decode_candidates_kernel<<<(unsigned)cblocks, 256, 0, s>>>(a);
     decode_nms_kernel<<<(unsigned)a.batch, kThreads, smem, s>>>(a);
     PB_CUDA(cudaGetLastError());
 }

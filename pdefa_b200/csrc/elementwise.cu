@@ -221,6 +221,97 @@ __global__ void gather_kernel(const float* data, const int64_t* idx, float* out,
     }
 }
 
+// 16-byte vector paths for NHWC views whose channels are contiguous: one thread
+// moves one pixel's group of 16 bytes (8 bf16 or 4 fp32 channels).
+bool nhwc_vec16(const TView& v) {
+    const int esz = v.dt == BF16 ? 2 : 4;
+    const int64_t vec = 16 / esz;
+    if (v.rank != 4 || v.stride[3] != 1 || v.shape[3] % vec) return false;
+    if (((uintptr_t)v.ptr) % 16) return false;
+    return (v.stride[2] % vec) == 0 && (v.stride[1] % vec) == 0 && (v.img_stride % vec) == 0;
+}
+
+__global__ void resize_nearest_vec_kernel(TView in, TView out, int64_t total, float sy, float sx, int vec) {
+    const int64_t Hi = in.shape[1], Wi = in.shape[2], G = in.shape[3] / vec;
+    const int64_t Ho = out.shape[1], Wo = out.shape[2];
+    const int esz = in.dt == BF16 ? 2 : 4;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        int64_t t = i;
+        const int64_t g = t % G; t /= G;
+        const int64_t wo = t % Wo; t /= Wo;
+        const int64_t ho = t % Ho;
+        const int64_t b = t / Ho;
+        int64_t hi = (int64_t)((float)ho * sy); if (hi > Hi - 1) hi = Hi - 1;
+        int64_t wi = (int64_t)((float)wo * sx); if (wi > Wi - 1) wi = Wi - 1;
+        const char* src = static_cast<const char*>(in.ptr) +
+                          (b * in.img_stride + hi * in.stride[1] + wi * in.stride[2] + g * vec) * esz;
+        char* dst = static_cast<char*>(const_cast<void*>(out.ptr)) +
+                    (b * out.img_stride + ho * out.stride[1] + wo * out.stride[2] + g * vec) * esz;
+        *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+    }
+}
+
+// Max pooling over 16-byte channel groups (bf16 compared as float; the result is one
+// of the inputs, so no rounding happens).
+__global__ void maxpool_vec_kernel(Pool2dArgs a, int64_t total, int vec) {
+    const int64_t H = a.in.shape[1], W = a.in.shape[2], G = a.in.shape[3] / vec;
+    const int64_t Ho = a.out.shape[1], Wo = a.out.shape[2];
+    const bool bf = a.in.dt == BF16;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        int64_t t = i;
+        const int64_t g = t % G; t /= G;
+        const int64_t wo = t % Wo; t /= Wo;
+        const int64_t ho = t % Ho;
+        const int64_t b = t / Ho;
+        float best[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) best[j] = -FLT_MAX;
+        const int64_t h0 = ho * a.sh - a.ph, w0 = wo * a.sw - a.pw;
+        for (int kh = 0; kh < a.kh; ++kh) {
+            const int64_t h = h0 + kh;
+            if (h < 0 || h >= H) continue;
+            for (int kw = 0; kw < a.kw; ++kw) {
+                const int64_t w = w0 + kw;
+                if (w < 0 || w >= W) continue;
+                const int64_t off = b * a.in.img_stride + h * a.in.stride[1] + w * a.in.stride[2] + g * vec;
+                if (bf) {
+                    const uint4 q = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.in.ptr) + off);
+                    const uint32_t u[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const __nv_bfloat162 h2 = *reinterpret_cast<const __nv_bfloat162*>(&u[j]);
+                        const float lo = __low2float(h2), hi = __high2float(h2);
+                        if (lo > best[2 * j]) best[2 * j] = lo;
+                        if (hi > best[2 * j + 1]) best[2 * j + 1] = hi;
+                    }
+                } else {
+                    const float4 q = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.in.ptr) + off);
+                    if (q.x > best[0]) best[0] = q.x;
+                    if (q.y > best[1]) best[1] = q.y;
+                    if (q.z > best[2]) best[2] = q.z;
+                    if (q.w > best[3]) best[3] = q.w;
+                }
+            }
+        }
+        const int64_t oo = b * a.out.img_stride + ho * a.out.stride[1] + wo * a.out.stride[2] + g * vec;
+        if (bf) {
+            uint32_t u[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                __nv_bfloat162 h2 = __floats2bfloat162_rn(best[2 * j], best[2 * j + 1]);
+                u[j] = *reinterpret_cast<uint32_t*>(&h2);
+            }
+            *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(const_cast<void*>(a.out.ptr)) + oo) =
+                make_uint4(u[0], u[1], u[2], u[3]);
+        } else {
+            *reinterpret_cast<float4*>(reinterpret_cast<float*>(const_cast<void*>(a.out.ptr)) + oo) =
+                make_float4(best[0], best[1], best[2], best[3]);
+        }
+    }
+}
+
 bool rows_vectorisable(const TView& in, const TView& out, int64_t* row) {
     if (in.rank < 1 || in.stride[in.rank - 1] != 1 || out.stride[out.rank - 1] != 1) return false;
     const int64_t r = in.shape[in.rank - 1];
@@ -295,6 +386,12 @@ void launch_gather(const float* data, const int64_t* idx, float* out, int64_t ou
 void launch_pool2d(const Pool2dArgs& a, cudaStream_t s) {
     const int64_t total = a.out.shape[1] * a.out.shape[2] * a.out.shape[3] * a.batch;
     if (!total) return;
+    if (a.mode == 0 && a.in.dt == a.out.dt && nhwc_vec16(a.in) && nhwc_vec16(a.out)) {
+        const int vec = a.in.dt == BF16 ? 8 : 4;
+        maxpool_vec_kernel<<<grid_for(total / vec, 256), 256, 0, s>>>(a, total / vec, vec);
+        PB_CUDA(cudaGetLastError());
+        return;
+    }
     pool2d_kernel<<<grid_for(total, 256), 256, 0, s>>>(a, total);
     PB_CUDA(cudaGetLastError());
 }
@@ -304,6 +401,12 @@ void launch_resize_nearest(const TView& in, const TView& out, int64_t batch, cud
     if (!total) return;
     const float sy = (float)in.shape[1] / (float)out.shape[1];
     const float sx = (float)in.shape[2] / (float)out.shape[2];
+    if (in.dt == out.dt && nhwc_vec16(in) && nhwc_vec16(out)) {
+        const int vec = in.dt == BF16 ? 8 : 4;
+        resize_nearest_vec_kernel<<<grid_for(total / vec, 256), 256, 0, s>>>(in, out, total / vec, sy, sx, vec);
+        PB_CUDA(cudaGetLastError());
+        return;
+    }
     resize_nearest_kernel<<<grid_for(total, 256), 256, 0, s>>>(in, out, total, sy, sx);
     PB_CUDA(cudaGetLastError());
 }

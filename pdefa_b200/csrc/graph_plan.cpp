@@ -1285,11 +1285,19 @@ struct PlanBuilder {
             void* d = P.alloc(h.size() * 4);
             if (!P.dry_) PB_CUDA(cudaMemcpy(d, h.data(), h.size() * 4, cudaMemcpyHostToDevice));
             a.weight = d;
-            kind("conv_simt");
-            add_step(n.name, [a, ext, pp](cudaStream_t s) mutable {
-                if (ext && pp->cur_in_) a.in.ptr = pp->cur_in_;
-                launch_conv_simt(a, s);
-            });
+            if (conv_direct_supported(a)) {
+                kind("conv_direct");
+                add_step(n.name, [a, ext, pp](cudaStream_t s) mutable {
+                    if (ext && pp->cur_in_) a.in.ptr = pp->cur_in_;
+                    launch_conv_direct(a, s);
+                });
+            } else {
+                kind("conv_simt");
+                add_step(n.name, [a, ext, pp](cudaStream_t s) mutable {
+                    if (ext && pp->cur_in_) a.in.ptr = pp->cur_in_;
+                    launch_conv_simt(a, s);
+                });
+            }
         }
         if (tanh_after) {
             const int64_t bt = B;

@@ -81,6 +81,11 @@ struct ConvArgs {
 // Strict fp32 SIMT implicit GEMM. weight: fp32 [kh][kw][cin][cout].
 void launch_conv_simt(const ConvArgs& a, cudaStream_t s);
 
+// Direct conv for tiny Cin (<= 8) and Cout <= 64 (the stem): fp32 FMA, weight
+// packing as for launch_conv_simt.
+bool conv_direct_supported(const ConvArgs& a);
+void launch_conv_direct(const ConvArgs& a, cudaStream_t s);
+
 // tcgen05 / TMA implicit GEMM. weight: [cout][kh][kw][cin] in the operand type
 // (bf16 for BF16, fp32 for TF32). Requires channel stride 1, 16-byte aligned pixel
 // strides and channel offsets, cin % chunk == 0 and cout % 16 == 0 (checked by

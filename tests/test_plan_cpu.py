@@ -21,20 +21,20 @@ def test_bf16_plan_is_all_tensor_core_and_copy_free(y8n):
     m, info = y8n
     steps = m.plan_summary(pb.BF16, batch=256)
     kinds = Counter(k for k, _ in steps)
-    # 63 convs: stem on the SIMT direct path (Cin=3, NCHW fp32 input), 62 on tcgen05
-    assert kinds["conv_simt"] == 1 and kinds["conv_tc_bf16"] == 62
+    # 63 convs: stem on the direct path (Cin=3, NCHW fp32 input), 62 on tcgen05
+    assert kinds["conv_direct"] == 1 and kinds["conv_tc_bf16"] == 62
     assert kinds["yolo_head"] == 1
     assert kinds["pool"] == 3 and kinds["resize"] == 2
     # C2f splits are views, concats are zero-copy, residual Adds live in conv epilogues
     assert kinds["copy"] == 0 and kinds["binary"] == 0 and kinds["unary"] == 0
     assert len(steps) == 69
-    assert steps[0] == ("conv_simt", "/model.0/conv/Conv")
+    assert steps[0] == ("conv_direct", "/model.0/conv/Conv")
 
 
 def test_fp32_plan_uses_strict_kernels_only(y8n):
     m, _ = y8n
     kinds = Counter(k for k, _ in m.plan_summary(pb.FP32, batch=1))
-    assert kinds["conv_simt"] == 63 and not any(k.startswith("conv_tc") for k in kinds)
+    assert kinds["conv_direct"] == 1 and kinds["conv_simt"] == 62 and not any(k.startswith("conv_tc") for k in kinds)
 
 
 def test_tf32_plan(y8n):
@@ -55,4 +55,4 @@ def test_stem_plan(tmp_path):
     p = str(tmp_path / "stem.engine")
     write_engine(p, g)
     steps = pb.Model(pb.Context(), p).plan_summary(pb.BF16, 1)
-    assert [k for k, _ in steps] == ["conv_simt", "copy"]      # conv + NHWC->NCHW output
+    assert [k for k, _ in steps] == ["conv_direct", "copy"]      # conv + NHWC->NCHW output
