@@ -9,13 +9,12 @@
 //     Order-preserving compaction uses warp ballots and a block scan.
 //  2. class groups are ranked by the position of their first candidate (the
 //     insertion order of the reference's defaultdict).
-//  3. keys (group, conf desc, candidate index) are bitonic-sorted in shared memory,
-//     which reproduces the reference's stable sort by confidence inside each group.
-//  4. one warp per class group runs the greedy scan: keep the next unsuppressed box,
-//     suppress later boxes whose IoU is not <= iou_thres (IoU = inter /
-//     (area_a + area_b - inter + 1e-9), 0 when the overlap is empty).
-//  5. kept boxes are re-sorted by (conf desc, group, index) -- the reference's final
-//     stable sort of keep_all -- and the first max_det are written out.
+//  3. keys (conf desc, group, candidate index) are bitonic-sorted in shared memory:
+//     the order of the reference's final stable sort of keep_all, which within a
+//     class is also its per-class stable sort by confidence.
+//  4. one greedy pass in that order keeps a box unless a kept box of its class has
+//     IoU not <= iou_thres with it (IoU = inter / (area_a + area_b - inter + 1e-9),
+//     0 when the overlap is empty) and stops after max_det kept boxes.
 // Limit: at most 16384 anchors per image (keys live in shared memory).
 #include <cfloat>
 #include <climits>
@@ -125,12 +124,10 @@ __global__ void decode_candidates_kernel(DecodeArgs p) {
 
 __global__ void __launch_bounds__(kThreads, 1) decode_nms_kernel(DecodeArgs p) {
     extern __shared__ unsigned long long keys[];                       // kMaxKeys
-    uint8_t* removed = reinterpret_cast<uint8_t*>(keys + kMaxKeys);    // kMaxKeys
-    int* first = reinterpret_cast<int*>(removed + kMaxKeys);           // kMaxClasses
-    int* grp = first + kMaxClasses;                                    // kMaxClasses
-    int* seg = grp + kMaxClasses;                                      // kMaxClasses + 1 starts
+    int* first = reinterpret_cast<int*>(keys + kMaxKeys);              // kMaxClasses
+    int* grp = first + kMaxClasses;          // kMaxClasses: group ranks, then survivor lists
     __shared__ int warp_tot[32];
-    __shared__ int s_n, s_kept, s_groups;
+    __shared__ int s_n, s_kept;
 
     const int b = blockIdx.x;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -197,15 +194,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_nms_kernel(DecodeArgs p) {
     }
     __syncthreads();
 
-    // ---- 3. sort by (group, conf desc, index) ----
+    // ---- 3. sort by the final output order: (conf desc, class group, index) ----
     int np = 1;
     while (np < n) np <<= 1;
     for (int i = tid; i < np; i += kThreads) {
         if (i < n) {
             const Det& d = cand[i];
-            keys[i] = ((unsigned long long)grp[d.cls] << 48) | ((unsigned long long)desc_key(d.conf) << 16) |
+            keys[i] = ((unsigned long long)desc_key(d.conf) << 26) | ((unsigned long long)grp[d.cls] << 16) |
                       (unsigned long long)i;
-            removed[i] = 0;
         } else {
             keys[i] = ~0ull;
         }
@@ -213,59 +209,62 @@ __global__ void __launch_bounds__(kThreads, 1) decode_nms_kernel(DecodeArgs p) {
     __syncthreads();
     bitonic_sort(keys, np);
 
-    // group segment starts
-    for (int i = tid; i < n; i += kThreads) {
-        const int g = (int)(keys[i] >> 48);
-        if (i == 0 || (int)(keys[i - 1] >> 48) != g) seg[g] = i;
-        if (i == n - 1) s_groups = g + 1;
-    }
-    if (n == 0 && tid == 0) s_groups = 0;
-    __syncthreads();
-    const int G = s_groups;
-    if (tid == 0) seg[G] = n;
-    __syncthreads();
-
-    // ---- 4. greedy NMS, one warp per class group ----
-    for (int g = warp; g < G; g += kThreads / 32) {
-        const int s0 = seg[g], s1 = seg[g + 1];
-        for (int i = s0; i < s1; ++i) {
-            __syncwarp();
-            if (removed[i]) continue;
-            const Det bi = cand[keys[i] & 0xFFFF];
-            for (int j = i + 1 + lane; j < s1; j += 32) {
-                if (removed[j]) continue;
-                const Det bj = cand[keys[j] & 0xFFFF];
-                if (!(iou_ref(bi, bj) <= p.iou)) removed[j] = 1;
+    // ---- 4. one greedy pass in output order ----
+    // A box's same-class predecessors in the reference's per-class order all come
+    // before it in this order, so deciding boxes in this order keeps exactly the
+    // boxes the per-class greedy keeps, and the first max_det kept are the output.
+    // Blocks of 1024 boxes: each thread first tests its box against everything kept
+    // before the block (kept boxes are the output records, out[0..kept0)); warp 0 then
+    // settles the block's survivors in order against boxes kept inside the block.
+    for (int base = 0; base < n && s_kept < p.max_det; base += kThreads) {
+        const int kept0 = s_kept;
+        const int i = base + tid;
+        bool alive = false;
+        Det c;
+        if (i < n) {
+            c = cand[keys[i] & 0xFFFF];
+            alive = true;
+            for (int r = 0; r < kept0; ++r) {
+                const Det& o = out[r];
+                if (o.cls == c.cls && !(iou_ref(o, c) <= p.iou)) { alive = false; break; }
             }
         }
-        __syncwarp();
-    }
-    __syncthreads();
-
-    // ---- 5. final stable order: (conf desc, group, index) ----
-    unsigned long long mine[kMaxKeys / kThreads];
-    int cnt = 0;
-    for (int i = tid; i < np; i += kThreads) {
-        unsigned long long nk = ~0ull;
-        if (i < n && !removed[i]) {
-            const uint32_t idx = (uint32_t)(keys[i] & 0xFFFF);
-            const unsigned long long g = keys[i] >> 48;
-            nk = ((unsigned long long)desc_key(cand[idx].conf) << 26) | (g << 16) | idx;
-            atomicAdd(&s_kept, 1);
+        const unsigned bal = __ballot_sync(0xffffffffu, alive);
+        if (lane == 0) warp_tot[warp] = __popc(bal);
+        __syncthreads();
+        if (warp == 0) {
+            int v = warp_tot[lane];
+            for (int o = 1; o < 32; o <<= 1) {
+                const int t = __shfl_up_sync(0xffffffffu, v, o);
+                if (lane >= o) v += t;
+            }
+            warp_tot[lane] = v;
         }
-        mine[cnt++] = nk;
+        __syncthreads();
+        if (alive) grp[(warp ? warp_tot[warp - 1] : 0) + __popc(bal & ((1u << lane) - 1u))] = i;
+        const int n_alive = warp_tot[31];
+        __syncthreads();
+        if (warp == 0) {
+            int kept = kept0;
+            for (int q = 0; q < n_alive && kept < p.max_det; ++q) {
+                const Det cq = cand[keys[grp[q]] & 0xFFFF];
+                bool sup = false;
+                for (int r = kept0 + lane; r < kept; r += 32) {
+                    const Det& o = out[r];
+                    if (o.cls == cq.cls && !(iou_ref(o, cq) <= p.iou)) sup = true;
+                }
+                sup = __any_sync(0xffffffffu, sup);
+                if (!sup) {
+                    if (lane == 0) out[kept] = cq;
+                    ++kept;
+                    __syncwarp();
+                }
+            }
+            if (lane == 0) s_kept = kept;
+        }
+        __syncthreads();
     }
-    __syncthreads();
-    cnt = 0;
-    for (int i = tid; i < np; i += kThreads) keys[i] = mine[cnt++];
-    __syncthreads();
-    bitonic_sort(keys, np);
-
-    // ---- 6. emit ----
-    const int kept = s_kept;
-    const int count = kept < p.max_det ? kept : p.max_det;
-    for (int r = tid; r < count; r += kThreads) out[r] = cand[keys[r] & 0xFFFF];
-    if (tid == 0) p.counts[b] = count;
+    if (tid == 0) p.counts[b] = s_kept;
 }
 
 }  // namespace
@@ -274,11 +273,10 @@ size_t decode_work_bytes(int64_t batch, int64_t anchors) { return (size_t)batch 
 
 void launch_decode_nms(const DecodeArgs& a, cudaStream_t s) {
     if (a.anchors > kMaxKeys) fail(ENGINE_ERR_NOT_IMPL, "decode: more than 16384 anchors per image");
-    // nc <= kMaxClasses - 1: the segment table holds one entry past the last group.
-    if (a.channels - 4 > kMaxClasses - 1 || a.channels < 5) fail(ENGINE_ERR_INVALID_SHAPE, "decode: bad channel count");
+    if (a.channels - 4 > kMaxClasses || a.channels < 5) fail(ENGINE_ERR_INVALID_SHAPE, "decode: bad channel count");
     if (a.max_det < 0) fail(ENGINE_ERR_INVALID_ARG, "decode: max_det must be >= 0");
     if (a.batch == 0) return;
-    const size_t smem = kMaxKeys * 8 + kMaxKeys + 3 * kMaxClasses * 4 + 16;
+    const size_t smem = kMaxKeys * 8 + 2 * kMaxClasses * 4;
     int dev = 0;
     PB_CUDA(cudaGetDevice(&dev));
     static bool set[64] = {};
