@@ -1,8 +1,10 @@
 // Blackwell (sm_100a) tensor-core implicit-GEMM convolution.
 //
 // GEMM view: D[M = batch*Ho*Wo pixels, N = Cout] = A[M, K] * W[N, K]^T with
-// K = kh*kw*Cin ordered (tap, channel). Per CTA one 128 x BN output tile:
-//   * warp 0 / lane 0 issues TMA loads into a ring of `stages` shared-memory slots:
+// K = kh*kw*Cin ordered (tap, channel), cut into 128 x BN output tiles. The kernel
+// is persistent (one CTA per SM, tiles taken round-robin) and warp-specialized:
+//   * warp 0 / lane 0 issues TMA loads into a ring of `stages` shared-memory slots
+//     that runs on across tile boundaries:
 //       A: im2col-mode tensor map (3x3 / strided / padded convs: the TMA unit walks
 //          128 consecutive output pixels and applies the tap offset, zero-filling
 //          padding) or a plain 2-D tiled map (1x1 stride-1 convs, GEMMs);
@@ -10,14 +12,16 @@
 //     Each load covers `CH` channels (CH*elem = 32/64/128 bytes, the swizzle width).
 //     No load uses cluster multicast.
 //   * warp 1 / lane 0 issues tcgen05.mma (kind::f16 for BF16, kind::tf32 for TF32)
-//     into a TMEM accumulator of 128 lanes x BN fp32 columns and releases slots with
-//     tcgen05.commit.
-//   * all four warps run the epilogue: tcgen05.ld of their 32 TMEM lanes, bias,
-//     activation, optional residual add, and a strided store (bf16 or fp32) that can
-//     land inside a channel slice of a concat buffer.
+//     into one of two TMEM accumulators (128 lanes x BN fp32 columns each), releases
+//     ring slots with tcgen05.commit and hands a finished accumulator to the epilogue.
+//   * warps 2-5 run the epilogue of tile t while tile t+1 accumulates: tcgen05.ld of
+//     their 32 TMEM lanes, bias, activation, optional residual add, and a strided
+//     store (bf16 or fp32) that can land inside a channel slice of a concat buffer.
 // Every mbarrier wait is bounded; on timeout the kernel records an error in the
-// device error word, drains its outstanding copies, frees TMEM and exits.
+// device error word, stops issuing work, drains its outstanding copies, frees TMEM
+// and exits.
 #include <cuda.h>
+#include <algorithm>
 #include <mutex>
 
 #include "common.h"
@@ -40,6 +44,7 @@ struct TcParams {
     void* out; int out_dt; int64_t out_img, out_sh, out_sw;
     const void* res; int res_dt; int64_t res_img, res_sh, res_sw;
     const float* bias; int act; float slope; int cout;
+    int64_t m_tiles; int n_tiles;
     int* err;
 };
 
@@ -105,8 +110,135 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// Activation of the tensor-core epilogue. The operands are BF16/TF32, so SiLU and
+// sigmoid use the hardware exponential (__expf, ~2 ulp) and a fast divide; the
+// reference's Winograd SiLU flavour and the rarer activations keep their exact form.
+template <int ACT>
+__device__ __forceinline__ float tc_act(float x, float slope) {
+    if (ACT == ACT_NONE) return x;
+    if (ACT == ACT_SILU) return __fdividef(x, 1.0f + __expf(-x));
+    if (ACT == ACT_SILU_WINO) return silu_wino_f(x);
+    return apply_act(x, ACT, slope, 0.0f);
+}
+
+__device__ __forceinline__ void load_res_chunk(const TcParams& p, int64_t rb, uint4 (&r)[4]) {
+    const uint4* src = p.res_dt == BF16
+        ? reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(p.res) + rb)
+        : reinterpret_cast<const uint4*>(reinterpret_cast<const float*>(p.res) + rb);
+    r[0] = __ldg(src);
+    r[1] = __ldg(src + 1);
+    if (p.res_dt != BF16) { r[2] = __ldg(src + 2); r[3] = __ldg(src + 3); }
+}
+
+// Epilogue for one 16-column chunk of one accumulator row: bias, activation,
+// residual, bf16/fp32 store (16 contiguous channels of one pixel).
+template <int ACT>
+__device__ __forceinline__ void epilogue_chunk(const TcParams& p, float (&v)[16], const uint4 (&r)[4],
+                                               int64_t ob, int ncol) {
+    if (p.bias) {
+        const float4* b4 = reinterpret_cast<const float4*>(p.bias + ncol);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const float4 b = __ldg(b4 + q);
+            v[4 * q] += b.x; v[4 * q + 1] += b.y; v[4 * q + 2] += b.z; v[4 * q + 3] += b.w;
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = tc_act<ACT>(v[i], p.slope);
+    if (p.res) {
+        if (p.res_dt == BF16) {
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+                const uint32_t w4[4] = {r[q].x, r[q].y, r[q].z, r[q].w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const __nv_bfloat162 h2 = *reinterpret_cast<const __nv_bfloat162*>(&w4[j]);
+                    v[q * 8 + 2 * j] += __low2float(h2);
+                    v[q * 8 + 2 * j + 1] += __high2float(h2);
+                }
+            }
+        } else {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                v[4 * q] += __uint_as_float(r[q].x); v[4 * q + 1] += __uint_as_float(r[q].y);
+                v[4 * q + 2] += __uint_as_float(r[q].z); v[4 * q + 3] += __uint_as_float(r[q].w);
+            }
+        }
+    }
+    if (p.out_dt == BF16) {
+        uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.out) + ob);
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+            uint32_t w4[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                __nv_bfloat162 h2 = __floats2bfloat162_rn(v[q * 8 + 2 * j], v[q * 8 + 2 * j + 1]);
+                w4[j] = *reinterpret_cast<uint32_t*>(&h2);
+            }
+            dst[q] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+        }
+    } else {
+        float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + ob);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) dst[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    }
+}
+
+// Epilogue warps 2..5: drain accumulator tiles in the order the MMA warp filled them.
+// The residual of the next 16 columns is loaded before the current chunk is
+// processed (the first chunk's before the accumulator wait), hiding its latency.
+template <int ACT>
+__device__ void epilogue_loop(const TcParams& p, uint32_t tmem, uint32_t half, uint64_t* tfull, uint64_t* tempty,
+                              volatile int* abort_flag, int64_t total) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int q = warp & 3;               // TMEM lane quarter this warp may access
+    const int row = q * 32 + lane;
+    const int64_t hw = (int64_t)p.Ho * p.Wo;
+    int64_t i = 0;
+    for (int64_t t = blockIdx.x; t < total; t += gridDim.x, ++i) {
+        const int buf = (int)(i & 1);
+        const int64_t mt = t / p.n_tiles;
+        const int n0 = (int)(t - mt * p.n_tiles) * p.bn;
+        const int64_t m = mt * BM + row;
+        const bool live = m < p.M;
+        int64_t ob = 0, rb = 0;
+        if (live) {
+            const int64_t b = m / hw, r = m - b * hw;
+            const int64_t ho = r / p.Wo, wo = r - ho * p.Wo;
+            ob = b * p.out_img + ho * p.out_sh + wo * p.out_sw + n0;
+            rb = b * p.res_img + ho * p.res_sh + wo * p.res_sw + n0;
+        }
+        uint4 rn[4] = {};
+        if (p.res && live) load_res_chunk(p, rb, rn);
+        bool ok = mbar_wait_bounded(&tfull[buf], (uint32_t)((i >> 1) & 1));
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) { if (lane == 0) { atomicExch(p.err, 3); *abort_flag = 1; } break; }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)buf * half;
+        for (int c0 = 0; c0 < p.bn; c0 += 16) {
+            const uint4 rc[4] = {rn[0], rn[1], rn[2], rn[3]};
+            if (p.res && live && c0 + 16 < p.bn) load_res_chunk(p, rb + c0 + 16, rn);
+            float v[16];
+            tmem_ld16(tbase + (uint32_t)c0, v);
+            if (live) epilogue_chunk<ACT>(p, v, rc, ob + c0, n0 + c0);
+        }
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[buf]);
+        if (__any_sync(0xffffffffu, *abort_flag != 0)) break;
+    }
+}
+
+// Persistent, warp-specialized kernel. 192 threads:
+//   warp 0  (lane 0): TMA producer, streams (tile, k-block) loads through the ring
+//                     without stopping at tile boundaries;
+//   warp 1  (lane 0): MMA issuer; owns two TMEM accumulators and alternates between
+//                     them, so tile t+1 accumulates while tile t is drained;
+//   warps 2-5:        epilogue; warp w reads TMEM lanes 32*(w%4).. (its row quarter).
+// Tiles are taken round-robin (tile = blockIdx.x + i*gridDim.x), N-tiles innermost
+// so CTAs working on the same pixel rows run close together (A re-reads hit L2).
 template <int KIND>
-__global__ void __launch_bounds__(128, 1)
+__global__ void __launch_bounds__(192, 4)
 conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const TcParams p) {
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
@@ -116,14 +248,15 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     const uint32_t a_bytes = p.stage_a_bytes, b_bytes = p.stage_b_bytes;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)S * (a_bytes + b_bytes));
     uint64_t* empty = full + S;
-    uint64_t* done = empty + S;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    uint64_t* tfull = empty + S;          // [2] MMA -> epilogue
+    uint64_t* tempty = tfull + 2;         // [2] epilogue -> MMA
+    uint64_t* mma_done = tempty + 2;      // all issued MMAs finished (before TMEM is freed)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t m0 = (int64_t)blockIdx.x * BM;
-    const int n0 = blockIdx.y * p.bn;
     const int nk = p.taps * p.cin_chunks;
+    const int64_t total = p.m_tiles * (int64_t)p.n_tiles;
 
     // A CTA that starts after another one recorded a timeout does no work at all.
     if (threadIdx.x == 0) *abort_flag = *reinterpret_cast<volatile int*>(p.err) != 0;
@@ -133,11 +266,12 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < S; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 1); }
-        mbar_init(done, 1);
+        for (int i = 0; i < 2; ++i) { mbar_init(&tfull[i], 1); mbar_init(&tempty[i], 4); }
+        mbar_init(mma_done, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     }
-    if (warp == 0) {
+    if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
                      ::"r"(smem_u32(tmem_slot)), "r"(p.tmem_cols) : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
@@ -146,137 +280,101 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = *tmem_slot;
+    const uint32_t half = (uint32_t)(p.tmem_cols >> 1);
 
-    if (warp == 0 && lane == 0) {
-        // ---------------- TMA producer ----------------
-        int issued = 0;
-        int64_t b = 0; int ho = 0, wo = 0;
-        if (p.a_mode == 0) {
-            const int64_t hw = (int64_t)p.Ho * p.Wo;
-            b = m0 / hw;
-            const int64_t r = m0 - b * hw;
-            ho = (int)(r / p.Wo);
-            wo = (int)(r - (int64_t)ho * p.Wo);
-        }
-        for (int kb = 0; kb < nk; ++kb) {
-            const int st = kb % S;
-            if (kb >= S && !mbar_wait_bounded(&empty[st], ((kb / S) & 1) ^ 1)) {
-                atomicExch(p.err, 1);
-                *abort_flag = 1;
-                break;
-            }
-            if (*abort_flag) break;
-            const int tap = kb / p.cin_chunks, cc = kb - tap * p.cin_chunks;
-            const uint32_t sa = base + (uint32_t)st * a_bytes;
-            const uint32_t sb = base + (uint32_t)S * a_bytes + (uint32_t)st * b_bytes;
-            mbar_expect_tx(&full[st], a_bytes + b_bytes);
-            if (p.a_mode == 0) {
-                const int r = tap / p.kw, s = tap - r * p.kw;
-                tma_load_im2col_4d(sa, &tmA, &full[st], cc * p.ch, wo * p.sw - p.pw, ho * p.sh - p.ph, (int)b,
-                                   (uint16_t)(s * p.dw), (uint16_t)(r * p.dh));
-            } else {
-                tma_load_2d(sa, &tmA, &full[st], cc * p.ch, (int)m0);
-            }
-            tma_load_2d(sb, &tmB, &full[st], tap * p.cin + cc * p.ch, n0);
-            ++issued;
-        }
-        // Drain: the last use of every slot must have landed before the CTA can exit.
-        for (int kb = issued > S ? issued - S : 0; kb < issued; ++kb) {
-            if (!mbar_wait_bounded(&full[kb % S], (kb / S) & 1)) atomicExch(p.err, 4);
-        }
-    } else if (warp == 1 && lane == 0) {
-        // ---------------- MMA issuer ----------------
-        const int ksteps = p.swb / 32;
-        for (int kb = 0; kb < nk; ++kb) {
-            const int st = kb % S;
-            if (!mbar_wait_bounded(&full[st], (kb / S) & 1)) {
-                atomicExch(p.err, 2);
-                *abort_flag = 1;
-                break;
-            }
-            if (*abort_flag) break;
-            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const uint32_t sa = base + (uint32_t)st * a_bytes;
-            const uint32_t sb = base + (uint32_t)S * a_bytes + (uint32_t)st * b_bytes;
-            for (int k = 0; k < ksteps; ++k) {
-                umma<KIND>(tmem, make_smem_desc(sa + 32u * k, p.swb), make_smem_desc(sb + 32u * k, p.swb),
-                           p.idesc, (kb | k) != 0);
-            }
-            umma_commit(&empty[st]);
-        }
-        umma_commit(done);
-    }
-    __syncwarp();
-
-    // ---------------- epilogue (all 4 warps) ----------------
-    bool ok = mbar_wait_bounded(done, 0);
-    if (!ok) { atomicExch(p.err, 3); *abort_flag = 1; }
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    const int row = warp * 32 + lane;
-    const int64_t m = m0 + row;
-    const bool live = ok && !*abort_flag && m < p.M;
-    int64_t ob = 0, rb = 0;
-    if (live) {
-        const int64_t hw = (int64_t)p.Ho * p.Wo;
-        const int64_t b = m / hw, r = m - b * hw;
-        const int64_t ho = r / p.Wo, wo = r - ho * p.Wo;
-        ob = b * p.out_img + ho * p.out_sh + wo * p.out_sw + n0;
-        rb = b * p.res_img + ho * p.res_sh + wo * p.res_sw + n0;
-    }
-    for (int c0 = 0; c0 < p.bn; c0 += 16) {
-        float v[16];
-        tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, v);
-        if (!live) continue;
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-            float x = v[i];
-            if (p.bias) x += __ldg(p.bias + n0 + c0 + i);
-            v[i] = apply_act(x, p.act, p.slope, 0.0f);
-        }
-        if (p.res) {
-            if (p.res_dt == BF16) {
-                const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(p.res) + rb + c0);
-#pragma unroll
-                for (int q = 0; q < 2; ++q) {
-                    const uint4 t = src[q];
-                    const uint32_t w4[4] = {t.x, t.y, t.z, t.w};
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const __nv_bfloat162 h2 = *reinterpret_cast<const __nv_bfloat162*>(&w4[j]);
-                        v[q * 8 + 2 * j] += __low2float(h2);
-                        v[q * 8 + 2 * j + 1] += __high2float(h2);
-                    }
-                }
-            } else {
-                const float4* src = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p.res) + rb + c0);
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const float4 t = src[q];
-                    v[4 * q] += t.x; v[4 * q + 1] += t.y; v[4 * q + 2] += t.z; v[4 * q + 3] += t.w;
-                }
-            }
-        }
-        if (p.out_dt == BF16) {
-            uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.out) + ob + c0);
-#pragma unroll
-            for (int q = 0; q < 2; ++q) {
-                uint32_t w4[4];
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    __nv_bfloat162 h2 = __floats2bfloat162_rn(v[q * 8 + 2 * j], v[q * 8 + 2 * j + 1]);
-                    w4[j] = *reinterpret_cast<uint32_t*>(&h2);
-                }
-                dst[q] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
-            }
-        } else {
-            float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + ob + c0);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) dst[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-        }
-    }
-    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-    __syncthreads();
     if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- TMA producer ----------------
+            int64_t it = 0;   // global k-block counter across tiles
+            for (int64_t t = blockIdx.x; t < total && !*abort_flag; t += gridDim.x) {
+                const int64_t mt = t / p.n_tiles;
+                const int n0 = (int)(t - mt * p.n_tiles) * p.bn;
+                const int64_t m0 = mt * BM;
+                int64_t b = 0; int ho = 0, wo = 0;
+                if (p.a_mode == 0) {
+                    const int64_t hw = (int64_t)p.Ho * p.Wo;
+                    b = m0 / hw;
+                    const int64_t r = m0 - b * hw;
+                    ho = (int)(r / p.Wo);
+                    wo = (int)(r - (int64_t)ho * p.Wo);
+                }
+                for (int kb = 0; kb < nk; ++kb, ++it) {
+                    const int st = (int)(it % S);
+                    if (it >= S && !mbar_wait_bounded(&empty[st], (uint32_t)(((it / S) & 1) ^ 1))) {
+                        atomicExch(p.err, 1);
+                        *abort_flag = 1;
+                        break;
+                    }
+                    const int tap = kb / p.cin_chunks, cc = kb - tap * p.cin_chunks;
+                    const uint32_t sa = base + (uint32_t)st * a_bytes;
+                    const uint32_t sb = base + (uint32_t)S * a_bytes + (uint32_t)st * b_bytes;
+                    mbar_expect_tx(&full[st], a_bytes + b_bytes);
+                    if (p.a_mode == 0) {
+                        const int r = tap / p.kw, s = tap - r * p.kw;
+                        tma_load_im2col_4d(sa, &tmA, &full[st], cc * p.ch, wo * p.sw - p.pw, ho * p.sh - p.ph,
+                                           (int)b, (uint16_t)(s * p.dw), (uint16_t)(r * p.dh));
+                    } else {
+                        tma_load_2d(sa, &tmA, &full[st], cc * p.ch, (int)m0);
+                    }
+                    tma_load_2d(sb, &tmB, &full[st], tap * p.cin + cc * p.ch, n0);
+                }
+            }
+            // Drain: the last use of every slot must have landed before the CTA exits.
+            for (int64_t k = it > S ? it - S : 0; k < it; ++k)
+                if (!mbar_wait_bounded(&full[k % S], (uint32_t)((k / S) & 1))) atomicExch(p.err, 4);
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---------------- MMA issuer ----------------
+            const int ksteps = p.swb / 32;
+            int64_t it = 0;
+            int64_t i = 0;    // local tile counter
+            for (int64_t t = blockIdx.x; t < total && !*abort_flag; t += gridDim.x, ++i) {
+                const int buf = (int)(i & 1);
+                if (i >= 2 && !mbar_wait_bounded(&tempty[buf], (uint32_t)(((i >> 1) & 1) ^ 1))) {
+                    atomicExch(p.err, 5);
+                    *abort_flag = 1;
+                    break;
+                }
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t d = tmem + (uint32_t)buf * half;
+                bool ok = true;
+                for (int kb = 0; kb < nk; ++kb, ++it) {
+                    const int st = (int)(it % S);
+                    if (!mbar_wait_bounded(&full[st], (uint32_t)((it / S) & 1))) { ok = false; break; }
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                    const uint32_t sa = base + (uint32_t)st * a_bytes;
+                    const uint32_t sb = base + (uint32_t)S * a_bytes + (uint32_t)st * b_bytes;
+                    for (int k = 0; k < ksteps; ++k)
+                        umma<KIND>(d, make_smem_desc(sa + 32u * k, p.swb), make_smem_desc(sb + 32u * k, p.swb),
+                                   p.idesc, (kb | k) != 0);
+                    umma_commit(&empty[st]);
+                }
+                if (!ok) { atomicExch(p.err, 2); *abort_flag = 1; break; }
+                umma_commit(&tfull[buf]);
+            }
+            umma_commit(mma_done);
+        }
+        __syncwarp();
+    } else {
+        // ---------------- epilogue (warps 2..5) ----------------
+        switch (p.act) {
+            case ACT_NONE: epilogue_loop<ACT_NONE>(p, tmem, half, tfull, tempty, abort_flag, total); break;
+            case ACT_SILU: epilogue_loop<ACT_SILU>(p, tmem, half, tfull, tempty, abort_flag, total); break;
+            case ACT_SILU_WINO: epilogue_loop<ACT_SILU_WINO>(p, tmem, half, tfull, tempty, abort_flag, total); break;
+            case ACT_RELU: epilogue_loop<ACT_RELU>(p, tmem, half, tfull, tempty, abort_flag, total); break;
+            case ACT_LEAKY: epilogue_loop<ACT_LEAKY>(p, tmem, half, tfull, tempty, abort_flag, total); break;
+            case ACT_SIGMOID: epilogue_loop<ACT_SIGMOID>(p, tmem, half, tfull, tempty, abort_flag, total); break;
+            default: epilogue_loop<ACT_GELU_TANH>(p, tmem, half, tfull, tempty, abort_flag, total); break;  // host-checked
+        }
+    }
+
+    // Free TMEM only after every issued MMA has completed.
+    __syncthreads();
+    if (warp == 1) {
+        if (!mbar_wait_bounded(mma_done, 0) && lane == 0) atomicExch(p.err, 6);
+        __syncwarp();
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(p.tmem_cols) : "memory");
     }
@@ -347,6 +445,8 @@ bool conv_tc_supported(const ConvArgs& a, int op_dt, const char** why) {
     if (a.in.stride[3] != 1 || a.out.stride[3] != 1) return no("channel stride must be 1");
     if (!pick_chunk(a.cin, esz)) return no("Cin not a multiple of the minimal chunk");
     if (!pick_bn(a.cout)) return no("Cout not a multiple of 16");
+    if (a.act < ACT_NONE || a.act > ACT_SILU_WINO) return no("activation not fusable");
+    if (a.bias && ((uintptr_t)a.bias) % 16) return no("bias not 16-byte aligned");
     if (((uintptr_t)a.in.ptr) % 16 || ((a.in.stride[2] * esz) % 16) || ((a.in.img_stride * esz) % 16) ||
         ((a.in.stride[1] * esz) % 16))
         return no("input view not 16-byte aligned");
@@ -387,16 +487,20 @@ void launch_conv_tc(const ConvArgs& a, int op_dt, int* err, cudaStream_t s) {
     p.taps = a.kh * a.kw; p.ch = ch; p.cin = a.cin; p.cin_chunks = a.cin / ch;
     p.bn = bn; p.swb = swb;
     p.tmem_cols = 32;
-    while (p.tmem_cols < bn) p.tmem_cols <<= 1;
+    while (p.tmem_cols < 2 * bn) p.tmem_cols <<= 1;    // two accumulators
     p.stage_a_bytes = BM * swb;
     p.stage_b_bytes = bn * swb;
     const uint32_t stage = p.stage_a_bytes + p.stage_b_bytes;
-    // A short ring (<= 4 slots, <= ~110 KB) keeps several CTAs resident per SM, so one
-    // CTA's epilogue and pipeline fill overlap other CTAs' loads and MMAs.
-    const int nk_total = a.kh * a.kw * (a.cin / ch);
-    int stages = nk_total < 4 ? nk_total : 4;
-    if (stages < 2) stages = 2;
-    while (stages > 2 && (size_t)stages * stage > 110u * 1024u) --stages;
+    // Persistent CTAs, several per SM when TMEM and shared memory allow: each CTA
+    // is one producer/MMA/epilogue pipeline, and small-K layers are limited by how
+    // fast epilogues drain, so more pipelines per SM beat a deeper ring. Each CTA
+    // keeps at least 4 ring slots (the ring runs on across tiles).
+    const uint32_t fixed = 1024 + 256 + 1024;     // alignment slack, barriers, per-CTA reserve
+    auto stages_for = [&](int c) { return (int)(((228u * 1024u) / (uint32_t)c - fixed) / stage); };
+    int ctas = std::min(4, 512 / p.tmem_cols);
+    while (ctas > 1 && stages_for(ctas) < 4) --ctas;
+    int stages = std::min(12, stages_for(ctas));
+    if (stages < 2) fail(ENGINE_ERR_INVALID_ARG, "conv_tc: tile does not fit in shared memory");
     p.stages = stages;
     const uint32_t fmt = op_dt == BF16 ? 1u : 2u;
     p.idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(bn >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
@@ -443,10 +547,19 @@ void launch_conv_tc(const ConvArgs& a, int op_dt, int* err, cudaStream_t s) {
                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
         if (r != CUDA_SUCCESS) fail(ENGINE_ERR_RUNTIME, "cuTensorMapEncodeTiled(W) failed: " + std::to_string((int)r));
     }
+    p.m_tiles = (M + BM - 1) / BM;
+    p.n_tiles = a.cout / bn;
     const size_t smem = (size_t)stages * stage + 1024 + 256;
-    dim3 grid((unsigned)((M + BM - 1) / BM), (unsigned)(a.cout / bn));
     int dev = 0;
     PB_CUDA(cudaGetDevice(&dev));
+    static int sm_count[64] = {};
+    int sms = 148;
+    if (dev < 64) {
+        if (!sm_count[dev]) PB_CUDA(cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev));
+        sms = sm_count[dev];
+    }
+    const int64_t tiles = p.m_tiles * p.n_tiles;
+    dim3 grid((unsigned)std::min<int64_t>(tiles, (int64_t)sms * ctas));
     static bool attr[2][64] = {};
     const int kind = op_dt == BF16 ? 0 : 1;
     if (dev < 64 && !attr[kind][dev]) {
@@ -454,8 +567,8 @@ void launch_conv_tc(const ConvArgs& a, int op_dt, int* err, cudaStream_t s) {
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
         attr[kind][dev] = true;
     }
-    if (kind == 0) conv_tc_kernel<0><<<grid, 128, smem, s>>>(tmA, tmB, p);
-    else conv_tc_kernel<1><<<grid, 128, smem, s>>>(tmA, tmB, p);
+    if (kind == 0) conv_tc_kernel<0><<<grid, 192, smem, s>>>(tmA, tmB, p);
+    else conv_tc_kernel<1><<<grid, 192, smem, s>>>(tmA, tmB, p);
     PB_CUDA(cudaGetLastError());
 }
 
