@@ -33,6 +33,10 @@ namespace {
 constexpr int kThreads = 1024;
 constexpr int kMaxKeys = 16384;
 constexpr int kMaxClasses = 1024;
+constexpr int kSub = 256;          // boxes settled per greedy sub-block
+constexpr int kKeptSmem = 512;     // kept boxes mirrored in shared memory
+constexpr size_t kNmsSmem = kMaxKeys * 8 + 2 * kMaxClasses * 4 + (kSub + kKeptSmem) * 48 +
+                            kSub * (kSub / 32) * 4 + kSub * 4;
 
 struct Det {
     double x1, y1, x2, y2;
@@ -67,16 +71,18 @@ __device__ __forceinline__ double clamp_ref(double v, double hi) {
     return v < 0.0 ? 0.0 : (v > hi ? hi : v);
 }
 
+// Bitonic sort of np (a power of two) keys, ascending; every thread takes whole
+// compare-exchange pairs, so all threads work in every pass.
 __device__ void bitonic_sort(unsigned long long* keys, int np) {
+    const int half = np >> 1;
     for (int k = 2; k <= np; k <<= 1) {
         for (int j = k >> 1; j > 0; j >>= 1) {
-            for (int i = threadIdx.x; i < np; i += kThreads) {
-                const int ixj = i ^ j;
-                if (ixj > i) {
-                    const unsigned long long a = keys[i], b = keys[ixj];
-                    const bool asc = (i & k) == 0;
-                    if ((a > b) == asc) { keys[i] = b; keys[ixj] = a; }
-                }
+            for (int t = threadIdx.x; t < half; t += kThreads) {
+                const int i = ((t & ~(j - 1)) << 1) | (t & (j - 1));   // bit log2(j) of i is 0
+                const int ixj = i | j;
+                const unsigned long long a = keys[i], b = keys[ixj];
+                const bool asc = (i & k) == 0;
+                if ((a > b) == asc) { keys[i] = b; keys[ixj] = a; }
             }
             __syncthreads();
         }
@@ -125,7 +131,7 @@ __global__ void decode_candidates_kernel(DecodeArgs p) {
 __global__ void __launch_bounds__(kThreads, 1) decode_nms_kernel(DecodeArgs p) {
     extern __shared__ unsigned long long keys[];                       // kMaxKeys
     int* first = reinterpret_cast<int*>(keys + kMaxKeys);              // kMaxClasses
-    int* grp = first + kMaxClasses;          // kMaxClasses: group ranks, then survivor lists
+    int* grp = first + kMaxClasses;          // kMaxClasses: group ranks
     __shared__ int warp_tot[32];
     __shared__ int s_n, s_kept;
 
@@ -209,58 +215,67 @@ __global__ void __launch_bounds__(kThreads, 1) decode_nms_kernel(DecodeArgs p) {
     __syncthreads();
     bitonic_sort(keys, np);
 
-    // ---- 4. one greedy pass in output order ----
+    // ---- 4. one greedy pass in output order, kSub boxes at a time ----
     // A box's same-class predecessors in the reference's per-class order all come
     // before it in this order, so deciding boxes in this order keeps exactly the
     // boxes the per-class greedy keeps, and the first max_det kept are the output.
-    // Blocks of 1024 boxes: each thread first tests its box against everything kept
-    // before the block (kept boxes are the output records, out[0..kept0)); warp 0 then
-    // settles the block's survivors in order against boxes kept inside the block.
-    for (int base = 0; base < n && s_kept < p.max_det; base += kThreads) {
+    // Per sub-block: (a) stage its records in shared memory; (b) mark boxes that a box
+    // kept before the sub-block suppresses; (c) build the in-block suppression matrix
+    // (bit i of row j: box i < j of the same class with IoU not <= thres); (d) one
+    // thread settles the boxes in order with that matrix; (e) append the kept ones.
+    Det* sub = reinterpret_cast<Det*>(grp + kMaxClasses);              // kSub
+    Det* kept_s = sub + kSub;                                          // kKeptSmem
+    uint32_t* mask = reinterpret_cast<uint32_t*>(kept_s + kKeptSmem);  // kSub * kSub / 32
+    int* pre = reinterpret_cast<int*>(mask + kSub * (kSub / 32));      // kSub
+    __shared__ uint32_t kbits[kSub / 32];
+    constexpr int kParts = kThreads / kSub;
+    for (int base = 0; base < n && s_kept < p.max_det; base += kSub) {
+        const int cnt = n - base < kSub ? n - base : kSub;
         const int kept0 = s_kept;
-        const int i = base + tid;
-        bool alive = false;
-        Det c;
-        if (i < n) {
-            c = cand[keys[i] & 0xFFFF];
-            alive = true;
-            for (int r = 0; r < kept0; ++r) {
-                const Det& o = out[r];
-                if (o.cls == c.cls && !(iou_ref(o, c) <= p.iou)) { alive = false; break; }
+        for (int i = tid; i < kSub; i += kThreads) {
+            if (i < cnt) sub[i] = cand[keys[base + i] & 0xFFFF];
+            pre[i] = 0;
+        }
+        if (tid < kSub / 32) kbits[tid] = 0;
+        __syncthreads();
+        const int j = tid % kSub, part = tid / kSub;
+        if (j < cnt) {
+            const Det c = sub[j];
+            bool sup = false;
+            for (int r = part; r < kept0 && !sup; r += kParts) {
+                const Det& o = r < kKeptSmem ? kept_s[r] : out[r];
+                if (o.cls == c.cls && !(iou_ref(o, c) <= p.iou)) sup = true;
+            }
+            if (sup) pre[j] = 1;
+            for (int w = part; w < kSub / 32; w += kParts) {
+                uint32_t bits = 0;
+                for (int t = 0; t < 32; ++t) {
+                    const int i = 32 * w + t;
+                    if (i >= j) break;
+                    const Det& o = sub[i];
+                    if (o.cls == c.cls && !(iou_ref(o, c) <= p.iou)) bits |= 1u << t;
+                }
+                mask[j * (kSub / 32) + w] = bits;
             }
         }
-        const unsigned bal = __ballot_sync(0xffffffffu, alive);
-        if (lane == 0) warp_tot[warp] = __popc(bal);
         __syncthreads();
-        if (warp == 0) {
-            int v = warp_tot[lane];
-            for (int o = 1; o < 32; o <<= 1) {
-                const int t = __shfl_up_sync(0xffffffffu, v, o);
-                if (lane >= o) v += t;
-            }
-            warp_tot[lane] = v;
-        }
-        __syncthreads();
-        if (alive) grp[(warp ? warp_tot[warp - 1] : 0) + __popc(bal & ((1u << lane) - 1u))] = i;
-        const int n_alive = warp_tot[31];
-        __syncthreads();
-        if (warp == 0) {
-            int kept = kept0;
-            for (int q = 0; q < n_alive && kept < p.max_det; ++q) {
-                const Det cq = cand[keys[grp[q]] & 0xFFFF];
+        if (tid == 0) {
+            int k = kept0;
+            for (int q = 0; q < cnt && k < p.max_det; ++q) {
+                if (pre[q]) continue;
+                const uint32_t* row = mask + q * (kSub / 32);
                 bool sup = false;
-                for (int r = kept0 + lane; r < kept; r += 32) {
-                    const Det& o = out[r];
-                    if (o.cls == cq.cls && !(iou_ref(o, cq) <= p.iou)) sup = true;
-                }
-                sup = __any_sync(0xffffffffu, sup);
-                if (!sup) {
-                    if (lane == 0) out[kept] = cq;
-                    ++kept;
-                    __syncwarp();
-                }
+                for (int w = 0; w <= (q >> 5); ++w) sup |= (row[w] & kbits[w]) != 0;
+                if (!sup) { kbits[q >> 5] |= 1u << (q & 31); ++k; }
             }
-            if (lane == 0) s_kept = kept;
+            s_kept = k;
+        }
+        __syncthreads();
+        if (tid < cnt && ((kbits[tid >> 5] >> (tid & 31)) & 1u)) {
+            int pos = kept0 + __popc(kbits[tid >> 5] & ((1u << (tid & 31)) - 1u));
+            for (int w = 0; w < (tid >> 5); ++w) pos += __popc(kbits[w]);
+            out[pos] = sub[tid];
+            if (pos < kKeptSmem) kept_s[pos] = sub[tid];
         }
         __syncthreads();
     }
@@ -276,7 +291,7 @@ void launch_decode_nms(const DecodeArgs& a, cudaStream_t s) {
     if (a.channels - 4 > kMaxClasses || a.channels < 5) fail(ENGINE_ERR_INVALID_SHAPE, "decode: bad channel count");
     if (a.max_det < 0) fail(ENGINE_ERR_INVALID_ARG, "decode: max_det must be >= 0");
     if (a.batch == 0) return;
-    const size_t smem = kMaxKeys * 8 + 2 * kMaxClasses * 4;
+    const size_t smem = kNmsSmem;
     int dev = 0;
     PB_CUDA(cudaGetDevice(&dev));
     static bool set[64] = {};

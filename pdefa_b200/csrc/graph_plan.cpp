@@ -1249,6 +1249,26 @@ struct PlanBuilder {
             a.weight = reinterpret_cast<const void*>(16);   // placeholder for the alignment check
             tc = conv_tc_supported(a, op_dt, &why);
         }
+        if (prec != PREC_FP32 && !tc && Ci > 8) {
+            // The input is not in the operand layout (a graph input in fp32 NCHW, or a
+            // view with a channel stride): stage it once into a dense NHWC buffer of the
+            // operand type and run the tensor-core path on that.
+            ConvArgs t = a;
+            t.weight = reinterpret_cast<const void*>(16);
+            t.in.dt = op_dt;
+            const int64_t H = in.shape[1], Wd = in.shape[2];
+            t.in.rank = 4;
+            t.in.stride[3] = 1; t.in.stride[2] = Ci; t.in.stride[1] = Wd * Ci; t.in.stride[0] = H * Wd * Ci;
+            t.in.img_stride = H * Wd * Ci;
+            t.in.ptr = reinterpret_cast<const void*>(256);
+            const char* why2 = nullptr;
+            if (conv_tc_supported(t, op_dt, &why2)) {
+                t.in.ptr = P.alloc(std::max<size_t>((size_t)t.in.img_stride * B * (op_dt == BF16 ? 2 : 4), 16));
+                add_copy(in, t.in, n.name + "/stage");
+                a = t;
+                tc = true;
+            }
+        }
         if (tc) {
             const int64_t K = KH * KW * Ci;
             void* d = P.alloc((size_t)Co * K * (op_dt == BF16 ? 2 : 4));
