@@ -21,6 +21,8 @@
 // device error word, stops issuing work, drains its outstanding copies, frees TMEM
 // and exits.
 #include <cuda.h>
+#include <cstdlib>
+#include <cstring>
 #include <algorithm>
 #include <mutex>
 
@@ -32,6 +34,29 @@ namespace pb {
 namespace {
 
 constexpr int BM = 128;
+// Epilogue warps per CTA: EPI = 4 (one group, one warp per TMEM lane quarter) or 8
+// (two groups that split the columns). Threads: producer warp, MMA warp, epilogue.
+template <int EPI> constexpr int conv_threads() { return 64 + 32 * EPI; }
+
+// Division by a launch-invariant divisor for n < 2^31: q = (n * m) >> p with
+// p = 31 + ceil(log2 d) and m = ceil(2^p / d) (the round-up method of Granlund and
+// Montgomery, "Division by invariant integers using multiplication", 1994).
+struct FastDiv {
+    uint64_t m = 1;
+    uint32_t p = 0, d = 1;
+};
+FastDiv make_fastdiv(uint32_t d) {
+    FastDiv f;
+    int k = 0;
+    while ((1ull << k) < d) ++k;
+    f.d = d;
+    f.p = 31u + (uint32_t)k;
+    f.m = ((1ull << f.p) + d - 1) / d;
+    return f;
+}
+__device__ __forceinline__ uint32_t fdiv(uint32_t n, const FastDiv& f) {
+    return (uint32_t)(((uint64_t)n * f.m) >> f.p);
+}
 
 struct TcParams {
     int64_t M;
@@ -45,6 +70,9 @@ struct TcParams {
     const void* res; int res_dt; int64_t res_img, res_sh, res_sw;
     const float* bias; int act; float slope; int cout;
     int64_t m_tiles; int n_tiles;
+    FastDiv div_ntiles, div_hw, div_wo;   // tile -> (m_tile, n_tile), pixel -> (image, row, col)
+    int tma_store;                        // 1: stage output chunks in shared memory, TMA-store them
+    uint32_t staging_bytes;               // bn * 128 * out element size (0 without tma_store)
     int* err;
 };
 
@@ -98,6 +126,16 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
                  ::"r"(smem_u32(bar)) : "memory");
 }
 
+// 16 consecutive fp32 columns of this thread's TMEM lane; no wait (tmem_wait_ld).
+__device__ __forceinline__ void tmem_ld16_async(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     uint32_t r[16];
     asm volatile(
@@ -113,11 +151,23 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
 // Activation of the tensor-core epilogue. The operands are BF16/TF32, so SiLU and
 // sigmoid use the hardware exponential (__expf, ~2 ulp) and a fast divide; the
 // reference's Winograd SiLU flavour and the rarer activations keep their exact form.
+__device__ __forceinline__ float tanh_approx(float x) {
+    float y;
+    asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// Activation of the tensor-core epilogue. The operands are BF16/TF32 (results are
+// held to 1e-2), so SiLU and sigmoid use the hardware tanh (one MUFU op):
+// sigmoid(x) = 0.5 + 0.5 tanh(x/2), SiLU(x) = x/2 + x/2 tanh(x/2). The reference's
+// Winograd SiLU flavour keeps its steps with an approximate final divide; the rarer
+// activations keep their exact form.
 template <int ACT>
 __device__ __forceinline__ float tc_act(float x, float slope) {
     if (ACT == ACT_NONE) return x;
-    if (ACT == ACT_SILU) return __fdividef(x, 1.0f + __expf(-x));
-    if (ACT == ACT_SILU_WINO) return silu_wino_f(x);
+    if (ACT == ACT_SILU) { const float h = 0.5f * x; return fmaf(h, tanh_approx(h), h); }
+    if (ACT == ACT_SIGMOID) return fmaf(0.5f, tanh_approx(0.5f * x), 0.5f);
+    if (ACT == ACT_SILU_WINO) return silu_wino_fast(x);
     return apply_act(x, ACT, slope, 0.0f);
 }
 
@@ -130,11 +180,10 @@ __device__ __forceinline__ void load_res_chunk(const TcParams& p, int64_t rb, ui
     if (p.res_dt != BF16) { r[2] = __ldg(src + 2); r[3] = __ldg(src + 3); }
 }
 
-// Epilogue for one 16-column chunk of one accumulator row: bias, activation,
-// residual, bf16/fp32 store (16 contiguous channels of one pixel).
+// Epilogue math for one 16-column chunk of one accumulator row: bias, activation,
+// residual add (16 contiguous channels of one pixel).
 template <int ACT>
-__device__ __forceinline__ void epilogue_chunk(const TcParams& p, float (&v)[16], const uint4 (&r)[4],
-                                               int64_t ob, int ncol) {
+__device__ __forceinline__ void epilogue_math(const TcParams& p, float (&v)[16], const uint4 (&r)[4], int ncol) {
     if (p.bias) {
         const float4* b4 = reinterpret_cast<const float4*>(p.bias + ncol);
 #pragma unroll
@@ -165,18 +214,24 @@ __device__ __forceinline__ void epilogue_chunk(const TcParams& p, float (&v)[16]
             }
         }
     }
+}
+
+__device__ __forceinline__ uint4 pack_bf16x8(const float* v) {
+    uint32_t w4[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        __nv_bfloat162 h2 = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+        w4[j] = *reinterpret_cast<uint32_t*>(&h2);
+    }
+    return make_uint4(w4[0], w4[1], w4[2], w4[3]);
+}
+
+// 16 channels of one pixel straight to global memory (views a TMA store cannot take).
+__device__ __forceinline__ void store_chunk_global(const TcParams& p, const float (&v)[16], int64_t ob) {
     if (p.out_dt == BF16) {
         uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.out) + ob);
-#pragma unroll
-        for (int q = 0; q < 2; ++q) {
-            uint32_t w4[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                __nv_bfloat162 h2 = __floats2bfloat162_rn(v[q * 8 + 2 * j], v[q * 8 + 2 * j + 1]);
-                w4[j] = *reinterpret_cast<uint32_t*>(&h2);
-            }
-            dst[q] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
-        }
+        dst[0] = pack_bf16x8(v);
+        dst[1] = pack_bf16x8(v + 8);
     } else {
         float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + ob);
 #pragma unroll
@@ -184,69 +239,165 @@ __device__ __forceinline__ void epilogue_chunk(const TcParams& p, float (&v)[16]
     }
 }
 
-// Epilogue warps 2..5: drain accumulator tiles in the order the MMA warp filled them.
-// The residual of the next 16 columns is loaded before the current chunk is
-// processed (the first chunk's before the accumulator wait), hiding its latency.
-template <int ACT>
-__device__ void epilogue_loop(const TcParams& p, uint32_t tmem, uint32_t half, uint64_t* tfull, uint64_t* tempty,
-                              volatile int* abort_flag, int64_t total) {
+// 16 channels of accumulator row `row` into the staging block of its chunk, in the
+// swizzled layout of the output tensor map (32-byte rows with SWIZZLE_32B for bf16,
+// 64-byte rows with SWIZZLE_64B for fp32): the 16-byte piece j of row r sits at
+// piece j ^ ((r >> 2) & 1), resp. j ^ ((r >> 1) & 3), so a quarter-warp's stores
+// hit distinct banks.
+__device__ __forceinline__ void store_chunk_staging(const TcParams& p, const float (&v)[16], uint8_t* blk, int row) {
+    if (p.out_dt == BF16) {
+        const int sw = (row >> 2) & 1;
+        uint4* r = reinterpret_cast<uint4*>(blk + row * 32);
+        r[0 ^ sw] = pack_bf16x8(v);
+        r[1 ^ sw] = pack_bf16x8(v + 8);
+    } else {
+        const int sw = (row >> 1) & 3;
+        float4* r = reinterpret_cast<float4*>(blk + row * 64);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) r[q ^ sw] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    }
+}
+
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int c0, int c1) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];"
+                 ::"l"(reinterpret_cast<uint64_t>(map)), "r"(src), "r"(c0), "r"(c1) : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// Named barriers 1 and 2 (one per epilogue group of 128 threads); the ids are
+// immediates so the kernel reserves only the barriers it uses.
+__device__ __forceinline__ void group_bar(int grp) {
+    if (grp == 0) asm volatile("bar.sync 1, 128;" ::: "memory");
+    else asm volatile("bar.sync 2, 128;" ::: "memory");
+}
+// Group barrier that also ORs a predicate over the group (every thread gets the result).
+__device__ __forceinline__ bool group_bar_or(int grp, bool pred) {
+    uint32_t r;
+    if (grp == 0)
+        asm volatile("{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbarrier.red.or.pred q, 1, 128, p;\n\t"
+                     "selp.u32 %0, 1, 0, q;\n\t}" : "=r"(r) : "r"((uint32_t)pred) : "memory");
+    else
+        asm volatile("{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbarrier.red.or.pred q, 2, 128, p;\n\t"
+                     "selp.u32 %0, 1, 0, q;\n\t}" : "=r"(r) : "r"((uint32_t)pred) : "memory");
+    return r != 0;
+}
+
+// Epilogue warps 2..EPI+1: drain accumulator tiles in the order the MMA warp filled
+// them. Warp w reads TMEM lanes 32*(w%4).. (its row quarter); with EPI = 8 the two
+// groups of four warps (2-5, 6-9) split the 16-column chunks (group g takes chunks
+// g, g+2, ..).
+// Addresses come from launch-invariant fast divisions and are computed before the
+// accumulator wait, with the first residual chunk; TMEM is read two chunks per
+// wait. With tma_store each group stages its chunks in shared memory and one of its
+// threads TMA-stores them (full, coalesced rows; the tensor map clips rows past M).
+template <int ACT, int EPI>
+__device__ void epilogue_loop(const TcParams& p, const CUtensorMap* tmOut, uint8_t* staging, uint32_t tmem,
+                              uint32_t half, uint64_t* tfull, uint64_t* tempty, volatile int* abort_flag,
+                              int64_t total) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int q = warp & 3;               // TMEM lane quarter this warp may access
+    constexpr int G = EPI / 4;            // groups
+    const int grp = (warp - 2) >> 2;      // 0: warps 2-5, 1: warps 6-9
     const int row = q * 32 + lane;
-    const int64_t hw = (int64_t)p.Ho * p.Wo;
+    const bool leader = (warp & 3) == 2 && lane == 0;   // warp 2 / warp 6, lane 0
+    const int nchunks = p.bn >> 4;
+    const uint32_t chunk_bytes = p.out_dt == BF16 ? 128u * 32u : 128u * 64u;
     int64_t i = 0;
     for (int64_t t = blockIdx.x; t < total; t += gridDim.x, ++i) {
         const int buf = (int)(i & 1);
-        const int64_t mt = t / p.n_tiles;
-        const int n0 = (int)(t - mt * p.n_tiles) * p.bn;
-        const int64_t m = mt * BM + row;
-        const bool live = m < p.M;
+        const uint32_t mt = fdiv((uint32_t)t, p.div_ntiles);
+        const int n0 = (int)((uint32_t)t - mt * (uint32_t)p.n_tiles) * p.bn;
+        const uint32_t m = mt * (uint32_t)BM + (uint32_t)row;
+        const bool live = (int64_t)m < p.M;
         int64_t ob = 0, rb = 0;
         if (live) {
-            const int64_t b = m / hw, r = m - b * hw;
-            const int64_t ho = r / p.Wo, wo = r - ho * p.Wo;
-            ob = b * p.out_img + ho * p.out_sh + wo * p.out_sw + n0;
-            rb = b * p.res_img + ho * p.res_sh + wo * p.res_sw + n0;
+            const uint32_t b = fdiv(m, p.div_hw), r = m - b * p.div_hw.d;
+            const uint32_t ho = fdiv(r, p.div_wo), wo = r - ho * p.div_wo.d;
+            ob = (int64_t)b * p.out_img + (int64_t)ho * p.out_sh + (int64_t)wo * p.out_sw + n0;
+            rb = (int64_t)b * p.res_img + (int64_t)ho * p.res_sh + (int64_t)wo * p.res_sw + n0;
         }
         uint4 rn[4] = {};
-        if (p.res && live) load_res_chunk(p, rb, rn);
+        if (p.res && live && grp < nchunks) load_res_chunk(p, rb + 16 * grp, rn);
         bool ok = mbar_wait_bounded(&tfull[buf], (uint32_t)((i >> 1) & 1));
         ok = __all_sync(0xffffffffu, ok);
-        if (!ok) { if (lane == 0) { atomicExch(p.err, 3); *abort_flag = 1; } break; }
+        if (p.tma_store) {
+            // One decision for the whole group (its warps meet at named barriers, so
+            // none may leave alone); the barrier also gates the staging writes on the
+            // previous tile's stores having read it.
+            if (leader) bulk_wait_read0();
+            if (group_bar_or(grp, !ok || *abort_flag != 0)) {
+                if (!ok && lane == 0) { atomicExch(p.err, 3); *abort_flag = 1; }
+                break;
+            }
+        } else if (!ok) {
+            if (lane == 0) { atomicExch(p.err, 3); *abort_flag = 1; }
+            break;
+        }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)buf * half;
-        for (int c0 = 0; c0 < p.bn; c0 += 16) {
-            const uint4 rc[4] = {rn[0], rn[1], rn[2], rn[3]};
-            if (p.res && live && c0 + 16 < p.bn) load_res_chunk(p, rb + c0 + 16, rn);
-            float v[16];
-            tmem_ld16(tbase + (uint32_t)c0, v);
-            if (live) epilogue_chunk<ACT>(p, v, rc, ob + c0, n0 + c0);
+        // EPI = 8 reads two chunks per TMEM wait; EPI = 4 reads one (fewer registers,
+        // so four CTAs fit per SM)
+        constexpr int PAIR = EPI == 8 ? 2 : 1;
+        for (int c = grp; c < nchunks; c += PAIR * G) {
+            const bool two = PAIR == 2 && c + G < nchunks;
+            uint32_t r0[16], r1[16];
+            tmem_ld16_async(tbase + (uint32_t)(16 * c), r0);
+            if (two) tmem_ld16_async(tbase + (uint32_t)(16 * (c + G)), r1);
+            tmem_wait_ld();
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                if (h == 1 && !two) break;
+                const int cc = c + G * h;           // chunk index
+                const uint4 rc[4] = {rn[0], rn[1], rn[2], rn[3]};
+                if (p.res && live && cc + G < nchunks) load_res_chunk(p, rb + 16 * (cc + G), rn);
+                float v[16];
+#pragma unroll
+                for (int k = 0; k < 16; ++k) v[k] = __uint_as_float(h ? r1[k] : r0[k]);
+                epilogue_math<ACT>(p, v, rc, n0 + 16 * cc);
+                if (p.tma_store) store_chunk_staging(p, v, staging + cc * chunk_bytes, row);
+                else if (live) store_chunk_global(p, v, ob + 16 * cc);
+            }
         }
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
         __syncwarp();
         if (lane == 0) mbar_arrive(&tempty[buf]);
-        if (__any_sync(0xffffffffu, *abort_flag != 0)) break;
+        if (p.tma_store) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            group_bar(grp);
+            if (leader) {
+                for (int c = grp; c < nchunks; c += G)
+                    tma_store_2d(tmOut, smem_u32(staging + c * chunk_bytes), n0 + 16 * c, (int)(mt * BM));
+                bulk_commit();
+            }
+        } else if (__any_sync(0xffffffffu, *abort_flag != 0)) {
+            break;
+        }
     }
+    if (p.tma_store && leader) bulk_wait0();
 }
 
-// Persistent, warp-specialized kernel. 192 threads:
+// Persistent, warp-specialized kernel. 64 + 32*EPI threads:
 //   warp 0  (lane 0): TMA producer, streams (tile, k-block) loads through the ring
 //                     without stopping at tile boundaries;
 //   warp 1  (lane 0): MMA issuer; owns two TMEM accumulators and alternates between
 //                     them, so tile t+1 accumulates while tile t is drained;
-//   warps 2-5:        epilogue; warp w reads TMEM lanes 32*(w%4).. (its row quarter).
+//   warps 2..EPI+1:   epilogue (see epilogue_loop).
 // Tiles are taken round-robin (tile = blockIdx.x + i*gridDim.x), N-tiles innermost
 // so CTAs working on the same pixel rows run close together (A re-reads hit L2).
-template <int KIND>
-__global__ void __launch_bounds__(192, 4)
-conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const TcParams p) {
+template <int KIND, int EPI>
+__global__ void __launch_bounds__(conv_threads<EPI>(), EPI == 8 ? 2 : 4)
+conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+               const __grid_constant__ CUtensorMap tmOut, const TcParams p) {
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
     uint8_t* const smem = smem_raw + (base - raw);
     const int S = p.stages;
     const uint32_t a_bytes = p.stage_a_bytes, b_bytes = p.stage_b_bytes;
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)S * (a_bytes + b_bytes));
+    uint8_t* const staging = smem;                          // output staging (tma_store), 1024-aligned
+    const uint32_t ring = base + p.staging_bytes;           // ring slots follow
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.staging_bytes + (size_t)S * (a_bytes + b_bytes));
     uint64_t* empty = full + S;
     uint64_t* tfull = empty + S;          // [2] MMA -> epilogue
     uint64_t* tempty = tfull + 2;         // [2] epilogue -> MMA
@@ -266,7 +417,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < S; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 1); }
-        for (int i = 0; i < 2; ++i) { mbar_init(&tfull[i], 1); mbar_init(&tempty[i], 4); }
+        for (int i = 0; i < 2; ++i) { mbar_init(&tfull[i], 1); mbar_init(&tempty[i], EPI); }
         mbar_init(mma_done, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -287,16 +438,15 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             // ---------------- TMA producer ----------------
             int64_t it = 0;   // global k-block counter across tiles
             for (int64_t t = blockIdx.x; t < total && !*abort_flag; t += gridDim.x) {
-                const int64_t mt = t / p.n_tiles;
-                const int n0 = (int)(t - mt * p.n_tiles) * p.bn;
-                const int64_t m0 = mt * BM;
-                int64_t b = 0; int ho = 0, wo = 0;
+                const uint32_t mt = fdiv((uint32_t)t, p.div_ntiles);
+                const int n0 = (int)((uint32_t)t - mt * (uint32_t)p.n_tiles) * p.bn;
+                const uint32_t m0 = mt * (uint32_t)BM;
+                uint32_t b = 0; int ho = 0, wo = 0;
                 if (p.a_mode == 0) {
-                    const int64_t hw = (int64_t)p.Ho * p.Wo;
-                    b = m0 / hw;
-                    const int64_t r = m0 - b * hw;
-                    ho = (int)(r / p.Wo);
-                    wo = (int)(r - (int64_t)ho * p.Wo);
+                    b = fdiv(m0, p.div_hw);
+                    const uint32_t r = m0 - b * p.div_hw.d;
+                    ho = (int)fdiv(r, p.div_wo);
+                    wo = (int)(r - (uint32_t)ho * p.div_wo.d);
                 }
                 for (int kb = 0; kb < nk; ++kb, ++it) {
                     const int st = (int)(it % S);
@@ -306,8 +456,8 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                         break;
                     }
                     const int tap = kb / p.cin_chunks, cc = kb - tap * p.cin_chunks;
-                    const uint32_t sa = base + (uint32_t)st * a_bytes;
-                    const uint32_t sb = base + (uint32_t)S * a_bytes + (uint32_t)st * b_bytes;
+                    const uint32_t sa = ring + (uint32_t)st * a_bytes;
+                    const uint32_t sb = ring + (uint32_t)S * a_bytes + (uint32_t)st * b_bytes;
                     mbar_expect_tx(&full[st], a_bytes + b_bytes);
                     if (p.a_mode == 0) {
                         const int r = tap / p.kw, s = tap - r * p.kw;
@@ -344,8 +494,8 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     const int st = (int)(it % S);
                     if (!mbar_wait_bounded(&full[st], (uint32_t)((it / S) & 1))) { ok = false; break; }
                     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                    const uint32_t sa = base + (uint32_t)st * a_bytes;
-                    const uint32_t sb = base + (uint32_t)S * a_bytes + (uint32_t)st * b_bytes;
+                    const uint32_t sa = ring + (uint32_t)st * a_bytes;
+                    const uint32_t sb = ring + (uint32_t)S * a_bytes + (uint32_t)st * b_bytes;
                     for (int k = 0; k < ksteps; ++k)
                         umma<KIND>(d, make_smem_desc(sa + 32u * k, p.swb), make_smem_desc(sb + 32u * k, p.swb),
                                    p.idesc, (kb | k) != 0);
@@ -358,15 +508,15 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         }
         __syncwarp();
     } else {
-        // ---------------- epilogue (warps 2..5) ----------------
+        // ---------------- epilogue (warps 2..EPI+1) ----------------
         switch (p.act) {
-            case ACT_NONE: epilogue_loop<ACT_NONE>(p, tmem, half, tfull, tempty, abort_flag, total); break;
-            case ACT_SILU: epilogue_loop<ACT_SILU>(p, tmem, half, tfull, tempty, abort_flag, total); break;
-            case ACT_SILU_WINO: epilogue_loop<ACT_SILU_WINO>(p, tmem, half, tfull, tempty, abort_flag, total); break;
-            case ACT_RELU: epilogue_loop<ACT_RELU>(p, tmem, half, tfull, tempty, abort_flag, total); break;
-            case ACT_LEAKY: epilogue_loop<ACT_LEAKY>(p, tmem, half, tfull, tempty, abort_flag, total); break;
-            case ACT_SIGMOID: epilogue_loop<ACT_SIGMOID>(p, tmem, half, tfull, tempty, abort_flag, total); break;
-            default: epilogue_loop<ACT_GELU_TANH>(p, tmem, half, tfull, tempty, abort_flag, total); break;  // host-checked
+            case ACT_NONE: epilogue_loop<ACT_NONE, EPI>(p, &tmOut, staging, tmem, half, tfull, tempty, abort_flag, total); break;
+            case ACT_SILU: epilogue_loop<ACT_SILU, EPI>(p, &tmOut, staging, tmem, half, tfull, tempty, abort_flag, total); break;
+            case ACT_SILU_WINO: epilogue_loop<ACT_SILU_WINO, EPI>(p, &tmOut, staging, tmem, half, tfull, tempty, abort_flag, total); break;
+            case ACT_RELU: epilogue_loop<ACT_RELU, EPI>(p, &tmOut, staging, tmem, half, tfull, tempty, abort_flag, total); break;
+            case ACT_LEAKY: epilogue_loop<ACT_LEAKY, EPI>(p, &tmOut, staging, tmem, half, tfull, tempty, abort_flag, total); break;
+            case ACT_SIGMOID: epilogue_loop<ACT_SIGMOID, EPI>(p, &tmOut, staging, tmem, half, tfull, tempty, abort_flag, total); break;
+            default: epilogue_loop<ACT_GELU_TANH, EPI>(p, &tmOut, staging, tmem, half, tfull, tempty, abort_flag, total); break;  // host-checked
         }
     }
 
@@ -446,6 +596,13 @@ bool conv_tc_supported(const ConvArgs& a, int op_dt, const char** why) {
     if (!pick_chunk(a.cin, esz)) return no("Cin not a multiple of the minimal chunk");
     if (!pick_bn(a.cout)) return no("Cout not a multiple of 16");
     if (a.act < ACT_NONE || a.act > ACT_SILU_WINO) return no("activation not fusable");
+    {
+        // tile and pixel indices use 32-bit fast division (n < 2^31)
+        const int64_t M = a.batch * a.out.shape[1] * a.out.shape[2];
+        const int bn = pick_bn(a.cout);
+        if (M + BM >= (int64_t(1) << 31) || ((M + BM - 1) / BM) * (a.cout / bn) >= (int64_t(1) << 31))
+            return no("more than 2^31 output pixels");
+    }
     if (a.bias && ((uintptr_t)a.bias) % 16) return no("bias not 16-byte aligned");
     if (((uintptr_t)a.in.ptr) % 16 || ((a.in.stride[2] * esz) % 16) || ((a.in.img_stride * esz) % 16) ||
         ((a.in.stride[1] * esz) % 16))
@@ -491,13 +648,22 @@ void launch_conv_tc(const ConvArgs& a, int op_dt, int* err, cudaStream_t s) {
     p.stage_a_bytes = BM * swb;
     p.stage_b_bytes = bn * swb;
     const uint32_t stage = p.stage_a_bytes + p.stage_b_bytes;
-    // Persistent CTAs, several per SM when TMEM and shared memory allow: each CTA
-    // is one producer/MMA/epilogue pipeline, and small-K layers are limited by how
-    // fast epilogues drain, so more pipelines per SM beat a deeper ring. Each CTA
-    // keeps at least 4 ring slots (the ring runs on across tiles).
-    const uint32_t fixed = 1024 + 256 + 1024;     // alignment slack, barriers, per-CTA reserve
+    // Two shapes of the kernel. 1x1 convs (one tap: each operand byte is loaded
+    // once) are bound by how fast tiles drain, so they get 8 epilogue warps and TMA
+    // stores through a shared-memory staging buffer (two CTAs per SM). Convs with
+    // several taps re-read the input per tap and are bound by the operand stream, so
+    // they keep 4 epilogue warps with direct stores and spend shared memory on more
+    // CTAs and deeper rings (up to four CTAs per SM).
+    const int epi = p.taps == 1 ? 8 : 4;
+    // Output staging for TMA stores: the view must have one pixel stride (a 2-D
+    // tensor map over [pixels, channels]).
+    const int oes = a.out.dt == BF16 ? 2 : 4;
+    const uint32_t staging = (uint32_t)bn * BM * oes;
+    p.tma_store = epi == 8 && pixel_dense(a.out) && staging <= 64u * 1024u;
+    p.staging_bytes = p.tma_store ? staging : 0u;
+    const uint32_t fixed = 1024 + 256 + 1024 + p.staging_bytes;   // alignment, barriers, reserve, staging
     auto stages_for = [&](int c) { return (int)(((228u * 1024u) / (uint32_t)c - fixed) / stage); };
-    int ctas = std::min(4, 512 / p.tmem_cols);
+    int ctas = std::min(epi == 8 ? 2 : 4, 512 / p.tmem_cols);     // register-file limit
     while (ctas > 1 && stages_for(ctas) < 4) --ctas;
     int stages = std::min(12, stages_for(ctas));
     if (stages < 2) fail(ENGINE_ERR_INVALID_ARG, "conv_tc: tile does not fit in shared memory");
@@ -511,7 +677,21 @@ void launch_conv_tc(const ConvArgs& a, int op_dt, int* err, cudaStream_t s) {
     p.bias = a.bias; p.act = a.act; p.slope = a.slope; p.cout = a.cout;
     p.err = err;
 
-    CUtensorMap tmA, tmB;
+    CUtensorMap tmA, tmB, tmOut;
+    std::memset(&tmOut, 0, sizeof(tmOut));
+    if (p.tma_store) {
+        // [pixels, Cout] view of the output, 16-channel boxes of 128 rows, swizzled
+        // like the staging blocks (32-byte rows for bf16, 64-byte rows for fp32)
+        cuuint64_t dims[2] = {(cuuint64_t)a.cout, (cuuint64_t)M};
+        cuuint64_t strides[1] = {(cuuint64_t)(a.out.stride[2] * oes)};
+        cuuint32_t box[2] = {16, (cuuint32_t)BM};
+        cuuint32_t es[2] = {1, 1};
+        CUresult r = g_tiled(&tmOut, a.out.dt == BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                             2, p.out, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                             a.out.dt == BF16 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B,
+                             CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) fail(ENGINE_ERR_RUNTIME, "cuTensorMapEncodeTiled(out) failed: " + std::to_string((int)r));
+    }
     const bool one = a.kh == 1 && a.kw == 1 && a.sh == 1 && a.sw == 1 && a.ph == 0 && a.pw == 0;
     if (one && pixel_dense(a.in)) {
         p.a_mode = 1;
@@ -549,7 +729,10 @@ void launch_conv_tc(const ConvArgs& a, int op_dt, int* err, cudaStream_t s) {
     }
     p.m_tiles = (M + BM - 1) / BM;
     p.n_tiles = a.cout / bn;
-    const size_t smem = (size_t)stages * stage + 1024 + 256;
+    p.div_ntiles = make_fastdiv((uint32_t)p.n_tiles);
+    p.div_hw = make_fastdiv((uint32_t)((int64_t)Ho * Wo));
+    p.div_wo = make_fastdiv((uint32_t)Wo);
+    const size_t smem = (size_t)stages * stage + p.staging_bytes + 1024 + 256;
     int dev = 0;
     PB_CUDA(cudaGetDevice(&dev));
     static int sm_count[64] = {};
@@ -560,15 +743,17 @@ void launch_conv_tc(const ConvArgs& a, int op_dt, int* err, cudaStream_t s) {
     }
     const int64_t tiles = p.m_tiles * p.n_tiles;
     dim3 grid((unsigned)std::min<int64_t>(tiles, (int64_t)sms * ctas));
-    static bool attr[2][64] = {};
+    static bool attr[4][64] = {};
     const int kind = op_dt == BF16 ? 0 : 1;
-    if (dev < 64 && !attr[kind][dev]) {
-        PB_CUDA(cudaFuncSetAttribute(kind == 0 ? conv_tc_kernel<0> : conv_tc_kernel<1>,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
-        attr[kind][dev] = true;
+    const int variant = kind * 2 + (epi == 8 ? 1 : 0);
+    void (*const fns[4])(CUtensorMap, CUtensorMap, CUtensorMap, TcParams) = {
+        conv_tc_kernel<0, 4>, conv_tc_kernel<0, 8>, conv_tc_kernel<1, 4>, conv_tc_kernel<1, 8>};
+    if (dev < 64 && !attr[variant][dev]) {
+        PB_CUDA(cudaFuncSetAttribute(fns[variant], cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+        attr[variant][dev] = true;
     }
-    if (kind == 0) conv_tc_kernel<0><<<grid, 192, smem, s>>>(tmA, tmB, p);
-    else conv_tc_kernel<1><<<grid, 192, smem, s>>>(tmA, tmB, p);
+    const int threads = epi == 8 ? conv_threads<8>() : conv_threads<4>();
+    fns[variant]<<<grid, threads, smem, s>>>(tmA, tmB, tmOut, p);
     PB_CUDA(cudaGetLastError());
 }
 

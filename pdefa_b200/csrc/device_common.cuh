@@ -42,7 +42,8 @@ __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x));
 // where 2^n is built from the exponent bits of (n + 127). Outside |x| <= 88.37626
 // it returns x (large x) or 0 (very negative x). Horner steps are fused
 // multiply-adds, as the reference is compiled with -ffp-contract=fast.
-__device__ __forceinline__ float silu_wino_f(float x) {
+template <bool FAST_DIV>
+__device__ __forceinline__ float silu_wino_impl(float x) {
     const float nx = -x;
     if (nx < -88.37626f) return x;
     if (nx > 88.37626f) return 0.0f;
@@ -58,8 +59,11 @@ __device__ __forceinline__ float silu_wino_f(float x) {
     p = fmaf(p, f, 1.0f);
     const uint32_t bits = (uint32_t)((int32_t)n + 127) << 23;
     const float scale = __uint_as_float(bits);
-    return x / fmaf(p, scale, 1.0f);
+    return FAST_DIV ? __fdividef(x, fmaf(p, scale, 1.0f)) : x / fmaf(p, scale, 1.0f);
 }
+__device__ __forceinline__ float silu_wino_f(float x) { return silu_wino_impl<false>(x); }
+// The same flavour with an approximate divide (~2 ulp), for the BF16/TF32 paths.
+__device__ __forceinline__ float silu_wino_fast(float x) { return silu_wino_impl<true>(x); }
 
 __device__ __forceinline__ float apply_act(float v, int act, float p0, float p1) {
     switch (act) {
