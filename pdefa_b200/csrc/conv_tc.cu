@@ -34,6 +34,7 @@ namespace pb {
 namespace {
 
 constexpr int BM = 128;
+constexpr int kMaxBuf = 4;                        // TMEM accumulator buffers at most
 // Epilogue warps per CTA: EPI = 4 (one group, one warp per TMEM lane quarter) or 8
 // (two groups that split the columns). Threads: producer warp, MMA warp, epilogue.
 template <int EPI> constexpr int conv_threads() { return 64 + 32 * EPI; }
@@ -64,6 +65,8 @@ struct TcParams {
     int sh, sw, ph, pw, dh, dw, kw;
     int taps, cin_chunks, ch, cin;
     int bn, stages, a_mode, tmem_cols, swb;
+    int nbuf;                             // TMEM accumulator buffers (2 or 4), bufcols columns each
+    uint32_t bufcols;
     uint32_t idesc;
     uint32_t stage_a_bytes, stage_b_bytes;
     void* out; int out_dt; int64_t out_img, out_sh, out_sw;
@@ -293,7 +296,7 @@ __device__ __forceinline__ bool group_bar_or(int grp, bool pred) {
 // threads TMA-stores them (full, coalesced rows; the tensor map clips rows past M).
 template <int ACT, int EPI>
 __device__ void epilogue_loop(const TcParams& p, const CUtensorMap* tmOut, uint8_t* staging, uint32_t tmem,
-                              uint32_t half, uint64_t* tfull, uint64_t* tempty, volatile int* abort_flag,
+                              uint64_t* tfull, uint64_t* tempty, volatile int* abort_flag,
                               int64_t total) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int q = warp & 3;               // TMEM lane quarter this warp may access
@@ -305,7 +308,8 @@ __device__ void epilogue_loop(const TcParams& p, const CUtensorMap* tmOut, uint8
     const uint32_t chunk_bytes = p.out_dt == BF16 ? 128u * 32u : 128u * 64u;
     int64_t i = 0;
     for (int64_t t = blockIdx.x; t < total; t += gridDim.x, ++i) {
-        const int buf = (int)(i & 1);
+        const int buf = (int)(i % p.nbuf);
+        const uint32_t use = (uint32_t)(i / p.nbuf);     // how often this buffer was filled before
         const uint32_t mt = fdiv((uint32_t)t, p.div_ntiles);
         const int n0 = (int)((uint32_t)t - mt * (uint32_t)p.n_tiles) * p.bn;
         const uint32_t m = mt * (uint32_t)BM + (uint32_t)row;
@@ -319,7 +323,7 @@ __device__ void epilogue_loop(const TcParams& p, const CUtensorMap* tmOut, uint8
         }
         uint4 rn[4] = {};
         if (p.res && live && grp < nchunks) load_res_chunk(p, rb + 16 * grp, rn);
-        bool ok = mbar_wait_bounded(&tfull[buf], (uint32_t)((i >> 1) & 1));
+        bool ok = mbar_wait_bounded(&tfull[buf], use & 1u);
         ok = __all_sync(0xffffffffu, ok);
         if (p.tma_store) {
             // One decision for the whole group (its warps meet at named barriers, so
@@ -335,7 +339,7 @@ __device__ void epilogue_loop(const TcParams& p, const CUtensorMap* tmOut, uint8
             break;
         }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)buf * half;
+        const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)buf * p.bufcols;
         // EPI = 8 reads two chunks per TMEM wait; EPI = 4 reads one (fewer registers,
         // so four CTAs fit per SM)
         constexpr int PAIR = EPI == 8 ? 2 : 1;
@@ -399,9 +403,9 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     const uint32_t ring = base + p.staging_bytes;           // ring slots follow
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.staging_bytes + (size_t)S * (a_bytes + b_bytes));
     uint64_t* empty = full + S;
-    uint64_t* tfull = empty + S;          // [2] MMA -> epilogue
-    uint64_t* tempty = tfull + 2;         // [2] epilogue -> MMA
-    uint64_t* mma_done = tempty + 2;      // all issued MMAs finished (before TMEM is freed)
+    uint64_t* tfull = empty + S;          // [kMaxBuf] MMA -> epilogue
+    uint64_t* tempty = tfull + kMaxBuf;   // [kMaxBuf] epilogue -> MMA
+    uint64_t* mma_done = tempty + kMaxBuf;  // all issued MMAs finished (before TMEM is freed)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -417,7 +421,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < S; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 1); }
-        for (int i = 0; i < 2; ++i) { mbar_init(&tfull[i], 1); mbar_init(&tempty[i], EPI); }
+        for (int i = 0; i < p.nbuf; ++i) { mbar_init(&tfull[i], 1); mbar_init(&tempty[i], EPI); }
         mbar_init(mma_done, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -431,7 +435,6 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = *tmem_slot;
-    const uint32_t half = (uint32_t)(p.tmem_cols >> 1);
 
     if (warp == 0) {
         if (lane == 0) {
@@ -481,14 +484,14 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             int64_t it = 0;
             int64_t i = 0;    // local tile counter
             for (int64_t t = blockIdx.x; t < total && !*abort_flag; t += gridDim.x, ++i) {
-                const int buf = (int)(i & 1);
-                if (i >= 2 && !mbar_wait_bounded(&tempty[buf], (uint32_t)(((i >> 1) & 1) ^ 1))) {
+                const int buf = (int)(i % p.nbuf);
+                if (i >= p.nbuf && !mbar_wait_bounded(&tempty[buf], (uint32_t)(((i / p.nbuf) & 1) ^ 1))) {
                     atomicExch(p.err, 5);
                     *abort_flag = 1;
                     break;
                 }
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                const uint32_t d = tmem + (uint32_t)buf * half;
+                const uint32_t d = tmem + (uint32_t)buf * p.bufcols;
                 bool ok = true;
                 for (int kb = 0; kb < nk; ++kb, ++it) {
                     const int st = (int)(it % S);
@@ -510,13 +513,13 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     } else {
         // ---------------- epilogue (warps 2..EPI+1) ----------------
         switch (p.act) {
-            case ACT_NONE: epilogue_loop<ACT_NONE, EPI>(p, &tmOut, staging, tmem, half, tfull, tempty, abort_flag, total); break;
-            case ACT_SILU: epilogue_loop<ACT_SILU, EPI>(p, &tmOut, staging, tmem, half, tfull, tempty, abort_flag, total); break;
-            case ACT_SILU_WINO: epilogue_loop<ACT_SILU_WINO, EPI>(p, &tmOut, staging, tmem, half, tfull, tempty, abort_flag, total); break;
-            case ACT_RELU: epilogue_loop<ACT_RELU, EPI>(p, &tmOut, staging, tmem, half, tfull, tempty, abort_flag, total); break;
-            case ACT_LEAKY: epilogue_loop<ACT_LEAKY, EPI>(p, &tmOut, staging, tmem, half, tfull, tempty, abort_flag, total); break;
-            case ACT_SIGMOID: epilogue_loop<ACT_SIGMOID, EPI>(p, &tmOut, staging, tmem, half, tfull, tempty, abort_flag, total); break;
-            default: epilogue_loop<ACT_GELU_TANH, EPI>(p, &tmOut, staging, tmem, half, tfull, tempty, abort_flag, total); break;  // host-checked
+            case ACT_NONE: epilogue_loop<ACT_NONE, EPI>(p, &tmOut, staging, tmem, tfull, tempty, abort_flag, total); break;
+            case ACT_SILU: epilogue_loop<ACT_SILU, EPI>(p, &tmOut, staging, tmem, tfull, tempty, abort_flag, total); break;
+            case ACT_SILU_WINO: epilogue_loop<ACT_SILU_WINO, EPI>(p, &tmOut, staging, tmem, tfull, tempty, abort_flag, total); break;
+            case ACT_RELU: epilogue_loop<ACT_RELU, EPI>(p, &tmOut, staging, tmem, tfull, tempty, abort_flag, total); break;
+            case ACT_LEAKY: epilogue_loop<ACT_LEAKY, EPI>(p, &tmOut, staging, tmem, tfull, tempty, abort_flag, total); break;
+            case ACT_SIGMOID: epilogue_loop<ACT_SIGMOID, EPI>(p, &tmOut, staging, tmem, tfull, tempty, abort_flag, total); break;
+            default: epilogue_loop<ACT_GELU_TANH, EPI>(p, &tmOut, staging, tmem, tfull, tempty, abort_flag, total); break;  // host-checked
         }
     }
 
@@ -643,8 +646,10 @@ void launch_conv_tc(const ConvArgs& a, int op_dt, int* err, cudaStream_t s) {
     p.sh = a.sh; p.sw = a.sw; p.ph = a.ph; p.pw = a.pw; p.dh = a.dh; p.dw = a.dw; p.kw = a.kw;
     p.taps = a.kh * a.kw; p.ch = ch; p.cin = a.cin; p.cin_chunks = a.cin / ch;
     p.bn = bn; p.swb = swb;
-    p.tmem_cols = 32;
-    while (p.tmem_cols < 2 * bn) p.tmem_cols <<= 1;    // two accumulators
+    p.bufcols = 32;
+    while (p.bufcols < (uint32_t)bn) p.bufcols <<= 1;
+    p.nbuf = 2;
+    p.tmem_cols = 2 * (int)p.bufcols;                   // two accumulators (four when TMEM allows, below)
     p.stage_a_bytes = BM * swb;
     p.stage_b_bytes = bn * swb;
     const uint32_t stage = p.stage_a_bytes + p.stage_b_bytes;
@@ -661,13 +666,16 @@ void launch_conv_tc(const ConvArgs& a, int op_dt, int* err, cudaStream_t s) {
     const uint32_t staging = (uint32_t)bn * BM * oes;
     p.tma_store = epi == 8 && pixel_dense(a.out) && staging <= 64u * 1024u;
     p.staging_bytes = p.tma_store ? staging : 0u;
-    const uint32_t fixed = 1024 + 256 + 1024 + p.staging_bytes;   // alignment, barriers, reserve, staging
+    const uint32_t fixed = 1024 + 512 + 1024 + p.staging_bytes;   // alignment, barriers, reserve, staging
     auto stages_for = [&](int c) { return (int)(((228u * 1024u) / (uint32_t)c - fixed) / stage); };
     int ctas = std::min(epi == 8 ? 2 : 4, 512 / p.tmem_cols);     // register-file limit
     while (ctas > 1 && stages_for(ctas) < 4) --ctas;
     int stages = std::min(12, stages_for(ctas));
     if (stages < 2) fail(ENGINE_ERR_INVALID_ARG, "conv_tc: tile does not fit in shared memory");
     p.stages = stages;
+    // With spare TMEM the MMA warp may run up to four tiles ahead of the epilogue
+    // (MMA completion latency is hidden behind more than one epilogue).
+    if (ctas * 4 * (int)p.bufcols <= 512) { p.nbuf = 4; p.tmem_cols = 4 * (int)p.bufcols; }
     const uint32_t fmt = op_dt == BF16 ? 1u : 2u;
     p.idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(bn >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
     p.out = const_cast<void*>(a.out.ptr); p.out_dt = a.out.dt;
@@ -732,7 +740,7 @@ void launch_conv_tc(const ConvArgs& a, int op_dt, int* err, cudaStream_t s) {
     p.div_ntiles = make_fastdiv((uint32_t)p.n_tiles);
     p.div_hw = make_fastdiv((uint32_t)((int64_t)Ho * Wo));
     p.div_wo = make_fastdiv((uint32_t)Wo);
-    const size_t smem = (size_t)stages * stage + p.staging_bytes + 1024 + 256;
+    const size_t smem = (size_t)stages * stage + p.staging_bytes + 1024 + 512;
     int dev = 0;
     PB_CUDA(cudaGetDevice(&dev));
     static int sm_count[64] = {};
