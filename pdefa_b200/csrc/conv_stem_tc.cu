@@ -1,0 +1,298 @@
+// Tensor-core stem convolution for BF16 precision: convs whose whole reduction
+// (kh*kw*Cin, e.g. 27 for the 3x3 RGB stem) fits one 32-wide K slab.
+//
+// K is too small for a TMA operand stream, so the CTA's threads build the A tile
+// themselves: thread m gathers the kh*kw*Cin input values of output pixel m (any
+// input view; the fp32 NCHW graph input is read in place), converts them to bf16
+// and writes one 64-byte K-major row (zero-padded to K = 32) into shared memory in
+// the SWIZZLE_64B layout. One thread issues two tcgen05.mma (M = 128, K = 16 each)
+// into a TMEM accumulator of Cout columns. The tile loop is double-buffered: while
+// the tensor core works on tile t, the threads drain tile t-1 (tcgen05.ld, bias,
+// activation, bf16 NHWC store). The weights sit in shared memory for the whole
+// persistent CTA. Every mbarrier wait is bounded (error word + early exit).
+#include <algorithm>
+
+#include "common.h"
+#include "device_common.cuh"
+
+namespace pb {
+
+namespace {
+
+constexpr int kRows = 128;     // output pixels per tile (MMA M)
+constexpr int kRowBytes = 64;  // 32 bf16 K values
+
+__device__ __forceinline__ uint64_t sw64_desc(uint32_t addr) {
+    // K-major, SWIZZLE_64B: 64-byte rows, 8-row groups 512 bytes apart (SBO).
+    uint64_t d = 0;
+    d |= (uint64_t)((addr & 0x3FFFF) >> 4);
+    d |= (uint64_t)1 << 16;
+    d |= (uint64_t)(512 >> 4) << 32;
+    d |= (uint64_t)1 << 46;
+    d |= (uint64_t)4 << 61;
+    return d;
+}
+
+// Byte offset of 16-byte piece j of row r in a SWIZZLE_64B tile (512-byte aligned).
+__device__ __forceinline__ uint32_t sw64_off(int r, int j) { return (uint32_t)(r * kRowBytes + ((j ^ ((r >> 1) & 3)) << 4)); }
+
+__device__ __forceinline__ float stem_act(float x, int act, float slope) {
+    if (act == ACT_SILU) {
+        const float h = 0.5f * x;
+        float t;
+        asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(h));
+        return fmaf(h, t, h);
+    }
+    return apply_act(x, act, slope, 0.0f);
+}
+
+struct StemParams {
+    ConvArgs a;
+    int Ho, Wo, K;
+    int64_t M, tiles;
+    int ncols;            // TMEM columns per accumulator (power of two >= cout)
+    int* err;
+};
+
+// The K = kh*kw*Cin input values of output pixel m in (tap, channel) order, zero
+// beyond K and outside the image. KH/KW/CIN > 0 fix the shape at compile time (the
+// 3x3 RGB stem) so the values stay in registers.
+template <int KH, int KW, int CIN>
+__device__ __forceinline__ void gather_row(const ConvArgs& a, const StemParams& P, int64_t m, int H, int W,
+                                           int64_t hw, float (&v)[32]) {
+#pragma unroll
+    for (int k = 0; k < 32; ++k) v[k] = 0.0f;
+    if (m >= P.M) return;
+    const int64_t b = m / hw, r = m - b * hw;
+    const int ho = (int)(r / P.Wo), wo = (int)(r - (int64_t)ho * P.Wo);
+    const int64_t ib = b * a.in.img_stride;
+    if (KH > 0) {
+#pragma unroll
+        for (int kr = 0; kr < KH; ++kr) {
+            const int hi = ho * a.sh - a.ph + kr * a.dh;
+#pragma unroll
+            for (int ks = 0; ks < KW; ++ks) {
+                const int wi = wo * a.sw - a.pw + ks * a.dw;
+                const bool in = hi >= 0 && hi < H && wi >= 0 && wi < W;
+                const int64_t off = ib + (int64_t)hi * a.in.stride[1] + (int64_t)wi * a.in.stride[2];
+#pragma unroll
+                for (int c = 0; c < CIN; ++c)
+                    v[(kr * KW + ks) * CIN + c] = in ? ld_elem(a.in.ptr, a.in.dt, off + (int64_t)c * a.in.stride[3]) : 0.0f;
+            }
+        }
+    } else {
+        float tmp[32];
+        int k = 0;
+        for (int kr = 0; kr < a.kh; ++kr) {
+            const int hi = ho * a.sh - a.ph + kr * a.dh;
+            for (int ks = 0; ks < a.kw; ++ks) {
+                const int wi = wo * a.sw - a.pw + ks * a.dw;
+                const bool in = hi >= 0 && hi < H && wi >= 0 && wi < W;
+                const int64_t off = ib + (int64_t)hi * a.in.stride[1] + (int64_t)wi * a.in.stride[2];
+                for (int c = 0; c < a.cin; ++c, ++k)
+                    tmp[k] = in ? ld_elem(a.in.ptr, a.in.dt, off + (int64_t)c * a.in.stride[3]) : 0.0f;
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = j < k ? tmp[j] : 0.0f;
+    }
+}
+
+template <int KH, int KW, int CIN>
+__global__ void __launch_bounds__(128, 4) conv_stem_tc_kernel(const StemParams P) {
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    uint8_t* const smem = smem_raw + (base - raw);
+    const ConvArgs& a = P.a;
+    const int cout = a.cout;
+    uint8_t* const sA = smem;                               // 2 x 128 rows x 64 B
+    uint8_t* const sB = smem + 2 * kRows * kRowBytes;       // cout rows x 64 B
+    uint64_t* const mbar = reinterpret_cast<uint64_t*>(sB + ((cout * kRowBytes + 1023) & ~1023));   // [2]
+    uint32_t* const tmem_slot = reinterpret_cast<uint32_t*>(mbar + 2);
+    volatile int* const abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int tid = threadIdx.x, warp = tid >> 5;
+    if (tid == 0) *abort_flag = *reinterpret_cast<volatile int*>(P.err) != 0;
+    __syncthreads();
+    if (*abort_flag) return;
+
+    // weights: [kh][kw][cin][cout] fp32 -> B row n = output channel, K-major bf16
+    const float* w = reinterpret_cast<const float*>(a.weight);
+    for (int i = tid; i < cout * 32; i += blockDim.x) {
+        const int n = i >> 5, k = i & 31;
+        const float v = k < P.K ? w[(int64_t)k * cout + n] : 0.0f;
+        __nv_bfloat16* row = reinterpret_cast<__nv_bfloat16*>(sB + sw64_off(n, k >> 3));
+        row[k & 7] = __float2bfloat16_rn(v);
+    }
+    if (tid == 0) {
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&mbar[0])) : "memory");
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&mbar[1])) : "memory");
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                     ::"r"(smem_u32(tmem_slot)), "r"(2 * P.ncols) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = *tmem_slot;
+    // BF16 A/B, F32 accumulate, K-major both, N = cout, M = 128
+    const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(cout >> 3) << 17) | ((uint32_t)(kRows >> 4) << 24);
+
+    const int H = (int)a.in.shape[1], W = (int)a.in.shape[2];
+    const int64_t hw = (int64_t)P.Ho * P.Wo;
+    const bool vec_out = a.out.stride[3] == 1 && ((uintptr_t)a.out.ptr % 16) == 0 && (a.out.stride[2] % 8) == 0 &&
+                         (a.out.stride[1] % 8) == 0 && (a.out.img_stride % 8) == 0;
+    int64_t prev_tile = -1;
+    int it = 0;
+    bool failed = false;
+    for (int64_t t = blockIdx.x;; t += gridDim.x, ++it) {
+        const bool have = t < P.tiles;
+        const int buf = it & 1;
+        if (have) {
+            // ---- gather: this thread's output pixel -> one A row (bf16, K padded to 32)
+            const int64_t m = t * kRows + tid;
+            float v[32];
+            gather_row<KH, KW, CIN>(a, P, m, H, W, hw, v);
+            uint8_t* const rowA = sA + buf * kRows * kRowBytes;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                uint32_t wd[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    __nv_bfloat162 h2 = __floats2bfloat162_rn(v[8 * j + 2 * q], v[8 * j + 2 * q + 1]);
+                    wd[q] = *reinterpret_cast<uint32_t*>(&h2);
+                }
+                *reinterpret_cast<uint4*>(rowA + sw64_off(tid, j)) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        }
+        __syncthreads();
+        if (have && tid == 0) {
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint32_t a0 = smem_u32(sA + buf * kRows * kRowBytes), b0 = smem_u32(sB);
+            const uint32_t d = tmem + (uint32_t)(buf * P.ncols);
+            for (int k = 0; k < 2; ++k) {
+                const uint64_t da = sw64_desc(a0 + 32u * k), db = sw64_desc(b0 + 32u * k);
+                asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                             "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+                             ::"r"(d), "l"(da), "l"(db), "r"(idesc), "r"(k));
+            }
+            asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                         ::"r"(smem_u32(&mbar[buf])) : "memory");
+        }
+        // ---- drain the previous tile while this one is on the tensor core
+        if (prev_tile >= 0) {
+            const int pb = buf ^ 1;
+            const uint32_t parity = (uint32_t)(((it - 1) >> 1) & 1);
+            bool ok = mbar_wait_bounded(&mbar[pb], parity, 200000000LL);
+            ok = __syncthreads_and(ok);
+            if (!ok) {
+                if (tid == 0) atomicExch(P.err, 8);
+                failed = true;
+                break;
+            }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const int64_t m = prev_tile * kRows + tid;
+            const bool live = m < P.M;
+            int64_t ob = 0;
+            if (live) {
+                const int64_t b = m / hw, r = m - b * hw;
+                const int64_t ho = r / P.Wo, wo = r - ho * P.Wo;
+                ob = b * a.out.img_stride + ho * a.out.stride[1] + wo * a.out.stride[2];
+            }
+            const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(pb * P.ncols);
+            for (int c0 = 0; c0 < cout; c0 += 16) {
+                uint32_t r[16];
+                asm volatile(
+                    "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+                    : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+                      "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+                    : "r"(taddr + (uint32_t)c0));
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                if (!live) continue;
+                float o[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    float x = __uint_as_float(r[i]) + (a.bias ? __ldg(a.bias + c0 + i) : 0.0f);
+                    o[i] = stem_act(x, a.act, a.slope);
+                }
+                if (vec_out && a.out.dt == BF16) {
+                    uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(const_cast<void*>(a.out.ptr)) + ob + c0);
+#pragma unroll
+                    for (int q = 0; q < 2; ++q) {
+                        uint32_t wd[4];
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            __nv_bfloat162 h2 = __floats2bfloat162_rn(o[8 * q + 2 * j], o[8 * q + 2 * j + 1]);
+                            wd[j] = *reinterpret_cast<uint32_t*>(&h2);
+                        }
+                        dst[q] = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 16; ++i)
+                        st_elem(const_cast<void*>(a.out.ptr), a.out.dt, ob + (int64_t)(c0 + i) * a.out.stride[3], o[i]);
+                }
+            }
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        }
+        if (!have) break;
+        prev_tile = t;
+    }
+    // Every issued MMA has completed once its tile was drained. On the error path the
+    // MMAs of this iteration and the previous one may still run: wait (bounded) for
+    // both before freeing TMEM.
+    if (failed && tid == 0) {
+        mbar_wait_bounded(&mbar[(it - 1) & 1], (uint32_t)(((it - 1) >> 1) & 1), 200000000LL);
+        if ((int64_t)blockIdx.x + (int64_t)it * gridDim.x < P.tiles)
+            mbar_wait_bounded(&mbar[it & 1], (uint32_t)((it >> 1) & 1), 200000000LL);
+    }
+    __syncthreads();
+    if (warp == 0) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * P.ncols) : "memory");
+    }
+}
+
+}  // namespace
+
+bool conv_stem_tc_supported(const ConvArgs& a) {
+    return a.kh * a.kw * a.cin <= 32 && a.cout % 16 == 0 && a.cout >= 16 && a.cout <= 256 && !a.res.ptr &&
+           a.out.dt == BF16 && (a.act >= ACT_NONE && a.act <= ACT_SILU);
+}
+
+void launch_conv_stem_tc(const ConvArgs& a, int* err, cudaStream_t s) {
+    if (!conv_stem_tc_supported(a)) fail(ENGINE_ERR_INVALID_ARG, "conv_stem_tc: layer not supported");
+    StemParams P;
+    P.a = a;
+    P.Ho = (int)a.out.shape[1];
+    P.Wo = (int)a.out.shape[2];
+    P.K = a.kh * a.kw * a.cin;
+    P.M = a.batch * P.Ho * P.Wo;
+    if (P.M == 0) return;
+    P.tiles = (P.M + kRows - 1) / kRows;
+    P.ncols = 32;
+    while (P.ncols < a.cout) P.ncols <<= 1;
+    P.err = err;
+    const size_t smem = 1024 + 2 * kRows * kRowBytes + ((a.cout * kRowBytes + 1023) & ~1023) + 64;
+    int dev = 0;
+    PB_CUDA(cudaGetDevice(&dev));
+    static int sm_count[64] = {};
+    int sms = 148;
+    if (dev < 64) {
+        if (!sm_count[dev]) PB_CUDA(cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev));
+        sms = sm_count[dev];
+    }
+    // TMEM: 2 * ncols columns per CTA, at most 512 per SM
+    const int per_sm = std::max(1, std::min(4, 512 / (2 * P.ncols)));
+    const int64_t grid = std::min<int64_t>(P.tiles, (int64_t)sms * per_sm);
+    if (a.kh == 3 && a.kw == 3 && a.cin == 3) conv_stem_tc_kernel<3, 3, 3><<<(unsigned)grid, 128, smem, s>>>(P);
+    else conv_stem_tc_kernel<0, 0, 0><<<(unsigned)grid, 128, smem, s>>>(P);
+    PB_CUDA(cudaGetLastError());
+}
+
+}  // namespace pb

@@ -1305,7 +1305,14 @@ struct PlanBuilder {
             void* d = P.alloc(h.size() * 4);
             if (!P.dry_) PB_CUDA(cudaMemcpy(d, h.data(), h.size() * 4, cudaMemcpyHostToDevice));
             a.weight = d;
-            if (conv_direct_supported(a)) {
+            if (prec == PREC_BF16 && conv_stem_tc_supported(a)) {
+                int* err = P.dry_ ? nullptr : device_error_word(P.device_);
+                kind("conv_stem_tc");
+                add_step(n.name, [a, ext, pp, err](cudaStream_t s) mutable {
+                    if (ext && pp->cur_in_) a.in.ptr = pp->cur_in_;
+                    launch_conv_stem_tc(a, err, s);
+                });
+            } else if (conv_direct_supported(a)) {
                 kind("conv_direct");
                 add_step(n.name, [a, ext, pp](cudaStream_t s) mutable {
                     if (ext && pp->cur_in_) a.in.ptr = pp->cur_in_;

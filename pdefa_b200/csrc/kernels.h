@@ -86,6 +86,12 @@ void launch_conv_simt(const ConvArgs& a, cudaStream_t s);
 bool conv_direct_supported(const ConvArgs& a);
 void launch_conv_direct(const ConvArgs& a, cudaStream_t s);
 
+// tcgen05 stem conv (BF16): kh*kw*Cin <= 32, Cout % 16 == 0 (<= 256), bf16 output, no
+// residual; threads gather im2col rows into shared memory. weight: as launch_conv_simt.
+// err: device error word for bounded waits.
+bool conv_stem_tc_supported(const ConvArgs& a);
+void launch_conv_stem_tc(const ConvArgs& a, int* err, cudaStream_t s);
+
 // tcgen05 / TMA implicit GEMM. weight: [cout][kh][kw][cin] in the operand type
 // (bf16 for BF16, fp32 for TF32). Requires channel stride 1, 16-byte aligned pixel
 // strides and channel offsets, cin % chunk == 0 and cout % 16 == 0 (checked by

@@ -49,7 +49,7 @@ def run_layer(cin, cout, k, s, hw, batch, precision="bf16", reps=5, warmup=3, ac
     ms = times[i] / reps
     p = k // 2
     ho = (hw + 2 * p - k) // s + 1
-    in_esz = 4 if summary[i][0] == "conv_direct" or prec != pb.BF16 else 2   # direct reads the fp32 input
+    in_esz = 4 if summary[i][0] in ("conv_direct", "conv_stem_tc") or prec != pb.BF16 else 2   # fp32 graph input read in place
     out_esz = 2 if prec == pb.BF16 else 4
     flops = 2.0 * cin * cout * k * k * ho * ho * batch
     bytes_ = float((in_esz * cin * hw * hw + out_esz * cout * ho * ho) * batch)

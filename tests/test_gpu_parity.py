@@ -118,13 +118,14 @@ def test_stem_cfg2_640(engine_dir, prec):
 @pytest.mark.parametrize("prec", [pb.FP32, pb.BF16])
 @pytest.mark.parametrize("cout,hw,s", [(16, 37, 2), (32, 53, 2), (48, 33, 1), (16, 20, 1)])
 def test_stem_rows_kernel_batched(engine_dir, prec, cout, hw, s):
-    """Cin=3 convs on the fp32 NCHW input (row-tiled direct kernel): odd sizes, batch 3,
-    each Cout tile width, against the fp64 oracle."""
+    """Cin=3 convs on the fp32 NCHW input (row-tiled direct kernel in FP32, tcgen05 stem
+    kernel in BF16): odd sizes, batch 3, each Cout tile width, against the fp64 oracle."""
     from oracle import onnx_numpy
     g, _ = build_single_conv(cin=3, cout=cout, k=3, s=s, hw=hw, seed=4)
     p = str(engine_dir / f"stem_rows_{cout}_{hw}_{s}.engine")
     write_engine(p, g)
-    assert [kd for kd, _ in pb.Model(pb.Context(), p).plan_summary(prec, 3)][0] == "conv_direct"
+    first = [kd for kd, _ in pb.Model(pb.Context(), p).plan_summary(prec, 3)][0]
+    assert first == ("conv_stem_tc" if prec == pb.BF16 else "conv_direct")
     x = np.random.default_rng(6).random((3, 3, hw, hw), dtype=np.float32)
     y = run_engine(p, x, prec)
     ref = onnx_numpy.run(g, [x])[0]

@@ -21,14 +21,15 @@ def test_bf16_plan_is_all_tensor_core_and_copy_free(y8n):
     m, info = y8n
     steps = m.plan_summary(pb.BF16, batch=256)
     kinds = Counter(k for k, _ in steps)
-    # 63 convs: stem on the direct path (Cin=3, NCHW fp32 input), 62 on tcgen05
-    assert kinds["conv_direct"] == 1 and kinds["conv_tc_bf16"] == 62
+    # 63 convs, all on tcgen05: the stem (Cin=3, NCHW fp32 input) gathers its own
+    # im2col rows (conv_stem_tc), the other 62 stream operands with TMA
+    assert kinds["conv_stem_tc"] == 1 and kinds["conv_tc_bf16"] == 62
     assert kinds["yolo_head"] == 1
     assert kinds["pool"] == 3 and kinds["resize"] == 2
     # C2f splits are views, concats are zero-copy, residual Adds live in conv epilogues
     assert kinds["copy"] == 0 and kinds["binary"] == 0 and kinds["unary"] == 0
     assert len(steps) == 69
-    assert steps[0] == ("conv_direct", "/model.0/conv/Conv")
+    assert steps[0] == ("conv_stem_tc", "/model.0/conv/Conv")
 
 
 def test_fp32_plan_uses_strict_kernels_only(y8n):
@@ -55,4 +56,4 @@ def test_stem_plan(tmp_path):
     p = str(tmp_path / "stem.engine")
     write_engine(p, g)
     steps = pb.Model(pb.Context(), p).plan_summary(pb.BF16, 1)
-    assert [k for k, _ in steps] == ["conv_direct", "copy"]      # conv + NHWC->NCHW output
+    assert [k for k, _ in steps] == ["conv_stem_tc", "copy"]     # conv + NHWC->NCHW output
