@@ -109,18 +109,43 @@ __device__ __forceinline__ void tma_load_im2col_4d(uint32_t dst, const CUtensorM
         : "memory");
 }
 
-template <int KIND>  // 0: kind::f16 (bf16 operands), 1: kind::tf32
-__device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc) {
+// One k-block: ksteps (1, 2 or 4) MMAs over consecutive 32-byte K slices of the A and
+// B rows, then a commit of all of them to `bar`, in one branch-free instruction
+// sequence (the extra MMAs are predicated off). A branch between a tcgen05.mma and the
+// next one costs the issuing thread a few hundred cycles, so the k-slices are never
+// issued from a loop. acc = 0 starts a fresh accumulator with the first slice.
+template <int KIND>
+__device__ __forceinline__ void umma_kblock(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc,
+                                            int ksteps, uint64_t* bar) {
+    // a 32-byte step is +2 in the descriptor's 16-byte start-address field
     if (KIND == 0) {
         asm volatile(
-            "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-            "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
-            ::"r"(tmem_d), "l"(da), "l"(db), "r"(idesc), "r"(acc));
+            "{\n\t.reg .pred pa, pt, p1, p2;\n\t.reg .b64 a1, b1, a2, b2, a3, b3;\n\t"
+            "setp.ne.b32 pa, %4, 0;\n\tsetp.eq.u32 pt, 0, 0;\n\t"
+            "setp.gt.s32 p1, %5, 1;\n\tsetp.gt.s32 p2, %5, 2;\n\t"
+            "add.s64 a1, %1, 2;\n\tadd.s64 b1, %2, 2;\n\tadd.s64 a2, %1, 4;\n\tadd.s64 b2, %2, 4;\n\t"
+            "add.s64 a3, %1, 6;\n\tadd.s64 b3, %2, 6;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, pa;\n\t"
+            "@p1 tcgen05.mma.cta_group::1.kind::f16 [%0], a1, b1, %3, pt;\n\t"
+            "@p2 tcgen05.mma.cta_group::1.kind::f16 [%0], a2, b2, %3, pt;\n\t"
+            "@p2 tcgen05.mma.cta_group::1.kind::f16 [%0], a3, b3, %3, pt;\n\t"
+            "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%6];\n\t}"
+            ::"r"(tmem_d), "l"(da), "l"(db), "r"(idesc), "r"(acc), "r"(ksteps), "r"(smem_u32(bar))
+            : "memory");
     } else {
         asm volatile(
-            "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-            "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}"
-            ::"r"(tmem_d), "l"(da), "l"(db), "r"(idesc), "r"(acc));
+            "{\n\t.reg .pred pa, pt, p1, p2;\n\t.reg .b64 a1, b1, a2, b2, a3, b3;\n\t"
+            "setp.ne.b32 pa, %4, 0;\n\tsetp.eq.u32 pt, 0, 0;\n\t"
+            "setp.gt.s32 p1, %5, 1;\n\tsetp.gt.s32 p2, %5, 2;\n\t"
+            "add.s64 a1, %1, 2;\n\tadd.s64 b1, %2, 2;\n\tadd.s64 a2, %1, 4;\n\tadd.s64 b2, %2, 4;\n\t"
+            "add.s64 a3, %1, 6;\n\tadd.s64 b3, %2, 6;\n\t"
+            "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, pa;\n\t"
+            "@p1 tcgen05.mma.cta_group::1.kind::tf32 [%0], a1, b1, %3, pt;\n\t"
+            "@p2 tcgen05.mma.cta_group::1.kind::tf32 [%0], a2, b2, %3, pt;\n\t"
+            "@p2 tcgen05.mma.cta_group::1.kind::tf32 [%0], a3, b3, %3, pt;\n\t"
+            "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%6];\n\t}"
+            ::"r"(tmem_d), "l"(da), "l"(db), "r"(idesc), "r"(acc), "r"(ksteps), "r"(smem_u32(bar))
+            : "memory");
     }
 }
 
@@ -138,18 +163,6 @@ __device__ __forceinline__ void tmem_ld16_async(uint32_t taddr, uint32_t (&r)[16
         : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
-    uint32_t r[16];
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-}
 
 // Activation of the tensor-core epilogue. The operands are BF16/TF32, so SiLU and
 // sigmoid use the hardware exponential (__expf, ~2 ulp) and a fast divide; the
@@ -499,10 +512,8 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                     const uint32_t sa = ring + (uint32_t)st * a_bytes;
                     const uint32_t sb = ring + (uint32_t)S * a_bytes + (uint32_t)st * b_bytes;
-                    for (int k = 0; k < ksteps; ++k)
-                        umma<KIND>(d, make_smem_desc(sa + 32u * k, p.swb), make_smem_desc(sb + 32u * k, p.swb),
-                                   p.idesc, (kb | k) != 0);
-                    umma_commit(&empty[st]);
+                    umma_kblock<KIND>(d, make_smem_desc(sa, p.swb), make_smem_desc(sb, p.swb), p.idesc, kb != 0,
+                                      ksteps, &empty[st]);
                 }
                 if (!ok) { atomicExch(p.err, 2); *abort_flag = 1; break; }
                 umma_commit(&tfull[buf]);
