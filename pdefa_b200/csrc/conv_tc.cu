@@ -35,6 +35,8 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int kMaxBuf = 4;                        // TMEM accumulator buffers at most
+constexpr int kMaxHalo = 4;                       // window slots (a_mode 2)
+constexpr uint32_t kBarrierBytes = 512;           // mbarriers, TMEM slot, abort flag
 // Epilogue warps per CTA: EPI = 4 (one group, one warp per TMEM lane quarter) or 8
 // (two groups that split the columns). Threads: producer warp, MMA warp, epilogue.
 template <int EPI> constexpr int conv_threads() { return 64 + 32 * EPI; }
@@ -74,6 +76,16 @@ struct TcParams {
     const float* bias; int act; float slope; int cout;
     int64_t m_tiles; int n_tiles;
     FastDiv div_ntiles, div_hw, div_wo;   // tile -> (m_tile, n_tile), pixel -> (image, row, col)
+    // a_mode 2 (halo): stride-1 convs read one zero-padded input window per tile and
+    // 64/32/16-channel chunk; tap (r, s) is the window shifted by r*Wp + s rows.
+    int Wp, NR, hstages;                  // padded row width, window rows, window slots
+    uint32_t Q;                           // output positions per image (Ho * Wp)
+    uint32_t halo_bytes, halo_tx;         // window slot stride, bytes one window load brings
+    // b_res: the whole weight matrix (every k-block's bn x ch tile, in k-block order)
+    // sits in shared memory for the CTA's lifetime, loaded once (n_tiles == 1).
+    int b_res;
+    uint32_t bres_bytes, btile_bytes;
+    FastDiv div_tpi, div_wp;              // tile -> (image, tile in image), position -> (row, col)
     int tma_store;                        // 1: stage output chunks in shared memory, TMA-store them
     uint32_t staging_bytes;               // bn * 128 * out element size (0 without tma_store)
     int* err;
@@ -99,6 +111,14 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
         : "memory");
 }
 
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
+                                            int c2, int c3) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], [%2];"
+        ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+        : "memory");
+}
+
 __device__ __forceinline__ void tma_load_im2col_4d(uint32_t dst, const CUtensorMap* map, uint64_t* bar,
                                                    int c, int w, int h, int n, uint16_t ow, uint16_t oh) {
     asm volatile(
@@ -113,15 +133,16 @@ __device__ __forceinline__ void tma_load_im2col_4d(uint32_t dst, const CUtensorM
 // B rows, then a commit of all of them to `bar`, in one branch-free instruction
 // sequence (the extra MMAs are predicated off). A branch between a tcgen05.mma and the
 // next one costs the issuing thread a few hundred cycles, so the k-slices are never
-// issued from a loop. acc = 0 starts a fresh accumulator with the first slice.
+// issued from a loop. acc = 0 starts a fresh accumulator with the first slice;
+// bar == nullptr issues no commit.
 template <int KIND>
 __device__ __forceinline__ void umma_kblock(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc,
                                             int ksteps, uint64_t* bar) {
     // a 32-byte step is +2 in the descriptor's 16-byte start-address field
     if (KIND == 0) {
         asm volatile(
-            "{\n\t.reg .pred pa, pt, p1, p2;\n\t.reg .b64 a1, b1, a2, b2, a3, b3;\n\t"
-            "setp.ne.b32 pa, %4, 0;\n\tsetp.eq.u32 pt, 0, 0;\n\t"
+            "{\n\t.reg .pred pa, pt, p1, p2, pc;\n\t.reg .b64 a1, b1, a2, b2, a3, b3;\n\t"
+            "setp.ne.b32 pa, %4, 0;\n\tsetp.eq.u32 pt, 0, 0;\n\tsetp.ne.b32 pc, %7, 0;\n\t"
             "setp.gt.s32 p1, %5, 1;\n\tsetp.gt.s32 p2, %5, 2;\n\t"
             "add.s64 a1, %1, 2;\n\tadd.s64 b1, %2, 2;\n\tadd.s64 a2, %1, 4;\n\tadd.s64 b2, %2, 4;\n\t"
             "add.s64 a3, %1, 6;\n\tadd.s64 b3, %2, 6;\n\t"
@@ -129,13 +150,14 @@ __device__ __forceinline__ void umma_kblock(uint32_t tmem_d, uint64_t da, uint64
             "@p1 tcgen05.mma.cta_group::1.kind::f16 [%0], a1, b1, %3, pt;\n\t"
             "@p2 tcgen05.mma.cta_group::1.kind::f16 [%0], a2, b2, %3, pt;\n\t"
             "@p2 tcgen05.mma.cta_group::1.kind::f16 [%0], a3, b3, %3, pt;\n\t"
-            "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%6];\n\t}"
-            ::"r"(tmem_d), "l"(da), "l"(db), "r"(idesc), "r"(acc), "r"(ksteps), "r"(smem_u32(bar))
+            "@pc tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%6];\n\t}"
+            ::"r"(tmem_d), "l"(da), "l"(db), "r"(idesc), "r"(acc), "r"(ksteps), "r"(bar ? smem_u32(bar) : 0u),
+              "r"(bar ? 1u : 0u)
             : "memory");
     } else {
         asm volatile(
-            "{\n\t.reg .pred pa, pt, p1, p2;\n\t.reg .b64 a1, b1, a2, b2, a3, b3;\n\t"
-            "setp.ne.b32 pa, %4, 0;\n\tsetp.eq.u32 pt, 0, 0;\n\t"
+            "{\n\t.reg .pred pa, pt, p1, p2, pc;\n\t.reg .b64 a1, b1, a2, b2, a3, b3;\n\t"
+            "setp.ne.b32 pa, %4, 0;\n\tsetp.eq.u32 pt, 0, 0;\n\tsetp.ne.b32 pc, %7, 0;\n\t"
             "setp.gt.s32 p1, %5, 1;\n\tsetp.gt.s32 p2, %5, 2;\n\t"
             "add.s64 a1, %1, 2;\n\tadd.s64 b1, %2, 2;\n\tadd.s64 a2, %1, 4;\n\tadd.s64 b2, %2, 4;\n\t"
             "add.s64 a3, %1, 6;\n\tadd.s64 b3, %2, 6;\n\t"
@@ -143,8 +165,9 @@ __device__ __forceinline__ void umma_kblock(uint32_t tmem_d, uint64_t da, uint64
             "@p1 tcgen05.mma.cta_group::1.kind::tf32 [%0], a1, b1, %3, pt;\n\t"
             "@p2 tcgen05.mma.cta_group::1.kind::tf32 [%0], a2, b2, %3, pt;\n\t"
             "@p2 tcgen05.mma.cta_group::1.kind::tf32 [%0], a3, b3, %3, pt;\n\t"
-            "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%6];\n\t}"
-            ::"r"(tmem_d), "l"(da), "l"(db), "r"(idesc), "r"(acc), "r"(ksteps), "r"(smem_u32(bar))
+            "@pc tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%6];\n\t}"
+            ::"r"(tmem_d), "l"(da), "l"(db), "r"(idesc), "r"(acc), "r"(ksteps), "r"(bar ? smem_u32(bar) : 0u),
+              "r"(bar ? 1u : 0u)
             : "memory");
     }
 }
@@ -325,12 +348,25 @@ __device__ void epilogue_loop(const TcParams& p, const CUtensorMap* tmOut, uint8
         const uint32_t use = (uint32_t)(i / p.nbuf);     // how often this buffer was filled before
         const uint32_t mt = fdiv((uint32_t)t, p.div_ntiles);
         const int n0 = (int)((uint32_t)t - mt * (uint32_t)p.n_tiles) * p.bn;
-        const uint32_t m = mt * (uint32_t)BM + (uint32_t)row;
-        const bool live = (int64_t)m < p.M;
+        uint32_t b, ho, wo;
+        bool live;
+        if (p.a_mode == 2) {
+            // row -> padded position P of image b; columns x >= Wo are padding
+            b = fdiv(mt, p.div_tpi);
+            const uint32_t P = (mt - b * p.div_tpi.d) * (uint32_t)BM + (uint32_t)row;
+            ho = fdiv(P, p.div_wp);
+            wo = P - ho * p.div_wp.d;
+            live = P < p.Q && (int)wo < p.Wo;
+        } else {
+            const uint32_t m = mt * (uint32_t)BM + (uint32_t)row;
+            live = (int64_t)m < p.M;
+            b = fdiv(m, p.div_hw);
+            const uint32_t r = m - b * p.div_hw.d;
+            ho = fdiv(r, p.div_wo);
+            wo = r - ho * p.div_wo.d;
+        }
         int64_t ob = 0, rb = 0;
         if (live) {
-            const uint32_t b = fdiv(m, p.div_hw), r = m - b * p.div_hw.d;
-            const uint32_t ho = fdiv(r, p.div_wo), wo = r - ho * p.div_wo.d;
             ob = (int64_t)b * p.out_img + (int64_t)ho * p.out_sh + (int64_t)wo * p.out_sw + n0;
             rb = (int64_t)b * p.res_img + (int64_t)ho * p.res_sh + (int64_t)wo * p.res_sw + n0;
         }
@@ -394,6 +430,92 @@ __device__ void epilogue_loop(const TcParams& p, const CUtensorMap* tmOut, uint8
     if (p.tma_store && leader) bulk_wait0();
 }
 
+struct MmaSmem {
+    uint32_t ring, halo, bres, a_bytes, b_bytes;
+    int S, HS;
+    uint64_t *full, *empty, *tfull, *tempty, *hfull, *hempty, *bres_full, *mma_done;
+    uint32_t tmem;
+};
+
+// MMA issuer (one thread). Every branch this thread takes while MMAs are in flight
+// costs it tens of cycles, so the operand mode is a template parameter and the tap
+// and chunk loops carry no per-k-block mode tests. WIN: a_mode 2 (windows; taps are
+// shifted windows); otherwise A comes from the ring (im2col or 2-D tiles). BRES:
+// weights resident in shared memory instead of streamed through the ring.
+template <int KIND, int WIN, bool BRES>
+__device__ __forceinline__ void mma_issuer(const TcParams& p, const MmaSmem& m, volatile int* abort_flag, int64_t total) {
+    const int ksteps = p.swb / 32;
+    const int taps = p.taps, chunks = p.cin_chunks, kw = p.kw;
+    const uint64_t bdesc0 = make_smem_desc(m.bres, p.swb);
+    const uint32_t bstep = (p.btile_bytes >> 4);          // descriptor units per resident k-block
+    int64_t it = 0, hit = 0, i = 0;
+    if (BRES && blockIdx.x < total && !mbar_wait_bounded(m.bres_full, 0)) {
+        atomicExch(p.err, 2);
+        *abort_flag = 1;
+    }
+    for (int64_t t = blockIdx.x; t < total && !*abort_flag; t += gridDim.x, ++i) {
+        const int buf = (int)(i % p.nbuf);
+        if (i >= p.nbuf && !mbar_wait_bounded(&m.tempty[buf], (uint32_t)(((i / p.nbuf) & 1) ^ 1))) {
+            atomicExch(p.err, 5);
+            *abort_flag = 1;
+            break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t d = m.tmem + (uint32_t)buf * p.bufcols;
+        bool ok = true;
+        if (WIN == 2) {
+            const uint32_t mt = fdiv((uint32_t)t, p.div_ntiles);
+            const uint32_t b = fdiv(mt, p.div_tpi);
+            const uint32_t P0 = (mt - b * p.div_tpi.d) * (uint32_t)BM;
+            const uint32_t off0 = P0 - fdiv(P0, p.div_wp) * p.div_wp.d;
+            for (int cc = 0; cc < chunks && ok; ++cc) {
+                const int hs = (int)(hit % m.HS);
+                if (!mbar_wait_bounded(&m.hfull[hs], (uint32_t)((hit / m.HS) & 1))) { ok = false; break; }
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint64_t adesc0 = make_smem_desc(m.halo + (uint32_t)hs * p.halo_bytes + off0 * (uint32_t)p.swb, p.swb);
+                for (int r = 0, tap = 0; r < p.taps / kw; ++r) {
+                    for (int s2 = 0; s2 < kw; ++s2, ++tap) {
+                        const uint64_t da = adesc0 + ((uint64_t)((uint32_t)(r * p.Wp + s2) * (uint32_t)p.swb) >> 4);
+                        uint64_t db;
+                        uint64_t* release = nullptr;
+                        if (BRES) {
+                            db = bdesc0 + (uint64_t)(cc * taps + tap) * bstep;
+                        } else {
+                            const int st = (int)(it % m.S);
+                            if (!mbar_wait_bounded(&m.full[st], (uint32_t)((it / m.S) & 1))) { ok = false; break; }
+                            ++it;
+                            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                            db = make_smem_desc(m.ring + (uint32_t)m.S * m.a_bytes + (uint32_t)st * m.b_bytes, p.swb);
+                            release = &m.empty[st];
+                        }
+                        umma_kblock<KIND>(d, da, db, p.idesc, (cc | tap) != 0, ksteps, release);
+                    }
+                    if (!ok) break;
+                }
+                if (!ok) break;
+                umma_commit(&m.hempty[hs]);
+                ++hit;
+            }
+        } else {
+            for (int tap = 0; tap < taps && ok; ++tap) {
+                for (int cc = 0; cc < chunks; ++cc) {
+                    const int st = (int)(it % m.S);
+                    if (!mbar_wait_bounded(&m.full[st], (uint32_t)((it / m.S) & 1))) { ok = false; break; }
+                    ++it;
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                    const uint64_t da = make_smem_desc(m.ring + (uint32_t)st * m.a_bytes, p.swb);
+                    const uint64_t db = BRES ? bdesc0 + (uint64_t)(tap * chunks + cc) * bstep
+                                             : make_smem_desc(m.ring + (uint32_t)m.S * m.a_bytes + (uint32_t)st * m.b_bytes, p.swb);
+                    umma_kblock<KIND>(d, da, db, p.idesc, (tap | cc) != 0, ksteps, &m.empty[st]);
+                }
+            }
+        }
+        if (!ok) { atomicExch(p.err, 2); *abort_flag = 1; break; }
+        umma_commit(&m.tfull[buf]);
+    }
+    umma_commit(m.mma_done);
+}
+
 // Persistent, warp-specialized kernel. 64 + 32*EPI threads:
 //   warp 0  (lane 0): TMA producer, streams (tile, k-block) loads through the ring
 //                     without stopping at tile boundaries;
@@ -412,14 +534,22 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     uint8_t* const smem = smem_raw + (base - raw);
     const int S = p.stages;
     const uint32_t a_bytes = p.stage_a_bytes, b_bytes = p.stage_b_bytes;
-    uint8_t* const staging = smem;                          // output staging (tma_store), 1024-aligned
-    const uint32_t ring = base + p.staging_bytes;           // ring slots follow
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.staging_bytes + (size_t)S * (a_bytes + b_bytes));
+    // [output staging | window slots | resident weights | A slots | B slots | barriers],
+    // 1024-aligned parts
+    uint8_t* const staging = smem;
+    const int HS = p.hstages;
+    const uint32_t halo = base + p.staging_bytes;
+    const uint32_t bres = halo + (uint32_t)HS * p.halo_bytes;
+    const uint32_t ring = bres + p.bres_bytes;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + (ring - base) + (size_t)S * (a_bytes + b_bytes));
     uint64_t* empty = full + S;
     uint64_t* tfull = empty + S;          // [kMaxBuf] MMA -> epilogue
     uint64_t* tempty = tfull + kMaxBuf;   // [kMaxBuf] epilogue -> MMA
     uint64_t* mma_done = tempty + kMaxBuf;  // all issued MMAs finished (before TMEM is freed)
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+    uint64_t* hfull = mma_done + 1;       // [kMaxHalo] window landed
+    uint64_t* hempty = hfull + kMaxHalo;  // [kMaxHalo] window consumed
+    uint64_t* bres_full = hempty + kMaxHalo;  // resident weights landed
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bres_full + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -436,6 +566,8 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         for (int i = 0; i < S; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 1); }
         for (int i = 0; i < p.nbuf; ++i) { mbar_init(&tfull[i], 1); mbar_init(&tempty[i], EPI); }
         mbar_init(mma_done, 1);
+        mbar_init(bres_full, 1);
+        for (int i = 0; i < HS; ++i) { mbar_init(&hfull[i], 1); mbar_init(&hempty[i], 1); }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     }
@@ -452,7 +584,18 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     if (warp == 0) {
         if (lane == 0) {
             // ---------------- TMA producer ----------------
-            int64_t it = 0;   // global k-block counter across tiles
+            int64_t it = 0;   // global ring counter across tiles
+            int64_t hit = 0;  // global window counter (a_mode 2)
+            const bool ring_used = S > 0;     // no ring: windows + resident weights only
+            if (p.b_res && blockIdx.x < total) {
+                mbar_expect_tx(bres_full, p.bres_bytes);
+                for (int kb = 0; kb < nk; ++kb) {
+                    int tap, cc;
+                    if (p.a_mode == 2) { cc = kb / p.taps; tap = kb - cc * p.taps; }
+                    else { tap = kb / p.cin_chunks; cc = kb - tap * p.cin_chunks; }
+                    tma_load_2d(bres + (uint32_t)kb * p.btile_bytes, &tmB, bres_full, tap * p.cin + cc * p.ch, 0);
+                }
+            }
             for (int64_t t = blockIdx.x; t < total && !*abort_flag; t += gridDim.x) {
                 const uint32_t mt = fdiv((uint32_t)t, p.div_ntiles);
                 const int n0 = (int)((uint32_t)t - mt * (uint32_t)p.n_tiles) * p.bn;
@@ -463,62 +606,73 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     const uint32_t r = m0 - b * p.div_hw.d;
                     ho = (int)fdiv(r, p.div_wo);
                     wo = (int)(r - (uint32_t)ho * p.div_wo.d);
+                } else if (p.a_mode == 2) {
+                    b = fdiv(mt, p.div_tpi);
+                    const uint32_t P0 = (mt - b * p.div_tpi.d) * (uint32_t)BM;
+                    ho = (int)fdiv(P0, p.div_wp);     // first window row (output row of P0)
                 }
-                for (int kb = 0; kb < nk; ++kb, ++it) {
+                bool stop = false;
+                for (int kb = 0; kb < nk && !stop; ++kb) {
+                    int tap, cc;
+                    if (p.a_mode == 2) {
+                        cc = kb / p.taps; tap = kb - cc * p.taps;
+                        if (tap == 0) {
+                            const int hs = (int)(hit % HS);
+                            if (hit >= HS && !mbar_wait_bounded(&hempty[hs], (uint32_t)(((hit / HS) & 1) ^ 1))) {
+                                atomicExch(p.err, 7);
+                                *abort_flag = 1;
+                                stop = true;
+                                break;
+                            }
+                            mbar_expect_tx(&hfull[hs], p.halo_tx);
+                            tma_load_4d(halo + (uint32_t)hs * p.halo_bytes, &tmA, &hfull[hs], cc * p.ch, -p.pw,
+                                        ho - p.ph, (int)b);
+                            ++hit;
+                        }
+                    } else {
+                        tap = kb / p.cin_chunks; cc = kb - tap * p.cin_chunks;
+                    }
+                    if (!ring_used) continue;
                     const int st = (int)(it % S);
                     if (it >= S && !mbar_wait_bounded(&empty[st], (uint32_t)(((it / S) & 1) ^ 1))) {
                         atomicExch(p.err, 1);
                         *abort_flag = 1;
                         break;
                     }
-                    const int tap = kb / p.cin_chunks, cc = kb - tap * p.cin_chunks;
                     const uint32_t sa = ring + (uint32_t)st * a_bytes;
                     const uint32_t sb = ring + (uint32_t)S * a_bytes + (uint32_t)st * b_bytes;
+                    ++it;
                     mbar_expect_tx(&full[st], a_bytes + b_bytes);
                     if (p.a_mode == 0) {
                         const int r = tap / p.kw, s = tap - r * p.kw;
                         tma_load_im2col_4d(sa, &tmA, &full[st], cc * p.ch, wo * p.sw - p.pw, ho * p.sh - p.ph,
                                            (int)b, (uint16_t)(s * p.dw), (uint16_t)(r * p.dh));
-                    } else {
+                    } else if (p.a_mode == 1) {
                         tma_load_2d(sa, &tmA, &full[st], cc * p.ch, (int)m0);
                     }
-                    tma_load_2d(sb, &tmB, &full[st], tap * p.cin + cc * p.ch, n0);
+                    if (!p.b_res) tma_load_2d(sb, &tmB, &full[st], tap * p.cin + cc * p.ch, n0);
                 }
             }
             // Drain: the last use of every slot must have landed before the CTA exits.
             for (int64_t k = it > S ? it - S : 0; k < it; ++k)
                 if (!mbar_wait_bounded(&full[k % S], (uint32_t)((k / S) & 1))) atomicExch(p.err, 4);
+            if (p.b_res && blockIdx.x < total && !mbar_wait_bounded(bres_full, 0)) atomicExch(p.err, 4);
+            for (int64_t k = hit > HS ? hit - HS : 0; k < hit; ++k)
+                if (!mbar_wait_bounded(&hfull[k % HS], (uint32_t)((k / HS) & 1))) atomicExch(p.err, 4);
         }
         __syncwarp();
     } else if (warp == 1) {
         if (lane == 0) {
             // ---------------- MMA issuer ----------------
-            const int ksteps = p.swb / 32;
-            int64_t it = 0;
-            int64_t i = 0;    // local tile counter
-            for (int64_t t = blockIdx.x; t < total && !*abort_flag; t += gridDim.x, ++i) {
-                const int buf = (int)(i % p.nbuf);
-                if (i >= p.nbuf && !mbar_wait_bounded(&tempty[buf], (uint32_t)(((i / p.nbuf) & 1) ^ 1))) {
-                    atomicExch(p.err, 5);
-                    *abort_flag = 1;
-                    break;
-                }
-                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                const uint32_t d = tmem + (uint32_t)buf * p.bufcols;
-                bool ok = true;
-                for (int kb = 0; kb < nk; ++kb, ++it) {
-                    const int st = (int)(it % S);
-                    if (!mbar_wait_bounded(&full[st], (uint32_t)((it / S) & 1))) { ok = false; break; }
-                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                    const uint32_t sa = ring + (uint32_t)st * a_bytes;
-                    const uint32_t sb = ring + (uint32_t)S * a_bytes + (uint32_t)st * b_bytes;
-                    umma_kblock<KIND>(d, make_smem_desc(sa, p.swb), make_smem_desc(sb, p.swb), p.idesc, kb != 0,
-                                      ksteps, &empty[st]);
-                }
-                if (!ok) { atomicExch(p.err, 2); *abort_flag = 1; break; }
-                umma_commit(&tfull[buf]);
+            MmaSmem m{ring, halo, bres, a_bytes, b_bytes, S, HS, full, empty, tfull, tempty, hfull, hempty, bres_full,
+                      mma_done, tmem};
+            if (p.a_mode == 2) {
+                if (p.b_res) mma_issuer<KIND, 2, true>(p, m, abort_flag, total);
+                else mma_issuer<KIND, 2, false>(p, m, abort_flag, total);
+            } else {
+                if (p.b_res) mma_issuer<KIND, 0, true>(p, m, abort_flag, total);
+                else mma_issuer<KIND, 0, false>(p, m, abort_flag, total);
             }
-            umma_commit(mma_done);
         }
         __syncwarp();
     } else {
@@ -612,7 +766,8 @@ bool conv_tc_supported(const ConvArgs& a, int op_dt, const char** why) {
     if (a.act < ACT_NONE || a.act > ACT_SILU_WINO) return no("activation not fusable");
     {
         // tile and pixel indices use 32-bit fast division (n < 2^31)
-        const int64_t M = a.batch * a.out.shape[1] * a.out.shape[2];
+        // (padded positions when a_mode 2 applies: Ho * (W + 2*pad_w) per image)
+        const int64_t M = a.batch * a.out.shape[1] * std::max<int64_t>(a.out.shape[2], a.in.shape[2] + 2 * a.pw) + BM;
         const int bn = pick_bn(a.cout);
         if (M + BM >= (int64_t(1) << 31) || ((M + BM - 1) / BM) * (a.cout / bn) >= (int64_t(1) << 31))
             return no("more than 2^31 output pixels");
@@ -644,8 +799,6 @@ void launch_conv_tc(const ConvArgs& a, int op_dt, int* err, cudaStream_t s) {
     if (!conv_tc_supported(a, op_dt, &why)) fail(ENGINE_ERR_INVALID_ARG, std::string("conv_tc: ") + why);
     load_driver_fns();
     const int esz = op_dt == BF16 ? 2 : 4;
-    const int ch = pick_chunk(a.cin, esz);
-    const int swb = ch * esz;
     const int bn = pick_bn(a.cout);
     const int Ho = (int)a.out.shape[1], Wo = (int)a.out.shape[2];
     const int64_t M = a.batch * Ho * Wo;
@@ -655,34 +808,92 @@ void launch_conv_tc(const ConvArgs& a, int op_dt, int* err, cudaStream_t s) {
     TcParams p{};
     p.M = M; p.Ho = Ho; p.Wo = Wo;
     p.sh = a.sh; p.sw = a.sw; p.ph = a.ph; p.pw = a.pw; p.dh = a.dh; p.dw = a.dw; p.kw = a.kw;
-    p.taps = a.kh * a.kw; p.ch = ch; p.cin = a.cin; p.cin_chunks = a.cin / ch;
-    p.bn = bn; p.swb = swb;
+    p.taps = a.kh * a.kw; p.cin = a.cin;
+    p.bn = bn;
     p.bufcols = 32;
     while (p.bufcols < (uint32_t)bn) p.bufcols <<= 1;
     p.nbuf = 2;
     p.tmem_cols = 2 * (int)p.bufcols;                   // two accumulators (four when TMEM allows, below)
-    p.stage_a_bytes = BM * swb;
-    p.stage_b_bytes = bn * swb;
-    const uint32_t stage = p.stage_a_bytes + p.stage_b_bytes;
-    // Two shapes of the kernel. 1x1 convs (one tap: each operand byte is loaded
-    // once) are bound by how fast tiles drain, so they get 8 epilogue warps and TMA
-    // stores through a shared-memory staging buffer (two CTAs per SM). Convs with
-    // several taps re-read the input per tap and are bound by the operand stream, so
-    // they keep 4 epilogue warps with direct stores and spend shared memory on more
-    // CTAs and deeper rings (up to four CTAs per SM).
-    const int epi = p.taps == 1 ? 8 : 4;
-    // Output staging for TMA stores: the view must have one pixel stride (a 2-D
-    // tensor map over [pixels, channels]).
+    // ---- operand plan --------------------------------------------------------
+    // The operand stream is bound by how many rows (one pixel or weight row of one
+    // channel chunk) the SM's TMA unit moves per output tile, so the plan minimises
+    // rows per tile and then maximises CTAs (pipelines) per SM. Candidates:
+    //   a_mode 1: 1x1 stride-1 conv on a pixel-dense input, plain 2-D tiles of A;
+    //   a_mode 0: TMA im2col, one 128-pixel load per tap and channel chunk;
+    //   a_mode 2: stride-1, dilation-1 convs whose padded rows fit one TMA box: one
+    //             zero-padded window of NR padded rows per tile and channel chunk, each
+    //             tap read as the window shifted by r*Wp + s rows;
+    // each with the weights streamed per k-block through the ring, or (b_res, one
+    // N tile) resident in shared memory, loaded once per CTA. 1x1 convs (bound by
+    // how fast tiles drain) never give up CTAs for resident weights and use 8
+    // epilogue warps with TMA-store staging; multi-tap convs use 8 epilogue warps
+    // when at most two CTAs fit, else 4.
+    const bool one = a.kh == 1 && a.kw == 1 && a.sh == 1 && a.sw == 1 && a.ph == 0 && a.pw == 0;
+    const int Wp = (int)a.in.shape[2] + 2 * a.pw;
+    const int NR = (a.kh * Wp + a.kw + BM - 2 + Wp - 1) / Wp;   // window rows covering row offsets + 128
+    const int ch = pick_chunk(a.cin, esz);
+    const int swb = ch * esz;
+    const int chunks = a.cin / ch;
+    const int nk = p.taps * chunks;
     const int oes = a.out.dt == BF16 ? 2 : 4;
     const uint32_t staging = (uint32_t)bn * BM * oes;
-    p.tma_store = epi == 8 && pixel_dense(a.out) && staging <= 64u * 1024u;
-    p.staging_bytes = p.tma_store ? staging : 0u;
-    const uint32_t fixed = 1024 + 512 + 1024 + p.staging_bytes;   // alignment, barriers, reserve, staging
-    auto stages_for = [&](int c) { return (int)(((228u * 1024u) / (uint32_t)c - fixed) / stage); };
-    int ctas = std::min(epi == 8 ? 2 : 4, 512 / p.tmem_cols);     // register-file limit
-    while (ctas > 1 && stages_for(ctas) < 4) --ctas;
-    int stages = std::min(12, stages_for(ctas));
-    if (stages < 2) fail(ENGINE_ERR_INVALID_ARG, "conv_tc: tile does not fit in shared memory");
+    const bool tma_store = p.taps == 1 && pixel_dense(a.out) && staging <= 64u * 1024u;
+    const uint32_t fixed = 1024 + kBarrierBytes + 1024 + (tma_store ? staging : 0u);   // alignment, barriers, reserve
+    const int max_ctas = std::min(p.taps == 1 ? 2 : 4, 512 / p.tmem_cols);   // register file, TMEM
+    const uint32_t btile = (uint32_t)bn * swb;
+    const uint32_t bres_all = (uint32_t)nk * btile;
+    const uint32_t win_tx = (uint32_t)NR * (uint32_t)Wp * (uint32_t)swb;
+    const uint32_t win_slot = (win_tx + 1023u) & ~1023u;
+    const bool window_ok = !one && a.sh == 1 && a.sw == 1 && a.dh == 1 && a.dw == 1 && Wp <= 256 && NR <= 256 &&
+                           Wo == Wp - a.kw + 1;
+    struct Cand { int mode, bres, ctas, stages; int64_t rows; };
+    Cand best{-1, 0, 0, 0, 0};
+    auto consider = [&](int mode, int bres) {
+        if (bres && (bn != a.cout || bres_all > 200u * 1024u)) return;
+        const uint32_t a_st = mode == 2 ? 0u : (uint32_t)BM * swb;
+        const uint32_t b_st = bres ? 0u : btile;
+        const uint32_t st = a_st + b_st;
+        const uint32_t fixed_c = fixed + (bres ? bres_all : 0u) + (mode == 2 ? 2u * win_slot : 0u);
+        // ring slots: at least 4 (3 for windows) while CTAs can be given up, 2 at one CTA
+        const int min_st = st == 0 ? 0 : (mode == 2 ? 3 : 4);
+        int c = max_ctas;
+        auto room = [&](int cc) { return (int64_t)(228u * 1024u) / cc - (int64_t)fixed_c; };
+        while (c > 1 && room(c) < (int64_t)min_st * st) --c;
+        if (room(c) < 0 || room(c) < (int64_t)(c == 1 ? std::min(min_st, 2) : min_st) * st) return;
+        const int stg = st == 0 ? 0 : (int)std::min<int64_t>(12, room(c) / st);
+        const int64_t rows = (mode == 2 ? (int64_t)chunks * NR * Wp : (int64_t)nk * BM) + (bres ? 0 : (int64_t)nk * bn);
+        if (p.taps == 1 && best.mode >= 0 && c < best.ctas) return;   // 1x1: never trade CTAs for rows
+        const bool better = best.mode < 0 || rows < best.rows || (rows == best.rows && c > best.ctas);
+        if (better) best = Cand{mode, bres, c, stg, rows};
+    };
+    if (one && pixel_dense(a.in)) {
+        consider(1, 0);
+        consider(1, 1);
+    } else {
+        consider(0, 0);
+        consider(0, 1);
+        if (window_ok) { consider(2, 0); consider(2, 1); }
+    }
+    if (best.mode < 0) fail(ENGINE_ERR_INVALID_ARG, "conv_tc: tile does not fit in shared memory");
+    p.a_mode = best.mode;
+    p.b_res = best.bres;
+    int ctas = best.ctas;
+    const int stages = best.stages;
+    const int epi = (p.taps == 1 || ctas <= 2) ? 8 : 4;
+    p.tma_store = tma_store;
+    p.staging_bytes = tma_store ? staging : 0u;
+    p.ch = ch; p.swb = swb; p.cin_chunks = chunks;
+    p.stage_a_bytes = p.a_mode == 2 ? 0u : (uint32_t)BM * swb;
+    p.stage_b_bytes = p.b_res ? 0u : btile;
+    const uint32_t stage2 = p.stage_a_bytes + p.stage_b_bytes;
+    p.btile_bytes = btile;
+    p.bres_bytes = p.b_res ? bres_all : 0u;
+    p.hstages = p.a_mode == 2 ? 2 : 0;
+    const uint32_t halo_tx = p.a_mode == 2 ? win_tx : 0u;
+    const uint32_t halo_slot = p.a_mode == 2 ? win_slot : 0u;
+    p.Wp = Wp; p.NR = NR;
+    p.halo_tx = halo_tx;
+    p.halo_bytes = halo_slot;
     p.stages = stages;
     // With spare TMEM the MMA warp may run up to four tiles ahead of the epilogue
     // (MMA completion latency is hidden behind more than one epilogue).
@@ -711,9 +922,7 @@ void launch_conv_tc(const ConvArgs& a, int op_dt, int* err, cudaStream_t s) {
                              CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
         if (r != CUDA_SUCCESS) fail(ENGINE_ERR_RUNTIME, "cuTensorMapEncodeTiled(out) failed: " + std::to_string((int)r));
     }
-    const bool one = a.kh == 1 && a.kw == 1 && a.sh == 1 && a.sw == 1 && a.ph == 0 && a.pw == 0;
-    if (one && pixel_dense(a.in)) {
-        p.a_mode = 1;
+    if (p.a_mode == 1) {
         cuuint64_t dims[2] = {(cuuint64_t)a.cin, (cuuint64_t)(a.batch * a.in.shape[1] * a.in.shape[2])};
         cuuint64_t strides[1] = {(cuuint64_t)(a.in.stride[2] * esz)};
         cuuint32_t box[2] = {(cuuint32_t)ch, (cuuint32_t)BM};
@@ -722,8 +931,19 @@ void launch_conv_tc(const ConvArgs& a, int op_dt, int* err, cudaStream_t s) {
                              CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle_of(swb), CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
         if (r != CUDA_SUCCESS) fail(ENGINE_ERR_RUNTIME, "cuTensorMapEncodeTiled(A) failed: " + std::to_string((int)r));
+    } else if (p.a_mode == 2) {
+        // [N, H, W, C] input; box = one channel chunk of NR padded rows of Wp pixels,
+        // out-of-image pixels read as zeros (the padding)
+        cuuint64_t dims[4] = {(cuuint64_t)a.cin, (cuuint64_t)a.in.shape[2], (cuuint64_t)a.in.shape[1], (cuuint64_t)a.batch};
+        cuuint64_t strides[3] = {(cuuint64_t)(a.in.stride[2] * esz), (cuuint64_t)(a.in.stride[1] * esz),
+                                 (cuuint64_t)(a.in.img_stride * esz)};
+        cuuint32_t box[4] = {(cuuint32_t)ch, (cuuint32_t)Wp, (cuuint32_t)NR, 1};
+        cuuint32_t es[4] = {1, 1, 1, 1};
+        CUresult r = g_tiled(&tmA, tdt, 4, const_cast<void*>(a.in.ptr), dims, strides, box, es,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle_of(swb), CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) fail(ENGINE_ERR_RUNTIME, "cuTensorMapEncodeTiled(window) failed: " + std::to_string((int)r));
     } else {
-        p.a_mode = 0;
         cuuint64_t dims[4] = {(cuuint64_t)a.cin, (cuuint64_t)a.in.shape[2], (cuuint64_t)a.in.shape[1], (cuuint64_t)a.batch};
         cuuint64_t strides[3] = {(cuuint64_t)(a.in.stride[2] * esz), (cuuint64_t)(a.in.stride[1] * esz),
                                  (cuuint64_t)(a.in.img_stride * esz)};
@@ -746,12 +966,22 @@ void launch_conv_tc(const ConvArgs& a, int op_dt, int* err, cudaStream_t s) {
                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
         if (r != CUDA_SUCCESS) fail(ENGINE_ERR_RUNTIME, "cuTensorMapEncodeTiled(W) failed: " + std::to_string((int)r));
     }
-    p.m_tiles = (M + BM - 1) / BM;
     p.n_tiles = a.cout / bn;
+    if (p.a_mode == 2) {
+        // tiles never straddle images: positions P = y*Wp + x of one image, Ho*Wp of them
+        p.Q = (uint32_t)Ho * (uint32_t)Wp;
+        const uint32_t tpi = (p.Q + BM - 1) / BM;
+        p.div_tpi = make_fastdiv(tpi);
+        p.div_wp = make_fastdiv((uint32_t)Wp);
+        p.m_tiles = (int64_t)tpi * a.batch;
+    } else {
+        p.m_tiles = (M + BM - 1) / BM;
+    }
     p.div_ntiles = make_fastdiv((uint32_t)p.n_tiles);
     p.div_hw = make_fastdiv((uint32_t)((int64_t)Ho * Wo));
     p.div_wo = make_fastdiv((uint32_t)Wo);
-    const size_t smem = (size_t)stages * stage + p.staging_bytes + 1024 + 512;
+    const size_t smem = (size_t)stages * stage2 + p.staging_bytes + (size_t)p.hstages * p.halo_bytes + p.bres_bytes +
+                        1024 + kBarrierBytes;
     int dev = 0;
     PB_CUDA(cudaGetDevice(&dev));
     static int sm_count[64] = {};
