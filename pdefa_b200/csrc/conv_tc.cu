@@ -815,19 +815,22 @@ void launch_conv_tc(const ConvArgs& a, int op_dt, int* err, cudaStream_t s) {
     p.nbuf = 2;
     p.tmem_cols = 2 * (int)p.bufcols;                   // two accumulators (four when TMEM allows, below)
     // ---- operand plan --------------------------------------------------------
-    // The operand stream is bound by how many rows (one pixel or weight row of one
-    // channel chunk) the SM's TMA unit moves per output tile, so the plan minimises
-    // rows per tile and then maximises CTAs (pipelines) per SM. Candidates:
+    // Operand modes:
     //   a_mode 1: 1x1 stride-1 conv on a pixel-dense input, plain 2-D tiles of A;
     //   a_mode 0: TMA im2col, one 128-pixel load per tap and channel chunk;
     //   a_mode 2: stride-1, dilation-1 convs whose padded rows fit one TMA box: one
     //             zero-padded window of NR padded rows per tile and channel chunk, each
     //             tap read as the window shifted by r*Wp + s rows;
-    // each with the weights streamed per k-block through the ring, or (b_res, one
-    // N tile) resident in shared memory, loaded once per CTA. 1x1 convs (bound by
-    // how fast tiles drain) never give up CTAs for resident weights and use 8
-    // epilogue warps with TMA-store staging; multi-tap convs use 8 epilogue warps
-    // when at most two CTAs fit, else 4.
+    // weights streamed per k-block through the ring, or (b_res, one N tile) resident
+    // in shared memory, loaded once per CTA. The choices follow per-layer sweeps of
+    // every combination on B200 (YOLOv8 layer shapes):
+    //   * CTAs per SM matter most: as many as TMEM allows (two accumulators of
+    //     bufcols columns each), four at most with 4 epilogue warps, two with 8;
+    //   * windows win where im2col moves narrow rows (channel chunks under 128
+    //     bytes: Cin = 16, 32, 80, ...), im2col elsewhere;
+    //   * resident weights whenever they fit without costing a CTA, and always for
+    //     windows (streamed weights would dominate the window's rows).
+    // 1x1 convs with 8 epilogue warps stage their output for TMA stores.
     const bool one = a.kh == 1 && a.kw == 1 && a.sh == 1 && a.sw == 1 && a.ph == 0 && a.pw == 0;
     const int Wp = (int)a.in.shape[2] + 2 * a.pw;
     const int NR = (a.kh * Wp + a.kw + BM - 2 + Wp - 1) / Wp;   // window rows covering row offsets + 128
@@ -835,51 +838,63 @@ void launch_conv_tc(const ConvArgs& a, int op_dt, int* err, cudaStream_t s) {
     const int swb = ch * esz;
     const int chunks = a.cin / ch;
     const int nk = p.taps * chunks;
+    const int tmem_ctas = 512 / p.tmem_cols;                     // two accumulators per CTA
+    // 1x1 convs drain a tile per handful of MMAs: 8 epilogue warps with TMA stores
+    // from 64 output channels up; multi-tap convs switch at Cout > 64 (TMEM then
+    // allows two CTAs at most).
+    const int epi = (one ? bn >= 64 : tmem_ctas <= 2) ? 8 : 4;
+    const int max_ctas = std::min(epi == 8 ? 2 : 4, tmem_ctas);  // register file, TMEM
     const int oes = a.out.dt == BF16 ? 2 : 4;
     const uint32_t staging = (uint32_t)bn * BM * oes;
-    const bool tma_store = p.taps == 1 && pixel_dense(a.out) && staging <= 64u * 1024u;
+    const bool tma_store = p.taps == 1 && epi == 8 && pixel_dense(a.out) && staging <= 64u * 1024u;
     const uint32_t fixed = 1024 + kBarrierBytes + 1024 + (tma_store ? staging : 0u);   // alignment, barriers, reserve
-    const int max_ctas = std::min(p.taps == 1 ? 2 : 4, 512 / p.tmem_cols);   // register file, TMEM
     const uint32_t btile = (uint32_t)bn * swb;
     const uint32_t bres_all = (uint32_t)nk * btile;
     const uint32_t win_tx = (uint32_t)NR * (uint32_t)Wp * (uint32_t)swb;
     const uint32_t win_slot = (win_tx + 1023u) & ~1023u;
     const bool window_ok = !one && a.sh == 1 && a.sw == 1 && a.dh == 1 && a.dw == 1 && Wp <= 256 && NR <= 256 &&
                            Wo == Wp - a.kw + 1;
-    struct Cand { int mode, bres, ctas, stages; int64_t rows; };
-    Cand best{-1, 0, 0, 0, 0};
-    auto consider = [&](int mode, int bres) {
-        if (bres && (bn != a.cout || bres_all > 200u * 1024u)) return;
+    struct Cand { int mode, bres, ctas, stages; };
+    // most CTAs (<= max_ctas) a configuration fits, with its ring depth; ctas 0 = none
+    auto fit = [&](int mode, int bres) {
+        Cand c{mode, bres, 0, 0};
+        if (bres && (bn != a.cout || bres_all > 200u * 1024u)) return c;
         const uint32_t a_st = mode == 2 ? 0u : (uint32_t)BM * swb;
         const uint32_t b_st = bres ? 0u : btile;
         const uint32_t st = a_st + b_st;
         const uint32_t fixed_c = fixed + (bres ? bres_all : 0u) + (mode == 2 ? 2u * win_slot : 0u);
-        // ring slots: at least 4 (3 for windows) while CTAs can be given up, 2 at one CTA
-        const int min_st = st == 0 ? 0 : (mode == 2 ? 3 : 4);
-        int c = max_ctas;
-        auto room = [&](int cc) { return (int64_t)(228u * 1024u) / cc - (int64_t)fixed_c; };
-        while (c > 1 && room(c) < (int64_t)min_st * st) --c;
-        if (room(c) < 0 || room(c) < (int64_t)(c == 1 ? std::min(min_st, 2) : min_st) * st) return;
-        const int stg = st == 0 ? 0 : (int)std::min<int64_t>(12, room(c) / st);
-        const int64_t rows = (mode == 2 ? (int64_t)chunks * NR * Wp : (int64_t)nk * BM) + (bres ? 0 : (int64_t)nk * bn);
-        if (p.taps == 1 && best.mode >= 0 && c < best.ctas) return;   // 1x1: never trade CTAs for rows
-        const bool better = best.mode < 0 || rows < best.rows || (rows == best.rows && c > best.ctas);
-        if (better) best = Cand{mode, bres, c, stg, rows};
+        const int min_st = st == 0 ? 0 : (mode == 2 ? 3 : 4);     // 2 suffice at one CTA
+        auto room = [&](int n) { return (int64_t)(228u * 1024u) / n - (int64_t)fixed_c; };
+        for (int n = max_ctas; n >= 1; --n) {
+            const int need = n == 1 ? std::min(min_st, 2) : min_st;
+            if (room(n) >= 0 && room(n) >= (int64_t)need * st) {
+                c.ctas = n;
+                c.stages = st == 0 ? 0 : (int)std::min<int64_t>(12, room(n) / st);
+                return c;
+            }
+        }
+        return c;
     };
+    Cand best{-1, 0, 0, 0};
     if (one && pixel_dense(a.in)) {
-        consider(1, 0);
-        consider(1, 1);
+        const Cand s0 = fit(1, 0), s1 = fit(1, 1);
+        best = s1.ctas > 0 && s1.ctas >= s0.ctas ? s1 : s0;
     } else {
-        consider(0, 0);
-        consider(0, 1);
-        if (window_ok) { consider(2, 0); consider(2, 1); }
+        if (window_ok && swb < 128) {
+            const Cand w1 = fit(2, 1), w0 = fit(2, 0);
+            if (w1.ctas > 0) best = w1;
+            else if (w0.ctas > 0) best = w0;
+        }
+        if (best.ctas == 0 || best.mode < 0) {
+            const Cand s0 = fit(0, 0), s1 = fit(0, 1);
+            best = s1.ctas > 0 && s1.ctas >= s0.ctas ? s1 : s0;
+        }
     }
-    if (best.mode < 0) fail(ENGINE_ERR_INVALID_ARG, "conv_tc: tile does not fit in shared memory");
+    if (best.mode < 0 || best.ctas == 0) fail(ENGINE_ERR_INVALID_ARG, "conv_tc: tile does not fit in shared memory");
     p.a_mode = best.mode;
     p.b_res = best.bres;
     int ctas = best.ctas;
     const int stages = best.stages;
-    const int epi = (p.taps == 1 || ctas <= 2) ? 8 : 4;
     p.tma_store = tma_store;
     p.staging_bytes = tma_store ? staging : 0u;
     p.ch = ch; p.swb = swb; p.cin_chunks = chunks;
