@@ -36,6 +36,20 @@ sys.path.insert(0, ROOT)
 METRIC = "YOLOv8n-640 images/sec at 1/2/4/8 B200; conv TFLOP/s vs tensor-core peak"
 
 
+def conv_tc_traffic_per_launch(batch: int):
+    """DRAM bytes (read + write) per conv_tc launch at `batch`, from the committed ncu
+    capture in profiles/ (bytes per image of one step's 62 launches, scaled by batch)."""
+    p = os.path.join(ROOT, "profiles", "conv_tc_dram_traffic_yolov8n640.md")
+    try:
+        with open(p) as f:
+            for line in f:
+                if line.startswith("traffic_bytes_per_image:"):
+                    return float(line.split(":")[1]) * batch / 62
+    except OSError:
+        pass
+    return None
+
+
 def load_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -269,7 +283,9 @@ def main():
     tc_flops = (flops_img - 2 * 3 * 16 * 9 * (args.imgsz // 2) ** 2) * B
     achieved = tc_flops / (tc_ms / 1e3) / 1e12 if tc_ms > 0 else None
     roofline = {"bound": "tensor", "achieved": achieved, "peak": peak_sus, "unit": "TFLOP/s",
-                "frac": (achieved / peak_sus) if achieved else None, "traffic": None,
+                "frac": (achieved / peak_sus) if achieved else None,
+                "traffic": conv_tc_traffic_per_launch(B) if args.imgsz == 640 else None,
+                "traffic_unit": "DRAM bytes per conv_tc launch (ncu, averaged over the 62 launches of a step)",
                 "kernel": "conv_tc_bf16 (62 launches/step)", "peak_source": f"{peak_src} bf16 sustained",
                 "conv_tflops_all_convs": flops_img * B / (conv_ms_all / 1e3) / 1e12 if conv_ms_all else None,
                 "ms_by_kernel_kind": {k: round(v, 4) for k, v in by_kind.items()},
