@@ -200,6 +200,7 @@ def main():
     import pdefa_b200 as pb
     from pdefa_b200 import _native as N
     from pdefa_b200.engine_file import write_engine
+    from pdefa_b200.replicas import job_throughput, reduce_job
     from pdefa_b200.yolo import build_yolov8, conv_flops
 
     torch.cuda.set_device(local)
@@ -266,11 +267,9 @@ def main():
     if args.layers and rank == 0:
         for (k, name), v in zip(summary, step_ms):
             print(f"{v / args.steps:9.4f} ms  {k:14s} {name}", file=sys.stderr)
-    t = torch.tensor([ms], device="cuda")
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
-    value = B * world * args.steps / (ms_max / 1e3)
+    # every rank processed B images per step; the job ends with the slowest rank
+    ms_max, images = reduce_job(ms, B * args.steps, device=torch.device("cuda", local))
+    value = job_throughput(images, ms_max)
 
     # roofline of the tensor-core conv family, measured inside the timed region
     hbm, peak_burst, peak_sus, peak_src = load_peaks()
@@ -305,10 +304,8 @@ def main():
         bi.detect(xnp, conf_thres=0.25, iou_thres=0.45, max_det=max_det)
     e2e_s = time.perf_counter() - t0
     bi.close()
-    te = torch.tensor([e2e_s], device="cuda")
-    if world > 1:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_value = B * world * e2e_steps / float(te.item())
+    e2e_ms, e2e_images = reduce_job(e2e_s * 1e3, B * e2e_steps, device=torch.device("cuda", local))
+    e2e_value = job_throughput(e2e_images, e2e_ms)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
