@@ -825,7 +825,8 @@ void launch_conv_tc(const ConvArgs& a, int op_dt, int* err, cudaStream_t s) {
     // in shared memory, loaded once per CTA. The choices follow per-layer sweeps of
     // every combination on B200 (YOLOv8 layer shapes):
     //   * CTAs per SM matter most: as many as TMEM allows (two accumulators of
-    //     bufcols columns each), four at most with 4 epilogue warps, two with 8;
+    //     bufcols columns each), four at most with 4 epilogue warps, two with 8,
+    //     even when that leaves a ring of two slots;
     //   * windows win where im2col moves narrow rows (channel chunks under 128
     //     bytes: Cin = 16, 32, 80, ...), im2col elsewhere;
     //   * resident weights whenever they fit without costing a CTA, and always for
@@ -863,11 +864,11 @@ void launch_conv_tc(const ConvArgs& a, int op_dt, int* err, cudaStream_t s) {
         const uint32_t b_st = bres ? 0u : btile;
         const uint32_t st = a_st + b_st;
         const uint32_t fixed_c = fixed + (bres ? bres_all : 0u) + (mode == 2 ? 2u * win_slot : 0u);
-        const int min_st = st == 0 ? 0 : (mode == 2 ? 3 : 4);     // 2 suffice at one CTA
+        // two ring slots suffice: more CTAs beat a deeper ring (swept on B200)
+        const int min_st = st == 0 ? 0 : 2;
         auto room = [&](int n) { return (int64_t)(228u * 1024u) / n - (int64_t)fixed_c; };
         for (int n = max_ctas; n >= 1; --n) {
-            const int need = n == 1 ? std::min(min_st, 2) : min_st;
-            if (room(n) >= 0 && room(n) >= (int64_t)need * st) {
+            if (room(n) >= 0 && room(n) >= (int64_t)min_st * st) {
                 c.ctas = n;
                 c.stages = st == 0 ? 0 : (int)std::min<int64_t>(12, room(n) / st);
                 return c;
