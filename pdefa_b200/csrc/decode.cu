@@ -53,18 +53,32 @@ __device__ __forceinline__ uint32_t desc_key(float f) {
     return ~asc;
 }
 
-__device__ __forceinline__ double iou_ref(const Det& a, const Det& b) {
+// Whether the reference's IoU (_bindings.py _iou: inter / (area_a + area_b - inter +
+// 1e-9) in float64, 0 without overlap) is NOT <= thr, decided exactly but with the
+// float64 division only where needed. With D the reference's rounded denominator and
+// q the exact quotient inter / D, the reference's IoU is rn(q). e = fma(-thr, D, inter) has the sign of
+// q - thr (one rounding keeps a nonzero sign). e <= 0: q <= thr, so rn(q) <= thr (thr is
+// a double and rounding is monotone). e > 2 ulp(thr) D: q - thr > ulp(thr) even after
+// e's rounding, so rn(q) > thr. Only q within ~2 ulp above thr (and odd inputs:
+// thr outside (0,1), D <= 0 or NaN) take the division.
+__device__ __forceinline__ bool iou_exceeds(const Det& a, const Det& b, double thr, double two_ulp_thr) {
     const double x1 = a.x1 > b.x1 ? a.x1 : b.x1;
     const double y1 = a.y1 > b.y1 ? a.y1 : b.y1;
     const double x2 = a.x2 < b.x2 ? a.x2 : b.x2;
     const double y2 = a.y2 < b.y2 ? a.y2 : b.y2;
     const double w = __dsub_rn(x2, x1);
     const double h = __dsub_rn(y2, y1);
-    if (w <= 0.0 || h <= 0.0) return 0.0;
+    if (w <= 0.0 || h <= 0.0) return !(0.0 <= thr);
     const double inter = __dmul_rn(w, h);
     const double area_a = __dmul_rn(__dsub_rn(a.x2, a.x1), __dsub_rn(a.y2, a.y1));
     const double area_b = __dmul_rn(__dsub_rn(b.x2, b.x1), __dsub_rn(b.y2, b.y1));
-    return __ddiv_rn(inter, __dadd_rn(__dsub_rn(__dadd_rn(area_a, area_b), inter), 1e-9));
+    const double D = __dadd_rn(__dsub_rn(__dadd_rn(area_a, area_b), inter), 1e-9);
+    if (thr > 0.0 && thr < 1.0 && D > 0.0) {
+        const double e = __fma_rn(-thr, D, inter);
+        if (e <= 0.0) return false;
+        if (e > __dmul_rn(two_ulp_thr, D)) return true;
+    }
+    return !(__ddiv_rn(inter, D) <= thr);
 }
 
 __device__ __forceinline__ double clamp_ref(double v, double hi) {
@@ -222,13 +236,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_nms_kernel(DecodeArgs p) {
     // Per sub-block: (a) stage its records in shared memory; (b) mark boxes that a box
     // kept before the sub-block suppresses; (c) build the in-block suppression matrix
     // (bit i of row j: box i < j of the same class with IoU not <= thres); (d) one
-    // thread settles the boxes in order with that matrix; (e) append the kept ones.
+    // warp settles the boxes in order with that matrix; (e) append the kept ones.
     Det* sub = reinterpret_cast<Det*>(grp + kMaxClasses);              // kSub
     Det* kept_s = sub + kSub;                                          // kKeptSmem
     uint32_t* mask = reinterpret_cast<uint32_t*>(kept_s + kKeptSmem);  // kSub * kSub / 32
     int* pre = reinterpret_cast<int*>(mask + kSub * (kSub / 32));      // kSub
     __shared__ uint32_t kbits[kSub / 32];
-    constexpr int kParts = kThreads / kSub;
+    // 2 ulp(thr) for thr in (0, 1) (used only there)
+    const double two_ulp = p.iou > 0.0 && p.iou < 1.0
+        ? 2.0 * (__longlong_as_double(__double_as_longlong(p.iou) + 1) - p.iou) : 0.0;
     for (int base = 0; base < n && s_kept < p.max_det; base += kSub) {
         const int cnt = n - base < kSub ? n - base : kSub;
         const int kept0 = s_kept;
@@ -238,37 +254,48 @@ __global__ void __launch_bounds__(kThreads, 1) decode_nms_kernel(DecodeArgs p) {
         }
         if (tid < kSub / 32) kbits[tid] = 0;
         __syncthreads();
-        const int j = tid % kSub, part = tid / kSub;
-        if (j < cnt) {
+        constexpr int kWarps = kThreads / 32;
+        // (b) boxes kept before this sub-block: one warp per candidate, lanes over kept
+        for (int j = warp; j < cnt; j += kWarps) {
             const Det c = sub[j];
             bool sup = false;
-            for (int r = part; r < kept0 && !sup; r += kParts) {
+            for (int r = lane; r < kept0 && !sup; r += 32) {
                 const Det& o = r < kKeptSmem ? kept_s[r] : out[r];
-                if (o.cls == c.cls && !(iou_ref(o, c) <= p.iou)) sup = true;
+                sup = o.cls == c.cls && iou_exceeds(o, c, p.iou, two_ulp);
             }
-            if (sup) pre[j] = 1;
-            for (int w = part; w < kSub / 32; w += kParts) {
-                uint32_t bits = 0;
-                for (int t = 0; t < 32; ++t) {
-                    const int i = 32 * w + t;
-                    if (i >= j) break;
+            sup = __any_sync(0xffffffffu, sup);
+            if (lane == 0) pre[j] = sup ? 1 : 0;
+        }
+        // (c) in-block suppression matrix: one warp per row j, a ballot per 32 columns;
+        //     only the words holding some i < j are written (the sweep reads no other)
+        for (int j = warp; j < cnt; j += kWarps) {
+            const Det c = sub[j];
+            for (int w = 0; 32 * w < j; ++w) {
+                const int i = 32 * w + lane;
+                bool sup = false;
+                if (i < j) {
                     const Det& o = sub[i];
-                    if (o.cls == c.cls && !(iou_ref(o, c) <= p.iou)) bits |= 1u << t;
+                    sup = o.cls == c.cls && iou_exceeds(o, c, p.iou, two_ulp);
                 }
-                mask[j * (kSub / 32) + w] = bits;
+                const uint32_t bits = __ballot_sync(0xffffffffu, sup);
+                if (lane == 0) mask[j * (kSub / 32) + w] = bits;
             }
         }
         __syncthreads();
-        if (tid == 0) {
+        // (d) settle the boxes in order: warp 0, lane w < 8 holds the kept bits of word w
+        if (warp == 0) {
+            uint32_t kbw = 0;
             int k = kept0;
             for (int q = 0; q < cnt && k < p.max_det; ++q) {
                 if (pre[q]) continue;
-                const uint32_t* row = mask + q * (kSub / 32);
-                bool sup = false;
-                for (int w = 0; w <= (q >> 5); ++w) sup |= (row[w] & kbits[w]) != 0;
-                if (!sup) { kbits[q >> 5] |= 1u << (q & 31); ++k; }
+                const uint32_t row = lane < kSub / 32 ? mask[q * (kSub / 32) + lane] : 0u;
+                if (!__any_sync(0xffffffffu, (row & kbw) != 0u)) {
+                    if (lane == (q >> 5)) kbw |= 1u << (q & 31);
+                    ++k;
+                }
             }
-            s_kept = k;
+            if (lane < kSub / 32) kbits[lane] = kbw;
+            if (lane == 0) s_kept = k;
         }
         __syncthreads();
         if (tid < cnt && ((kbits[tid >> 5] >> (tid & 31)) & 1u)) {
