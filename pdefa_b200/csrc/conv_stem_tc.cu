@@ -99,7 +99,7 @@ __device__ __forceinline__ void gather_row(const ConvArgs& a, const StemParams& 
 }
 
 template <int KH, int KW, int CIN>
-__global__ void __launch_bounds__(128, 4) conv_stem_tc_kernel(const StemParams P) {
+__global__ void __launch_bounds__(128, 8) conv_stem_tc_kernel(const StemParams P) {
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
@@ -287,8 +287,10 @@ void launch_conv_stem_tc(const ConvArgs& a, int* err, cudaStream_t s) {
         if (!sm_count[dev]) PB_CUDA(cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev));
         sms = sm_count[dev];
     }
-    // TMEM: 2 * ncols columns per CTA, at most 512 per SM
-    const int per_sm = std::max(1, std::min(4, 512 / (2 * P.ncols)));
+    // Each CTA works its tiles one after another (gather, MMA, drain), so throughput
+    // comes from CTAs per SM: up to 8 (64 registers a thread), TMEM 2 * ncols columns
+    // each within 512.
+    const int per_sm = std::max(1, std::min(8, 512 / (2 * P.ncols)));
     const int64_t grid = std::min<int64_t>(P.tiles, (int64_t)sms * per_sm);
     if (a.kh == 3 && a.kw == 3 && a.cin == 3) conv_stem_tc_kernel<3, 3, 3><<<(unsigned)grid, 128, smem, s>>>(P);
     else conv_stem_tc_kernel<0, 0, 0><<<(unsigned)grid, 128, smem, s>>>(P);
