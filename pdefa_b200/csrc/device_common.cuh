@@ -42,8 +42,7 @@ __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x));
 // where 2^n is built from the exponent bits of (n + 127). Outside |x| <= 88.37626
 // it returns x (large x) or 0 (very negative x). Horner steps are fused
 // multiply-adds, as the reference is compiled with -ffp-contract=fast.
-template <bool FAST_DIV>
-__device__ __forceinline__ float silu_wino_impl(float x) {
+__device__ __forceinline__ float silu_wino_f(float x) {
     const float nx = -x;
     if (nx < -88.37626f) return x;
     if (nx > 88.37626f) return 0.0f;
@@ -59,11 +58,30 @@ __device__ __forceinline__ float silu_wino_impl(float x) {
     p = fmaf(p, f, 1.0f);
     const uint32_t bits = (uint32_t)((int32_t)n + 127) << 23;
     const float scale = __uint_as_float(bits);
-    return FAST_DIV ? __fdividef(x, fmaf(p, scale, 1.0f)) : x / fmaf(p, scale, 1.0f);
+    return x / fmaf(p, scale, 1.0f);
 }
-__device__ __forceinline__ float silu_wino_f(float x) { return silu_wino_impl<false>(x); }
-// The same flavour with an approximate divide (~2 ulp), for the BF16/TF32 paths.
-__device__ __forceinline__ float silu_wino_fast(float x) { return silu_wino_impl<true>(x); }
+
+// The same flavour for the BF16/TF32 epilogues (results held to 1e-2): branch-free,
+// round-to-nearest-even for n (differs from round-half-away only at exact ties, where
+// both neighbours are valid results of the flavour's jump), n clamped so 2^n stays a
+// normal float, and an approximate divide (~2 ulp).
+__device__ __forceinline__ float silu_wino_fast(float x) {
+    const float fx = -x * 1.44269504088896341f;
+    const float n = fminf(fmaxf(rintf(fx), -126.0f), 127.0f);
+    const float f = fx - n;
+    float p = 1.9875691500e-4f;
+    p = fmaf(p, f, 1.3981999507e-3f);
+    p = fmaf(p, f, 8.3334519073e-3f);
+    p = fmaf(p, f, 4.1665795894e-2f);
+    p = fmaf(p, f, 1.6666665459e-1f);
+    p = fmaf(p, f, 5.0000001201e-1f);
+    p = fmaf(p, f, 1.0f);
+    const float scale = __int_as_float(((int)n + 127) << 23);
+    float y = __fdividef(x, fmaf(p, scale, 1.0f));
+    y = x > 88.37626f ? x : y;
+    y = x < -88.37626f ? 0.0f : y;
+    return y;
+}
 
 __device__ __forceinline__ float apply_act(float v, int act, float p0, float p1) {
     switch (act) {
