@@ -831,7 +831,6 @@ void launch_conv_tc(const ConvArgs& a, int op_dt, int* err, cudaStream_t s) {
     //     bytes: Cin = 16, 32, 80, ...), im2col elsewhere;
     //   * resident weights whenever they fit without costing a CTA, and always for
     //     windows (streamed weights would dominate the window's rows).
-    // 1x1 convs with 8 epilogue warps stage their output for TMA stores.
     const bool one = a.kh == 1 && a.kw == 1 && a.sh == 1 && a.sw == 1 && a.ph == 0 && a.pw == 0;
     const int Wp = (int)a.in.shape[2] + 2 * a.pw;
     const int NR = (a.kh * Wp + a.kw + BM - 2 + Wp - 1) / Wp;   // window rows covering row offsets + 128
@@ -840,14 +839,14 @@ void launch_conv_tc(const ConvArgs& a, int op_dt, int* err, cudaStream_t s) {
     const int chunks = a.cin / ch;
     const int nk = p.taps * chunks;
     const int tmem_ctas = 512 / p.tmem_cols;                     // two accumulators per CTA
-    // 1x1 convs drain a tile per handful of MMAs: 8 epilogue warps with TMA stores
-    // from 64 output channels up; multi-tap convs switch at Cout > 64 (TMEM then
-    // allows two CTAs at most).
-    const int epi = (one ? bn >= 64 : tmem_ctas <= 2) ? 8 : 4;
+    // 8 epilogue warps for 1x1 convs from 128 output channels up and for multi-tap
+    // convs above 64 (TMEM then allows two CTAs at most); 1x1 convs always stage
+    // their output for TMA stores.
+    const int epi = (one ? bn >= 128 : tmem_ctas <= 2) ? 8 : 4;
     const int max_ctas = std::min(epi == 8 ? 2 : 4, tmem_ctas);  // register file, TMEM
     const int oes = a.out.dt == BF16 ? 2 : 4;
     const uint32_t staging = (uint32_t)bn * BM * oes;
-    const bool tma_store = p.taps == 1 && epi == 8 && pixel_dense(a.out) && staging <= 64u * 1024u;
+    const bool tma_store = p.taps == 1 && pixel_dense(a.out) && staging <= 64u * 1024u;
     const uint32_t fixed = 1024 + kBarrierBytes + 1024 + (tma_store ? staging : 0u);   // alignment, barriers, reserve
     const uint32_t btile = (uint32_t)bn * swb;
     const uint32_t bres_all = (uint32_t)nk * btile;
