@@ -111,6 +111,14 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
         : "memory");
 }
 
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
+                                            int c2) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];"
+        ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+        : "memory");
+}
+
 __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
                                             int c2, int c3) {
     asm volatile(
@@ -593,7 +601,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     int tap, cc;
                     if (p.a_mode == 2) { cc = kb / p.taps; tap = kb - cc * p.taps; }
                     else { tap = kb / p.cin_chunks; cc = kb - tap * p.cin_chunks; }
-                    tma_load_2d(bres + (uint32_t)kb * p.btile_bytes, &tmB, bres_full, tap * p.cin + cc * p.ch, 0);
+                    tma_load_3d(bres + (uint32_t)kb * p.btile_bytes, &tmB, bres_full, cc * p.ch, tap, 0);
                 }
             }
             for (int64_t t = blockIdx.x; t < total && !*abort_flag; t += gridDim.x) {
@@ -650,7 +658,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     } else if (p.a_mode == 1) {
                         tma_load_2d(sa, &tmA, &full[st], cc * p.ch, (int)m0);
                     }
-                    if (!p.b_res) tma_load_2d(sb, &tmB, &full[st], tap * p.cin + cc * p.ch, n0);
+                    if (!p.b_res) tma_load_3d(sb, &tmB, &full[st], cc * p.ch, tap, n0);
                 }
             }
             // Drain: the last use of every slot must have landed before the CTA exits.
@@ -732,11 +740,17 @@ CUtensorMapSwizzle swizzle_of(int swb) {
     return swb == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : (swb == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
 }
 
+// Channels per k-block (one swizzled smem row of 128, 64 or 32 bytes). The largest
+// row that divides Cin, except that Cin with only 32-byte rows and more than 64
+// bytes per pixel (Cin = 48, 80, 112 ... in bf16) takes 128-byte rows with a zero
+// padded last chunk: on B200 a k-block costs about the same whatever its row width,
+// so 80 -> 80 3x3 at 80x80 runs 1.85x faster in two 64-channel chunks (of which 48
+// channels read as zeros) than in five 16-channel ones (swept per layer).
 int pick_chunk(int cin, int esz) {
     const int c128 = 128 / esz, c64 = 64 / esz, c32 = 32 / esz;
     if (cin % c128 == 0) return c128;
     if (cin % c64 == 0) return c64;
-    if (cin % c32 == 0) return c32;
+    if (cin % c32 == 0) return cin * esz > 64 ? c128 : c32;
     return 0;
 }
 
@@ -836,7 +850,7 @@ void launch_conv_tc(const ConvArgs& a, int op_dt, int* err, cudaStream_t s) {
     const int NR = (a.kh * Wp + a.kw + BM - 2 + Wp - 1) / Wp;   // window rows covering row offsets + 128
     const int ch = pick_chunk(a.cin, esz);
     const int swb = ch * esz;
-    const int chunks = a.cin / ch;
+    const int chunks = (a.cin + ch - 1) / ch;   // a last, partial chunk reads zeros past Cin
     const int nk = p.taps * chunks;
     const int tmem_ctas = 512 / p.tmem_cols;                     // two accumulators per CTA
     // 8 epilogue warps for 1x1 convs from 128 output channels up and for multi-tap
@@ -971,12 +985,13 @@ void launch_conv_tc(const ConvArgs& a, int op_dt, int* err, cudaStream_t s) {
         if (r != CUDA_SUCCESS) fail(ENGINE_ERR_RUNTIME, "cuTensorMapEncodeIm2col(A) failed: " + std::to_string((int)r));
     }
     {
-        const int64_t K = (int64_t)a.kh * a.kw * a.cin;
-        cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)a.cout};
-        cuuint64_t strides[1] = {(cuuint64_t)(K * esz)};
-        cuuint32_t box[2] = {(cuuint32_t)ch, (cuuint32_t)bn};
-        cuuint32_t es[2] = {1, 1};
-        CUresult r = g_tiled(&tmB, tdt, 2, const_cast<void*>(a.weight), dims, strides, box, es,
+        // [Cout, taps, Cin] weights: one box = one channel chunk of one tap for bn
+        // output channels; channels past Cin (a partial last chunk) read as zeros
+        cuuint64_t dims[3] = {(cuuint64_t)a.cin, (cuuint64_t)p.taps, (cuuint64_t)a.cout};
+        cuuint64_t strides[2] = {(cuuint64_t)a.cin * esz, (cuuint64_t)p.taps * a.cin * esz};
+        cuuint32_t box[3] = {(cuuint32_t)ch, 1, (cuuint32_t)bn};
+        cuuint32_t es[3] = {1, 1, 1};
+        CUresult r = g_tiled(&tmB, tdt, 3, const_cast<void*>(a.weight), dims, strides, box, es,
                              CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle_of(swb), CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
         if (r != CUDA_SUCCESS) fail(ENGINE_ERR_RUNTIME, "cuTensorMapEncodeTiled(W) failed: " + std::to_string((int)r));
