@@ -10,8 +10,10 @@ Printed JSON line (rank 0):
 * value: images/s over all GPUs with inputs resident in HBM (seeded torch.rand on the
   device, 1.26 GB per GPU > L2, so no L2 flush is needed), device-timed with CUDA
   events, max over ranks;
-* e2e: the same through the public batch API (pdefa_batch_run, what
-  BatchInference.detect calls) from pinned host images to host detections;
+* e2e: the same through the public batch API (BatchInference.detect_arrays ->
+  pdefa_batch_run) from pinned host images to host detections, the runner
+  pipelining micro-batches of --e2e-micro images (copy of one overlapping the
+  inference of the previous);
 * roofline: the tcgen05 convolution kernels of the step (the dominant kernel
   family): conv FLOPs / their CUDA-event time measured inside the timed region,
   against the measured sustained BF16 peak;
@@ -178,6 +180,8 @@ def main():
     ap.add_argument("--imgsz", type=int, default=640)
     ap.add_argument("--precision", default="bf16", choices=["bf16", "tf32", "fp32"])
     ap.add_argument("--e2e-steps", type=int, default=0, help="steps for the e2e leg (default: --steps)")
+    ap.add_argument("--e2e-micro", type=int, default=64,
+                    help="micro-batch of the e2e leg's pipelined batch runner (images per GPU launch)")
     ap.add_argument("--cpu-images", type=int, default=48, help="images in the bounded CPU baseline sample")
     ap.add_argument("--ref-images", type=int, default=4, help="images per step of the reference arm")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -292,16 +296,19 @@ def main():
 
     # e2e: pinned host images -> public batch API on this GPU -> host detections
     e2e_steps = args.e2e_steps or args.steps
+    e2e_micro = max(1, min(B, args.e2e_micro))
     xh = torch.empty((B, 3, args.imgsz, args.imgsz), dtype=torch.float32, pin_memory=True)
     xh.copy_(x)
-    bi = pb.BatchInference(ctx, model, batch_size=B, devices=[local], precision=prec)
+    # micro-batches of e2e_micro images: the copy of one onto the GPU overlaps the
+    # inference of the previous one
+    bi = pb.BatchInference(ctx, model, batch_size=e2e_micro, devices=[local], precision=prec)
     xnp = xh.numpy()
-    bi.detect(xnp)
+    bi.detect_arrays(xnp)
     if world > 1:
         dist.barrier()
     t0 = time.perf_counter()
     for _ in range(e2e_steps):
-        bi.detect(xnp, conf_thres=0.25, iou_thres=0.45, max_det=max_det)
+        bi.detect_arrays(xnp, conf_thres=0.25, iou_thres=0.45, max_det=max_det)
     e2e_s = time.perf_counter() - t0
     bi.close()
     e2e_ms, e2e_images = reduce_job(e2e_s * 1e3, B * e2e_steps, device=torch.device("cuda", local))
@@ -327,7 +334,8 @@ def main():
             "data": "synthetic (seeded uniform images, random-init weights)", "config": config(args, world),
             "clocks": clocks, "gpu_launches": launches_per_step * args.steps,
             "e2e": {"value": e2e_value, "unit": "images/s", "h2d_bytes_per_step": xh.numel() * 4,
-                    "d2h_bytes_per_step": B * 4 + B * max_det * 48},
+                    "d2h_bytes_per_step": B * 4 + B * max_det * 48, "micro_batch": e2e_micro,
+                    "api": "BatchInference.detect_arrays (pdefa_batch_run), pinned host images"},
             "roofline": roofline, "cpu_baseline": cpu,
             "conv_gflop_per_image": flops_img / 1e9,
         }))

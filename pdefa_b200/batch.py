@@ -2,9 +2,11 @@
 
 The reference runs `batch_size` batch-1 Sessions on a Python thread pool over one
 CPU. Here one replica of the model lives on each selected GPU; a batch of images is
-split into contiguous shards, each GPU runs its shard as one batched forward pass
-plus the GPU decode/NMS, and only detections come back. There is no collective.
-The C++ runner (pdefa_batch_run) drives all GPUs from native threads.
+split into contiguous shards, each GPU runs its shard in micro-batches of
+`batch_size` images (batched forward pass plus the GPU decode/NMS), and only
+detections come back. There is no collective. The C++ runner (pdefa_batch_run)
+drives all GPUs from native threads and pipelines each GPU's micro-batches over two
+streams: the copy of micro-batch i+1 onto the GPU overlaps the inference of i.
 """
 from __future__ import annotations
 
@@ -41,19 +43,40 @@ class BatchInference:
                "batch_create")
         self._handle = h
 
-    def detect(self, images, metas: Optional[Sequence[PreprocessMeta]] = None, conf_thres: float = 0.25,
-               iou_thres: float = 0.45, max_det: int = 300) -> List[List[dict]]:
-        """images: [N, 3, H, W] float32 array -> per-image detection dicts."""
+    # PdefaDetection (include/pdefa_b200_ext.h) as a numpy record
+    DET_DTYPE = [("x1", "<f8"), ("y1", "<f8"), ("x2", "<f8"), ("y2", "<f8"), ("conf", "<f4"), ("cls", "<i4"),
+                 ("anchor", "<i4"), ("reserved", "<i4")]
+
+    def detect_arrays(self, images, metas: Optional[Sequence[PreprocessMeta]] = None, conf_thres: float = 0.25,
+                      iou_thres: float = 0.45, max_det: int = 300):
+        """images: [N, 3, H, W] float32 array -> (counts int32 [N], dets record array
+        [N, max_det] with fields x1 y1 x2 y2 conf cls anchor); image b's detections
+        are dets[b, :counts[b]], best first. Images in page-locked memory (e.g. a
+        pinned torch tensor's .numpy()) reach the GPU fastest."""
         import numpy as np
         x = np.ascontiguousarray(images, dtype=np.float32)
         n = x.shape[0]
         md = max(int(max_det), 0)
-        counts = (N.i32 * max(n, 1))()
-        dets = (N.Detection * max(n * md, 1))()
+        counts = np.zeros(max(n, 1), dtype=np.int32)
+        dets = np.zeros((max(n, 1), max(md, 1)), dtype=self.DET_DTYPE)
         marr = (N.PreMeta * n)(*[m.to_c() for m in metas]) if metas is not None else None
         _check(N.lib().pdefa_batch_run(self._handle, x.ctypes.data, n, marr, float(conf_thres), float(iou_thres),
-                                       md, counts, dets), "batch_run")
-        return [[_det_dict(dets[b * md + i]) for i in range(counts[b])] for b in range(n)]
+                                       md, counts.ctypes.data_as(C.POINTER(N.i32)),
+                                       dets.ctypes.data_as(C.POINTER(N.Detection))), "batch_run")
+        return counts[:n], dets[:n, :md]
+
+    def detect(self, images, metas: Optional[Sequence[PreprocessMeta]] = None, conf_thres: float = 0.25,
+               iou_thres: float = 0.45, max_det: int = 300) -> List[List[dict]]:
+        """images: [N, 3, H, W] float32 array -> per-image detection dicts
+        (x1, y1, x2, y2, conf, cls), best first."""
+        counts, dets = self.detect_arrays(images, metas, conf_thres, iou_thres, max_det)
+        out = []
+        for b in range(len(counts)):
+            d = dets[b, :counts[b]]
+            out.append([{"x1": x1, "y1": y1, "x2": x2, "y2": y2, "conf": cf, "cls": c}
+                        for x1, y1, x2, y2, cf, c in zip(d["x1"].tolist(), d["y1"].tolist(), d["x2"].tolist(),
+                                                         d["y2"].tolist(), d["conf"].tolist(), d["cls"].tolist())])
+        return out
 
     def run(self, image_paths: List[str], target_w: int = 640, target_h: int = 640) -> List[Tuple[Tensor, PreprocessMeta]]:
         """Reference signature (image files -> raw outputs). Needs host image decoding."""

@@ -1,6 +1,7 @@
 // Additive entry points (include/pdefa_b200_ext.h): precision/device selection,
 // device-pointer execution, tensor-core GEMM, batched GPU decode/NMS and the
 // multi-GPU batch runner (one replica per device, contiguous shards, no collective).
+#include <cstring>
 #include <thread>
 
 #include "../../include/pdefa_b200_ext.h"
@@ -59,21 +60,46 @@ void decode_on_device(const float* d_preds, int64_t batch, int64_t channels, int
 }  // namespace
 
 struct PdefaBatchRunner {
-    struct Replica {
-        int device = 0;
-        cudaStream_t stream = nullptr;
+    // One of two ping-pong pipeline lanes of a replica: its own plans (input and
+    // activation buffers), decode buffers and pinned host copies of the results, so
+    // that the copy of micro-batch i+1 onto the GPU overlaps the inference of i.
+    struct Lane {
         std::map<int64_t, std::unique_ptr<Plan>> plans;
-        void* counts = nullptr;
-        void* dets = nullptr;
+        void* counts = nullptr;      // device [max_per_device]
+        void* dets = nullptr;        // device [max_per_device * max_det]
         void* work = nullptr;
         void* meta = nullptr;
+        int32_t* h_counts = nullptr; // pinned host mirrors
+        PdefaDetection* h_dets = nullptr;
         size_t dets_cap = 0;
+        cudaEvent_t h2d = nullptr, done = nullptr;
+        bool busy = false;           // results of (c0, nb) pending
+        int64_t c0 = 0, nb = 0;
+    };
+    struct Replica {
+        int device = 0;
+        cudaStream_t stream = nullptr;   // inference + decode + result copies
+        cudaStream_t copy = nullptr;     // image copies onto the GPU
+        Lane lanes[2];
     };
     std::shared_ptr<const Graph> graph;
     int precision = PREC_BF16;
     int64_t max_per_device = 1;
     std::vector<Replica> reps;
 };
+
+namespace {
+
+void free_lane(PdefaBatchRunner::Lane& l) {
+    if (l.counts) { cudaFree(l.counts); cudaFree(l.dets); cudaFree(l.work); cudaFree(l.meta); }
+    if (l.h_counts) { cudaFreeHost(l.h_counts); cudaFreeHost(l.h_dets); }
+    l.counts = l.dets = l.work = l.meta = nullptr;
+    l.h_counts = nullptr;
+    l.h_dets = nullptr;
+    l.dets_cap = 0;
+}
+
+}  // namespace
 
 extern "C" {
 
@@ -298,6 +324,11 @@ ENGINE_API EngineStatus pdefa_batch_create(EngineModel* model, int32_t n_devices
             require_device(rp.device);
             PB_CUDA(cudaSetDevice(rp.device));
             PB_CUDA(cudaStreamCreateWithFlags(&rp.stream, cudaStreamNonBlocking));
+            PB_CUDA(cudaStreamCreateWithFlags(&rp.copy, cudaStreamNonBlocking));
+            for (auto& l : rp.lanes) {
+                PB_CUDA(cudaEventCreateWithFlags(&l.h2d, cudaEventDisableTiming));
+                PB_CUDA(cudaEventCreateWithFlags(&l.done, cudaEventDisableTiming));
+            }
         }
         *out_runner = r.release();
         return ENGINE_OK;
@@ -317,46 +348,76 @@ ENGINE_API EngineStatus pdefa_batch_run(PdefaBatchRunner* r, const float* images
         std::vector<std::thread> th;
         for (int d = 0; d < nd; ++d) {
             th.emplace_back([&, d] {
+                auto& rp = r->reps[d];
+                // results of a lane's finished micro-batch -> the caller's arrays
+                auto retire = [&](PdefaBatchRunner::Lane& l) {
+                    if (!l.busy) return;
+                    l.busy = false;
+                    PB_CUDA(cudaEventSynchronize(l.done));
+                    std::memcpy(out_counts + l.c0, l.h_counts, (size_t)l.nb * 4);
+                    if (max_det > 0)
+                        std::memcpy(out_dets + l.c0 * max_det, l.h_dets, (size_t)l.nb * max_det * sizeof(PdefaDetection));
+                };
                 try {
-                    auto& rp = r->reps[d];
                     PB_CUDA(cudaSetDevice(rp.device));
                     const int64_t lo = std::min(n_images, d * per), hi = std::min(n_images, lo + per);
-                    for (int64_t c0 = lo; c0 < hi; c0 += r->max_per_device) {
+                    // Micro-batches of at most max_per_device images alternate between the two
+                    // lanes: the copy stream brings micro-batch i+1 onto the GPU while the
+                    // compute stream runs inference + decode of micro-batch i.
+                    int64_t i = 0;
+                    for (int64_t c0 = lo; c0 < hi; c0 += r->max_per_device, ++i) {
                         const int64_t nb = std::min(r->max_per_device, hi - c0);
-                        auto it = rp.plans.find(nb);
-                        if (it == rp.plans.end())
-                            it = rp.plans.emplace(nb, std::make_unique<Plan>(r->graph, nb, r->precision, rp.device)).first;
+                        auto& l = rp.lanes[i & 1];
+                        retire(l);    // the lane's buffers are free once its previous micro-batch is done
+                        auto it = l.plans.find(nb);
+                        if (it == l.plans.end())
+                            it = l.plans.emplace(nb, std::make_unique<Plan>(r->graph, nb, r->precision, rp.device)).first;
                         Plan& p = *it->second;
                         const auto& os = p.output_shape(0);
                         if (os.size() != 3) fail(ENGINE_ERR_INVALID_SHAPE, "batch runner expects a [B, 4+nc, A] output");
                         const int64_t ch = os[1], A = os[2];
-                        const size_t need = (size_t)nb * std::max(1, max_det) * sizeof(PdefaDetection);
-                        if (rp.dets_cap < need || !rp.work) {
-                            if (rp.counts) { cudaFree(rp.counts); cudaFree(rp.dets); cudaFree(rp.work); cudaFree(rp.meta); }
+                        const size_t need = (size_t)r->max_per_device * std::max(1, max_det) * sizeof(PdefaDetection);
+                        if (l.dets_cap < need || !l.work) {
+                            free_lane(l);
                             const int64_t cap_imgs = r->max_per_device;
-                            PB_CUDA(cudaMalloc(&rp.counts, cap_imgs * 4));
-                            const size_t dc = (size_t)cap_imgs * std::max(1, max_det) * sizeof(PdefaDetection);
-                            PB_CUDA(cudaMalloc(&rp.dets, dc));
-                            PB_CUDA(cudaMalloc(&rp.work, decode_work_bytes(cap_imgs, A)));
-                            PB_CUDA(cudaMalloc(&rp.meta, cap_imgs * sizeof(PdefaPreprocessMeta)));
-                            rp.dets_cap = dc;
+                            PB_CUDA(cudaMalloc(&l.counts, cap_imgs * 4));
+                            PB_CUDA(cudaMalloc(&l.dets, need));
+                            PB_CUDA(cudaMalloc(&l.work, decode_work_bytes(cap_imgs, A)));
+                            PB_CUDA(cudaMalloc(&l.meta, cap_imgs * sizeof(PdefaPreprocessMeta)));
+                            PB_CUDA(cudaMallocHost(reinterpret_cast<void**>(&l.h_counts), cap_imgs * 4));
+                            PB_CUDA(cudaMallocHost(reinterpret_cast<void**>(&l.h_dets), need));
+                            l.dets_cap = need;
                         }
                         const size_t ibytes = p.input_bytes(0);
                         PB_CUDA(cudaMemcpyAsync(p.input_buffer(0), images + c0 * (ibytes / 4 / nb), ibytes,
-                                                cudaMemcpyHostToDevice, rp.stream));
+                                                cudaMemcpyHostToDevice, rp.copy));
+                        PB_CUDA(cudaEventRecord(l.h2d, rp.copy));
+                        PB_CUDA(cudaStreamWaitEvent(rp.stream, l.h2d, 0));
                         p.run(rp.stream);
                         decode_on_device(p.output_buffer(0), nb, ch, A, metas ? metas + c0 : nullptr, conf_thres,
-                                         iou_thres, max_det, static_cast<int32_t*>(rp.counts), rp.dets, rp.work,
-                                         static_cast<int32_t*>(rp.meta), device_error_word(rp.device), rp.stream);
-                        PB_CUDA(cudaMemcpyAsync(out_counts + c0, rp.counts, nb * 4, cudaMemcpyDeviceToHost, rp.stream));
+                                         iou_thres, max_det, static_cast<int32_t*>(l.counts), l.dets, l.work,
+                                         static_cast<int32_t*>(l.meta), device_error_word(rp.device), rp.stream);
+                        PB_CUDA(cudaMemcpyAsync(l.h_counts, l.counts, nb * 4, cudaMemcpyDeviceToHost, rp.stream));
                         if (max_det > 0)
-                            PB_CUDA(cudaMemcpyAsync(out_dets + c0 * max_det, rp.dets, (size_t)nb * max_det * sizeof(PdefaDetection),
+                            PB_CUDA(cudaMemcpyAsync(l.h_dets, l.dets, (size_t)nb * max_det * sizeof(PdefaDetection),
                                                     cudaMemcpyDeviceToHost, rp.stream));
-                        PB_CUDA(cudaStreamSynchronize(rp.stream));
+                        PB_CUDA(cudaEventRecord(l.done, rp.stream));
+                        l.busy = true;
+                        l.c0 = c0;
+                        l.nb = nb;
                     }
+                    retire(rp.lanes[i & 1]);
+                    retire(rp.lanes[(i + 1) & 1]);
                     if (read_device_error(rp.device)) fail(ENGINE_ERR_RUNTIME, "device-side wait timed out");
                 } catch (const std::exception& e) {
                     errs[d] = e.what();
+                    // leave no lane pending: its buffers may be reused by the next call
+                    for (auto& l : rp.lanes) {
+                        if (l.busy) cudaEventSynchronize(l.done);
+                        l.busy = false;
+                    }
+                    cudaStreamSynchronize(rp.copy);
+                    cudaStreamSynchronize(rp.stream);
                 }
             });
         }
@@ -372,9 +433,15 @@ ENGINE_API void pdefa_batch_destroy(PdefaBatchRunner* r) {
     for (auto& rp : r->reps) {
         cudaSetDevice(rp.device);
         if (rp.stream) cudaStreamSynchronize(rp.stream);
-        rp.plans.clear();
-        if (rp.counts) { cudaFree(rp.counts); cudaFree(rp.dets); cudaFree(rp.work); cudaFree(rp.meta); }
+        if (rp.copy) cudaStreamSynchronize(rp.copy);
+        for (auto& l : rp.lanes) {
+            l.plans.clear();
+            free_lane(l);
+            if (l.h2d) cudaEventDestroy(l.h2d);
+            if (l.done) cudaEventDestroy(l.done);
+        }
         if (rp.stream) cudaStreamDestroy(rp.stream);
+        if (rp.copy) cudaStreamDestroy(rp.copy);
     }
     delete r;
 }

@@ -315,3 +315,25 @@ def test_batch_inference_matches_session_decode(y8n_128):
     for i in range(6):
         exp = pb.decode_yolo(y[i], None, 0.25, 0.45, 100)
         assert got[i] == exp
+
+
+def test_batch_inference_pipelined_micro_batches(y8n_128):
+    """Micro-batches alternate between the runner's two pipeline lanes (copy of one
+    overlapping inference of the other); results equal one single-batch pass, also
+    when the runner is reused and the last micro-batch is short."""
+    ctx = pb.Context(precision=pb.BF16)
+    m = pb.Model(ctx, y8n_128)
+    x = np.random.default_rng(11).random((7, 3, 128, 128), dtype=np.float32)
+    with pb.BatchInference(ctx, m, batch_size=7, devices=[0]) as bi:
+        c_ref, d_ref = bi.detect_arrays(x, conf_thres=0.2, iou_thres=0.5, max_det=50)
+    assert c_ref.shape == (7,) and d_ref.shape == (7, 50)
+    with pb.BatchInference(ctx, m, batch_size=2, devices=[0]) as bi:
+        for _ in range(2):
+            c, d = bi.detect_arrays(x, conf_thres=0.2, iou_thres=0.5, max_det=50)
+            np.testing.assert_array_equal(c, c_ref)
+            for b in range(7):
+                np.testing.assert_array_equal(d[b, :c[b]], d_ref[b, :c_ref[b]])
+        lists = bi.detect(x[:3], conf_thres=0.2, iou_thres=0.5, max_det=50)
+    for b in range(3):
+        assert [(e["x1"], e["y1"], e["x2"], e["y2"], e["conf"], e["cls"]) for e in lists[b]] == \
+            [(r["x1"], r["y1"], r["x2"], r["y2"], float(r["conf"]), int(r["cls"])) for r in d_ref[b, :c_ref[b]]]
