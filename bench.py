@@ -10,10 +10,11 @@ Printed JSON line (rank 0):
 * value: images/s over all GPUs with inputs resident in HBM (seeded torch.rand on the
   device, 1.26 GB per GPU > L2, so no L2 flush is needed), device-timed with CUDA
   events, max over ranks;
-* e2e: the same through the public batch API (BatchInference.detect_arrays ->
-  pdefa_batch_run) from pinned host images to host detections, the runner
-  pipelining micro-batches of --e2e-micro images (copy of one overlapping the
-  inference of the previous);
+* e2e: the same through the public batch API from pinned host images to host
+  detections: 8-bit RGB frames letterboxed on the GPU (BatchInference.detect_u8 ->
+  pdefa_batch_run_u8), and under e2e.f32_input float32 NCHW tensors
+  (detect_arrays -> pdefa_batch_run); the runner pipelines micro-batches of
+  --e2e-micro images (copy of one overlapping the inference of the previous);
 * roofline: the tcgen05 convolution kernels of the step (the dominant kernel
   family): conv FLOPs / their CUDA-event time measured inside the timed region,
   against the measured sustained BF16 peak;
@@ -294,25 +295,37 @@ def main():
                 "ms_by_kernel_kind": {k: round(v, 4) for k, v in by_kind.items()},
                 "decode_ms": ms_max / args.steps - sum(by_kind.values())}
 
-    # e2e: pinned host images -> public batch API on this GPU -> host detections
+    # e2e: pinned host images -> public batch API on this GPU -> host detections.
+    # Headline: decoded 8-bit RGB frames (what a camera or an image decoder hands
+    # over), letterboxed on the GPU (detect_u8); also the float32-tensor entry
+    # (detect_arrays), whose copies are 4x larger. The runner pipelines micro-batches
+    # of e2e_micro images: the copy of one onto the GPU overlaps the previous one's
+    # inference.
     e2e_steps = args.e2e_steps or args.steps
     e2e_micro = max(1, min(B, args.e2e_micro))
+    bi = pb.BatchInference(ctx, model, batch_size=e2e_micro, devices=[local], precision=prec)
+
+    def timed(fn):
+        fn()
+        if world > 1:
+            dist.barrier()
+        t0 = time.perf_counter()
+        for _ in range(e2e_steps):
+            fn()
+        ms, images = reduce_job((time.perf_counter() - t0) * 1e3, B * e2e_steps, device=torch.device("cuda", local))
+        return job_throughput(images, ms)
+
+    gen = torch.Generator(device="cuda").manual_seed(1000 + rank)
+    u8 = torch.empty((B, args.imgsz, args.imgsz, 3), dtype=torch.uint8, pin_memory=True)
+    u8.copy_(torch.randint(0, 256, (B, args.imgsz, args.imgsz, 3), dtype=torch.uint8, device="cuda", generator=gen))
+    u8np = u8.numpy()
+    e2e_value = timed(lambda: bi.detect_u8(u8np, args.imgsz, args.imgsz, conf_thres=0.25, iou_thres=0.45,
+                                           max_det=max_det))
     xh = torch.empty((B, 3, args.imgsz, args.imgsz), dtype=torch.float32, pin_memory=True)
     xh.copy_(x)
-    # micro-batches of e2e_micro images: the copy of one onto the GPU overlaps the
-    # inference of the previous one
-    bi = pb.BatchInference(ctx, model, batch_size=e2e_micro, devices=[local], precision=prec)
     xnp = xh.numpy()
-    bi.detect_arrays(xnp)
-    if world > 1:
-        dist.barrier()
-    t0 = time.perf_counter()
-    for _ in range(e2e_steps):
-        bi.detect_arrays(xnp, conf_thres=0.25, iou_thres=0.45, max_det=max_det)
-    e2e_s = time.perf_counter() - t0
+    e2e_f32_value = timed(lambda: bi.detect_arrays(xnp, conf_thres=0.25, iou_thres=0.45, max_det=max_det))
     bi.close()
-    e2e_ms, e2e_images = reduce_job(e2e_s * 1e3, B * e2e_steps, device=torch.device("cuda", local))
-    e2e_value = job_throughput(e2e_images, e2e_ms)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -333,9 +346,12 @@ def main():
             "vs_baseline": None, "dtype": "bf16" if prec == pb.BF16 else ("tf32" if prec == pb.TF32 else "f32"),
             "data": "synthetic (seeded uniform images, random-init weights)", "config": config(args, world),
             "clocks": clocks, "gpu_launches": launches_per_step * args.steps,
-            "e2e": {"value": e2e_value, "unit": "images/s", "h2d_bytes_per_step": xh.numel() * 4,
+            "e2e": {"value": e2e_value, "unit": "images/s", "h2d_bytes_per_step": u8.numel(),
                     "d2h_bytes_per_step": B * 4 + B * max_det * 48, "micro_batch": e2e_micro,
-                    "api": "BatchInference.detect_arrays (pdefa_batch_run), pinned host images"},
+                    "api": "BatchInference.detect_u8 (pdefa_batch_run_u8): pinned 8-bit RGB frames "
+                           f"[{B}, {args.imgsz}, {args.imgsz}, 3], GPU letterbox + inference + decode",
+                    "f32_input": {"value": e2e_f32_value, "h2d_bytes_per_step": xh.numel() * 4,
+                                  "api": "BatchInference.detect_arrays (pdefa_batch_run), pinned float32 NCHW"}},
             "roofline": roofline, "cpu_baseline": cpu,
             "conv_gflop_per_image": flops_img / 1e9,
         }))

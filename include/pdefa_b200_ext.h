@@ -136,6 +136,35 @@ ENGINE_API EngineStatus pdefa_batch_run(PdefaBatchRunner* runner, const float* i
                                         int32_t* out_counts, PdefaDetection* out_dets);
 ENGINE_API void         pdefa_batch_destroy(PdefaBatchRunner* runner);
 
+/* GPU letterbox preprocess for images already decoded to 8-bit pixels. Replaces the
+ * host letterbox of pdefa_preprocess_letterbox (pdefa/src/pdefa_c_api.cpp:83-126 ->
+ * imageloader/src/preprocess.cpp:15-147) with the same arithmetic: the float32 NCHW
+ * output and the meta record are bit-identical to the reference's.
+ * images: [n, src_h, src_w, channels] uint8, channels 1 (gray), 3 (RGB) or 4 (RGBA,
+ * alpha dropped); out: [n, 3, cfg->target_h, cfg->target_w] float32. The n images
+ * share one size, so one meta record describes them all. */
+ENGINE_API EngineStatus pdefa_letterbox_meta(int32_t src_w, int32_t src_h, const PdefaPreprocessConfig* cfg,
+                                             PdefaPreprocessMeta* out_meta);
+/* Device pointers on the current device; enqueues on `stream`, no allocation. */
+ENGINE_API EngineStatus pdefa_letterbox_device(const uint8_t* d_images, int64_t n, int32_t src_h, int32_t src_w,
+                                               int32_t channels, const PdefaPreprocessConfig* cfg, float* d_out,
+                                               void* stream);
+/* Host arrays; runs on `device` and returns when `out` is written. */
+ENGINE_API EngineStatus pdefa_letterbox(const uint8_t* images, int64_t n, int32_t src_h, int32_t src_w,
+                                        int32_t channels, const PdefaPreprocessConfig* cfg, float* out,
+                                        PdefaPreprocessMeta* out_meta, int32_t device);
+/* pdefa_batch_run from 8-bit images: each GPU receives its shard's pixels (a quarter
+ * of the float32 bytes for RGB), letterboxes them into the model input, runs
+ * inference and decode, and returns detections in original-image coordinates (the
+ * decode unmaps boxes with the letterbox meta, as decode_yolo(out, meta) does).
+ * The model input must be [B, 3, cfg->target_h, cfg->target_w]. out_meta (may be
+ * NULL) receives the shared meta record. */
+ENGINE_API EngineStatus pdefa_batch_run_u8(PdefaBatchRunner* runner, const uint8_t* images, int64_t n_images,
+                                           int32_t src_h, int32_t src_w, int32_t channels,
+                                           const PdefaPreprocessConfig* cfg, double conf_thres, double iou_thres,
+                                           int32_t max_det, int32_t* out_counts, PdefaDetection* out_dets,
+                                           PdefaPreprocessMeta* out_meta);
+
 #ifdef __cplusplus
 }
 #endif

@@ -10,7 +10,7 @@ from .api import (  # noqa: F401
     BF16, FP32, TF32,
     Box, Context, EngineModel, Model, PdefaError, PreprocessMeta, Session, Tensor, TensorInfo,
     _model_input_shape, cpu_brand, decode_yolo, decode_yolo_arrays, device_count, empty, from_list,
-    load, load_image, load_image_as_tensor, map_box_to_original, map_point_to_original, ones,
+    letterbox_meta, letterbox_u8, load, load_image, load_image_as_tensor, map_box_to_original, map_point_to_original, ones,
     ops_add, ops_argmax, ops_clip, ops_concat, ops_div, ops_gather, ops_gelu, ops_matmul, ops_mul,
     ops_reduce_max, ops_reduce_mean, ops_reduce_sum, ops_relu, ops_reshape, ops_sigmoid, ops_silu,
     ops_softmax, ops_stack, ops_sub, ops_tanh, ops_transpose, prepare_for_engine, prepare_for_model,
@@ -24,6 +24,7 @@ __all__ = [
     "version", "simd_level", "cpu_brand", "device_count",
     "load_image", "preprocess_letterbox", "prepare_for_engine", "load_image_as_tensor",
     "map_box_to_original", "map_point_to_original", "decode_yolo", "decode_yolo_arrays", "prepare_for_model",
+    "letterbox_u8", "letterbox_meta",
     "ops_matmul", "ops_relu", "ops_silu", "tensor_empty",
     "ops_add", "ops_sub", "ops_mul", "ops_div",
     "ops_sigmoid", "ops_tanh", "ops_gelu", "ops_clip", "ops_softmax",

@@ -17,6 +17,11 @@ i32, i64, u64, f32, f64, sz = C.c_int32, C.c_int64, C.c_uint64, C.c_float, C.c_d
 P = C.POINTER
 
 
+class PreConfig(C.Structure):
+    """PdefaPreprocessConfig (pdefa/include/pdefa_c_api.h:49-54)."""
+    _fields_ = [("target_w", i32), ("target_h", i32), ("scale", f32), ("pad_value", f32)]
+
+
 class PreMeta(C.Structure):
     """PdefaPreprocessMeta (pdefa/include/pdefa_c_api.h:56-62)."""
     _fields_ = [("target_w", i32), ("target_h", i32), ("orig_w", i32), ("orig_h", i32),
@@ -111,6 +116,11 @@ _SIGS = {
     "pdefa_batch_create": ([vp, i32, P(i32), i32, i64, P(vp)], C.c_int),
     "pdefa_batch_run": ([vp, vp, i64, P(PreMeta), f64, f64, i32, P(i32), P(Detection)], C.c_int),
     "pdefa_batch_destroy": ([vp], None),
+    "pdefa_batch_run_u8": ([vp, vp, i64, i32, i32, i32, P(PreConfig), f64, f64, i32, P(i32), P(Detection),
+                            P(PreMeta)], C.c_int),
+    "pdefa_letterbox_meta": ([i32, i32, P(PreConfig), P(PreMeta)], C.c_int),
+    "pdefa_letterbox_device": ([vp, i64, i32, i32, i32, P(PreConfig), vp, vp], C.c_int),
+    "pdefa_letterbox": ([vp, i64, i32, i32, i32, P(PreConfig), vp, P(PreMeta), i32], C.c_int),
 }
 
 _lib = None

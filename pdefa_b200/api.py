@@ -10,7 +10,9 @@ Differences from the reference:
 * Context.set_precision / set_device select strict FP32, TF32 or BF16 arithmetic
   and the GPU; Session.run_device runs on device pointers;
 * image decoding is not part of this library: load_image / prepare_for_engine
-  raise PdefaError (pass NCHW float arrays instead).
+  raise PdefaError; decoded 8-bit images are letterboxed on the GPU by
+  letterbox_u8 (bit-identical to the reference's preprocess_letterbox) or inside
+  BatchInference.detect_u8.
 """
 from __future__ import annotations
 
@@ -575,6 +577,47 @@ def prepare_for_engine(path: str, target_w: int = 640, target_h: int = 640, scal
 
 def load_image_as_tensor(path: str, target_w: int = 640, target_h: int = 640):
     raise PdefaError("load_image_as_tensor: image decoding is not part of the pdefa B200 library")
+
+
+def _u8_batch(images):
+    """[h, w] (gray), [h, w, C], [N, h, w] (gray) or [N, h, w, C] uint8 ->
+    ([N, h, w, C] array, C); a 3-D array whose last extent is 1, 3 or 4 is one image."""
+    import numpy as np
+    a = np.ascontiguousarray(images, dtype=np.uint8)
+    if a.ndim == 2:
+        a = a[None, :, :, None]
+    elif a.ndim == 3:
+        a = a[None] if a.shape[2] in (1, 3, 4) else a[..., None]
+    if a.ndim != 4 or a.shape[3] not in (1, 3, 4):
+        raise PdefaError("letterbox: images must be uint8 [h, w], [h, w, C] or [N, h, w, C] with C = 1, 3 or 4")
+    return np.ascontiguousarray(a), int(a.shape[3])
+
+
+def letterbox_meta(src_w: int, src_h: int, target_w: int = 640, target_h: int = 640, scale: float = 1.0 / 255.0,
+                   pad_value: float = 0.0) -> PreprocessMeta:
+    """Letterbox geometry of a src_w x src_h image (imageloader/src/preprocess.cpp:22-41)."""
+    m = N.PreMeta()
+    _check(N.lib().pdefa_letterbox_meta(int(src_w), int(src_h), C.byref(N.PreConfig(target_w, target_h, scale,
+                                                                                        pad_value)), C.byref(m)),
+           "letterbox_meta")
+    return PreprocessMeta.from_c(m)
+
+
+def letterbox_u8(images, target_w: int = 640, target_h: int = 640, scale: float = 1.0 / 255.0,
+                 pad_value: float = 0.0, device: int = 0):
+    """GPU letterbox of decoded 8-bit images -> (float32 [N, 3, target_h, target_w]
+    numpy array, PreprocessMeta). images: [h, w] gray, [h, w, C] or [N, h, w, C]
+    uint8 with C = 1, 3 or 4 (RGBA drops alpha). Bit-identical to the reference's
+    preprocess_letterbox (imageloader/src/preprocess.cpp:15-147)."""
+    import numpy as np
+    a, ch = _u8_batch(images)
+    n, h, w = a.shape[:3]
+    out = np.empty((n, 3, target_h, target_w), np.float32)
+    m = N.PreMeta()
+    _check(N.lib().pdefa_letterbox(a.ctypes.data, n, h, w, ch, C.byref(N.PreConfig(target_w, target_h, scale,
+                                                                                     pad_value)),
+                                   out.ctypes.data, C.byref(m), int(device)), "letterbox")
+    return out, PreprocessMeta.from_c(m)
 
 
 def map_box_to_original(box: Box, meta: PreprocessMeta) -> Box:

@@ -5,8 +5,9 @@ CPU. Here one replica of the model lives on each selected GPU; a batch of images
 split into contiguous shards, each GPU runs its shard in micro-batches of
 `batch_size` images (batched forward pass plus the GPU decode/NMS), and only
 detections come back. There is no collective. The C++ runner (pdefa_batch_run)
-drives all GPUs from native threads and pipelines each GPU's micro-batches over two
-streams: the copy of micro-batch i+1 onto the GPU overlaps the inference of i.
+drives all GPUs from native threads and pipelines each GPU's micro-batches over
+three streams: the copy of micro-batch i+1 onto the GPU and the decode of i-1 overlap
+the inference of i.
 """
 from __future__ import annotations
 
@@ -64,6 +65,31 @@ class BatchInference:
                                        md, counts.ctypes.data_as(C.POINTER(N.i32)),
                                        dets.ctypes.data_as(C.POINTER(N.Detection))), "batch_run")
         return counts[:n], dets[:n, :md]
+
+    def detect_u8(self, images, target_w: int = 640, target_h: int = 640, scale: float = 1.0 / 255.0,
+                  pad_value: float = 0.0, conf_thres: float = 0.25, iou_thres: float = 0.45, max_det: int = 300):
+        """Decoded 8-bit images -> (counts, dets, meta) like detect_arrays, boxes in
+        original-image coordinates. images: [N, h, w, C] (C = 1, 3, 4) or [N, h, w]
+        uint8, all of one size. Each GPU receives the pixels (a quarter of the float32
+        bytes for RGB), letterboxes them into the model input exactly as the
+        reference's preprocess_letterbox does, runs inference and decode with the
+        letterbox meta (decode_yolo(out, meta))."""
+        import numpy as np
+        a = np.ascontiguousarray(images, dtype=np.uint8)
+        if a.ndim == 3:
+            a = a[..., None]
+        if a.ndim != 4 or a.shape[3] not in (1, 3, 4):
+            raise PdefaError("detect_u8: images must be uint8 [N, h, w] or [N, h, w, C] with C = 1, 3 or 4")
+        n, h, w, ch = a.shape
+        md = max(int(max_det), 0)
+        counts = np.zeros(max(n, 1), dtype=np.int32)
+        dets = np.zeros((max(n, 1), max(md, 1)), dtype=self.DET_DTYPE)
+        m = N.PreMeta()
+        cfg = N.PreConfig(int(target_w), int(target_h), float(scale), float(pad_value))
+        _check(N.lib().pdefa_batch_run_u8(self._handle, a.ctypes.data, n, h, w, ch, C.byref(cfg), float(conf_thres),
+                                          float(iou_thres), md, counts.ctypes.data_as(C.POINTER(N.i32)),
+                                          dets.ctypes.data_as(C.POINTER(N.Detection)), C.byref(m)), "batch_run_u8")
+        return counts[:n], dets[:n, :md], PreprocessMeta.from_c(m)
 
     def detect(self, images, metas: Optional[Sequence[PreprocessMeta]] = None, conf_thres: float = 0.25,
                iou_thres: float = 0.45, max_det: int = 300) -> List[List[dict]]:

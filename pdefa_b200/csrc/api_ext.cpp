@@ -72,14 +72,17 @@ struct PdefaBatchRunner {
         int32_t* h_counts = nullptr; // pinned host mirrors
         PdefaDetection* h_dets = nullptr;
         size_t dets_cap = 0;
-        cudaEvent_t h2d = nullptr, done = nullptr;
+        cudaEvent_t h2d = nullptr, ran = nullptr, done = nullptr;
         bool busy = false;           // results of (c0, nb) pending
         int64_t c0 = 0, nb = 0;
+        void* pixels = nullptr;      // device copy of an 8-bit micro-batch (pdefa_batch_run_u8)
+        size_t pixels_cap = 0;
     };
     struct Replica {
         int device = 0;
-        cudaStream_t stream = nullptr;   // inference + decode + result copies
+        cudaStream_t stream = nullptr;   // letterbox + inference
         cudaStream_t copy = nullptr;     // image copies onto the GPU
+        cudaStream_t post = nullptr;     // decode + result copies (overlap the next inference)
         Lane lanes[2];
     };
     std::shared_ptr<const Graph> graph;
@@ -93,6 +96,9 @@ namespace {
 void free_lane(PdefaBatchRunner::Lane& l) {
     if (l.counts) { cudaFree(l.counts); cudaFree(l.dets); cudaFree(l.work); cudaFree(l.meta); }
     if (l.h_counts) { cudaFreeHost(l.h_counts); cudaFreeHost(l.h_dets); }
+    if (l.pixels) cudaFree(l.pixels);
+    l.pixels = nullptr;
+    l.pixels_cap = 0;
     l.counts = l.dets = l.work = l.meta = nullptr;
     l.h_counts = nullptr;
     l.h_dets = nullptr;
@@ -325,8 +331,10 @@ ENGINE_API EngineStatus pdefa_batch_create(EngineModel* model, int32_t n_devices
             PB_CUDA(cudaSetDevice(rp.device));
             PB_CUDA(cudaStreamCreateWithFlags(&rp.stream, cudaStreamNonBlocking));
             PB_CUDA(cudaStreamCreateWithFlags(&rp.copy, cudaStreamNonBlocking));
+            PB_CUDA(cudaStreamCreateWithFlags(&rp.post, cudaStreamNonBlocking));
             for (auto& l : rp.lanes) {
                 PB_CUDA(cudaEventCreateWithFlags(&l.h2d, cudaEventDisableTiming));
+                PB_CUDA(cudaEventCreateWithFlags(&l.ran, cudaEventDisableTiming));
                 PB_CUDA(cudaEventCreateWithFlags(&l.done, cudaEventDisableTiming));
             }
         }
@@ -335,10 +343,32 @@ ENGINE_API EngineStatus pdefa_batch_create(EngineModel* model, int32_t n_devices
     });
 }
 
-ENGINE_API EngineStatus pdefa_batch_run(PdefaBatchRunner* r, const float* images, int64_t n_images,
-                                        const PdefaPreprocessMeta* metas, double conf_thres, double iou_thres,
-                                        int32_t max_det, int32_t* out_counts, PdefaDetection* out_dets) {
-    if (!r || !images || !out_counts || (!out_dets && max_det > 0)) return ENGINE_ERR_NULL_PTR;
+}  // extern "C"
+
+namespace {
+
+// What pdefa_batch_run / pdefa_batch_run_u8 feed the runner: float32 model inputs, or
+// 8-bit images letterboxed on the GPU.
+struct BatchInput {
+    const float* f32 = nullptr;
+    const uint8_t* u8 = nullptr;
+    int channels = 0;
+    LetterboxGeom geo{};
+};
+
+PdefaPreprocessMeta meta_of(const LetterboxGeom& g) {
+    PdefaPreprocessMeta m;
+    m.target_w = g.W; m.target_h = g.H;
+    m.orig_w = g.src_w; m.orig_h = g.src_h;
+    m.pad_x = g.px; m.pad_y = g.py;
+    m.scaled_w = g.sw; m.scaled_h = g.sh;
+    m.ratio = g.ratio;
+    return m;
+}
+
+EngineStatus run_batch(PdefaBatchRunner* r, const BatchInput& in, int64_t n_images, const PdefaPreprocessMeta* metas,
+                       double conf_thres, double iou_thres, int32_t max_det, int32_t* out_counts,
+                       PdefaDetection* out_dets) {
     return guarded([&]() -> EngineStatus {
         clear_error();
         if (max_det < 0) return ENGINE_ERR_INVALID_ARG;
@@ -389,19 +419,44 @@ ENGINE_API EngineStatus pdefa_batch_run(PdefaBatchRunner* r, const float* images
                             l.dets_cap = need;
                         }
                         const size_t ibytes = p.input_bytes(0);
-                        PB_CUDA(cudaMemcpyAsync(p.input_buffer(0), images + c0 * (ibytes / 4 / nb), ibytes,
-                                                cudaMemcpyHostToDevice, rp.copy));
-                        PB_CUDA(cudaEventRecord(l.h2d, rp.copy));
-                        PB_CUDA(cudaStreamWaitEvent(rp.stream, l.h2d, 0));
+                        if (in.f32) {
+                            PB_CUDA(cudaMemcpyAsync(p.input_buffer(0), in.f32 + c0 * (ibytes / 4 / nb), ibytes,
+                                                    cudaMemcpyHostToDevice, rp.copy));
+                            PB_CUDA(cudaEventRecord(l.h2d, rp.copy));
+                            PB_CUDA(cudaStreamWaitEvent(rp.stream, l.h2d, 0));
+                        } else {
+                            // 8-bit pixels cross PCIe (a quarter of the float32 bytes for RGB) and
+                            // are letterboxed into the plan's input on the GPU
+                            if (ibytes != (size_t)nb * 3 * in.geo.H * in.geo.W * sizeof(float))
+                                fail(ENGINE_ERR_INVALID_SHAPE, "batch_run_u8: the model input is not [B, 3, target_h, target_w]");
+                            const size_t pb_img = (size_t)in.geo.src_h * in.geo.src_w * in.channels;
+                            if (l.pixels_cap < pb_img * r->max_per_device) {
+                                if (l.pixels) cudaFree(l.pixels);
+                                l.pixels = nullptr;
+                                l.pixels_cap = 0;
+                                PB_CUDA(cudaMalloc(&l.pixels, pb_img * r->max_per_device));
+                                l.pixels_cap = pb_img * r->max_per_device;
+                            }
+                            PB_CUDA(cudaMemcpyAsync(l.pixels, in.u8 + c0 * pb_img, pb_img * nb, cudaMemcpyHostToDevice,
+                                                    rp.copy));
+                            PB_CUDA(cudaEventRecord(l.h2d, rp.copy));
+                            PB_CUDA(cudaStreamWaitEvent(rp.stream, l.h2d, 0));
+                            launch_letterbox_u8(static_cast<const uint8_t*>(l.pixels), nb, in.channels, in.geo,
+                                                p.input_buffer(0), rp.stream);
+                        }
                         p.run(rp.stream);
+                        // decode on its own stream: one CTA per image leaves most SMs to the
+                        // next micro-batch's convolutions
+                        PB_CUDA(cudaEventRecord(l.ran, rp.stream));
+                        PB_CUDA(cudaStreamWaitEvent(rp.post, l.ran, 0));
                         decode_on_device(p.output_buffer(0), nb, ch, A, metas ? metas + c0 : nullptr, conf_thres,
                                          iou_thres, max_det, static_cast<int32_t*>(l.counts), l.dets, l.work,
-                                         static_cast<int32_t*>(l.meta), device_error_word(rp.device), rp.stream);
-                        PB_CUDA(cudaMemcpyAsync(l.h_counts, l.counts, nb * 4, cudaMemcpyDeviceToHost, rp.stream));
+                                         static_cast<int32_t*>(l.meta), device_error_word(rp.device), rp.post);
+                        PB_CUDA(cudaMemcpyAsync(l.h_counts, l.counts, nb * 4, cudaMemcpyDeviceToHost, rp.post));
                         if (max_det > 0)
                             PB_CUDA(cudaMemcpyAsync(l.h_dets, l.dets, (size_t)nb * max_det * sizeof(PdefaDetection),
-                                                    cudaMemcpyDeviceToHost, rp.stream));
-                        PB_CUDA(cudaEventRecord(l.done, rp.stream));
+                                                    cudaMemcpyDeviceToHost, rp.post));
+                        PB_CUDA(cudaEventRecord(l.done, rp.post));
                         l.busy = true;
                         l.c0 = c0;
                         l.nb = nb;
@@ -418,6 +473,7 @@ ENGINE_API EngineStatus pdefa_batch_run(PdefaBatchRunner* r, const float* images
                     }
                     cudaStreamSynchronize(rp.copy);
                     cudaStreamSynchronize(rp.stream);
+                    cudaStreamSynchronize(rp.post);
                 }
             });
         }
@@ -428,20 +484,122 @@ ENGINE_API EngineStatus pdefa_batch_run(PdefaBatchRunner* r, const float* images
     });
 }
 
+
+}  // namespace
+
+extern "C" {
+
+ENGINE_API EngineStatus pdefa_batch_run(PdefaBatchRunner* r, const float* images, int64_t n_images,
+                                        const PdefaPreprocessMeta* metas, double conf_thres, double iou_thres,
+                                        int32_t max_det, int32_t* out_counts, PdefaDetection* out_dets) {
+    if (!r || !images || !out_counts || (!out_dets && max_det > 0)) return ENGINE_ERR_NULL_PTR;
+    BatchInput in;
+    in.f32 = images;
+    return run_batch(r, in, n_images, metas, conf_thres, iou_thres, max_det, out_counts, out_dets);
+}
+
+ENGINE_API EngineStatus pdefa_batch_run_u8(PdefaBatchRunner* r, const uint8_t* images, int64_t n_images, int32_t src_h,
+                                           int32_t src_w, int32_t channels, const PdefaPreprocessConfig* cfg,
+                                           double conf_thres, double iou_thres, int32_t max_det, int32_t* out_counts,
+                                           PdefaDetection* out_dets, PdefaPreprocessMeta* out_meta) {
+    if (!r || !images || !cfg || !out_counts || (!out_dets && max_det > 0)) return ENGINE_ERR_NULL_PTR;
+    return guarded([&]() -> EngineStatus {
+        clear_error();
+        if (src_h <= 0 || src_w <= 0 || cfg->target_w <= 0 || cfg->target_h <= 0 ||
+            (channels != 1 && channels != 3 && channels != 4)) {
+            set_error("batch_run_u8: bad image size, target or channel count");
+            return ENGINE_ERR_INVALID_ARG;
+        }
+        BatchInput in;
+        in.u8 = images;
+        in.channels = channels;
+        in.geo = letterbox_geometry(src_w, src_h, cfg->target_w, cfg->target_h, cfg->scale, cfg->pad_value);
+        const PdefaPreprocessMeta m = meta_of(in.geo);
+        if (out_meta) *out_meta = m;
+        // boxes come back in original-image coordinates, as decode_yolo(out, meta) gives them
+        std::vector<PdefaPreprocessMeta> metas((size_t)std::max<int64_t>(n_images, 1), m);
+        return run_batch(r, in, n_images, metas.data(), conf_thres, iou_thres, max_det, out_counts, out_dets);
+    });
+}
+
+ENGINE_API EngineStatus pdefa_letterbox_meta(int32_t src_w, int32_t src_h, const PdefaPreprocessConfig* cfg,
+                                             PdefaPreprocessMeta* out_meta) {
+    if (!cfg || !out_meta) return ENGINE_ERR_NULL_PTR;
+    if (src_w <= 0 || src_h <= 0 || cfg->target_w <= 0 || cfg->target_h <= 0) return ENGINE_ERR_INVALID_ARG;
+    *out_meta = meta_of(letterbox_geometry(src_w, src_h, cfg->target_w, cfg->target_h, cfg->scale, cfg->pad_value));
+    return ENGINE_OK;
+}
+
+ENGINE_API EngineStatus pdefa_letterbox_device(const uint8_t* d_images, int64_t n, int32_t src_h, int32_t src_w,
+                                               int32_t channels, const PdefaPreprocessConfig* cfg, float* d_out,
+                                               void* stream) {
+    if (!d_images || !cfg || !d_out) return ENGINE_ERR_NULL_PTR;
+    return guarded([&]() -> EngineStatus {
+        clear_error();
+        if (n < 0 || src_h <= 0 || src_w <= 0 || cfg->target_w <= 0 || cfg->target_h <= 0 ||
+            (channels != 1 && channels != 3 && channels != 4)) {
+            set_error("letterbox: bad image size, target or channel count");
+            return ENGINE_ERR_INVALID_ARG;
+        }
+        const LetterboxGeom g = letterbox_geometry(src_w, src_h, cfg->target_w, cfg->target_h, cfg->scale,
+                                                   cfg->pad_value);
+        for (int64_t b0 = 0; b0 < n; b0 += 65535)
+            launch_letterbox_u8(d_images + (size_t)b0 * src_h * src_w * channels, std::min<int64_t>(65535, n - b0),
+                                channels, g, d_out + (size_t)b0 * 3 * g.H * g.W, static_cast<cudaStream_t>(stream));
+        return ENGINE_OK;
+    });
+}
+
+ENGINE_API EngineStatus pdefa_letterbox(const uint8_t* images, int64_t n, int32_t src_h, int32_t src_w,
+                                        int32_t channels, const PdefaPreprocessConfig* cfg, float* out,
+                                        PdefaPreprocessMeta* out_meta, int32_t device) {
+    if (!images || !cfg || !out) return ENGINE_ERR_NULL_PTR;
+    return guarded([&]() -> EngineStatus {
+        clear_error();
+        if (n < 0 || src_h <= 0 || src_w <= 0 || cfg->target_w <= 0 || cfg->target_h <= 0 ||
+            (channels != 1 && channels != 3 && channels != 4)) {
+            set_error("letterbox: bad image size, target or channel count");
+            return ENGINE_ERR_INVALID_ARG;
+        }
+        const LetterboxGeom g = letterbox_geometry(src_w, src_h, cfg->target_w, cfg->target_h, cfg->scale,
+                                                   cfg->pad_value);
+        if (out_meta) *out_meta = meta_of(g);
+        if (n == 0) return ENGINE_OK;
+        require_device(device);
+        PB_CUDA(cudaSetDevice(device));
+        cudaStream_t s;
+        PB_CUDA(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
+        struct SG { cudaStream_t s; ~SG() { cudaStreamSynchronize(s); cudaStreamDestroy(s); } } sg{s};
+        const size_t ib = (size_t)n * src_h * src_w * channels, ob = (size_t)n * 3 * g.H * g.W * sizeof(float);
+        DeviceBuffer din(ib), dout(ob);
+        PB_CUDA(cudaMemcpyAsync(din.p, images, ib, cudaMemcpyHostToDevice, s));
+        for (int64_t b0 = 0; b0 < n; b0 += 65535)
+            launch_letterbox_u8(static_cast<const uint8_t*>(din.p) + (size_t)b0 * src_h * src_w * channels,
+                                std::min<int64_t>(65535, n - b0), channels, g,
+                                static_cast<float*>(dout.p) + (size_t)b0 * 3 * g.H * g.W, s);
+        PB_CUDA(cudaMemcpyAsync(out, dout.p, ob, cudaMemcpyDeviceToHost, s));
+        PB_CUDA(cudaStreamSynchronize(s));
+        return ENGINE_OK;
+    });
+}
+
 ENGINE_API void pdefa_batch_destroy(PdefaBatchRunner* r) {
     if (!r) return;
     for (auto& rp : r->reps) {
         cudaSetDevice(rp.device);
         if (rp.stream) cudaStreamSynchronize(rp.stream);
         if (rp.copy) cudaStreamSynchronize(rp.copy);
+        if (rp.post) cudaStreamSynchronize(rp.post);
         for (auto& l : rp.lanes) {
             l.plans.clear();
             free_lane(l);
             if (l.h2d) cudaEventDestroy(l.h2d);
+            if (l.ran) cudaEventDestroy(l.ran);
             if (l.done) cudaEventDestroy(l.done);
         }
         if (rp.stream) cudaStreamDestroy(rp.stream);
         if (rp.copy) cudaStreamDestroy(rp.copy);
+        if (rp.post) cudaStreamDestroy(rp.post);
     }
     delete r;
 }

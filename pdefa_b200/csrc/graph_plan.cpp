@@ -1425,6 +1425,7 @@ Plan::~Plan() {
     cudaSetDevice(device_);
     for (auto& p : pending_) { cudaEventDestroy(p.second.first); cudaEventDestroy(p.second.second); }
     for (auto e : ev_pool_) cudaEventDestroy(e);
+    if (gexec_) cudaGraphExecDestroy(gexec_);
     for (void* p : allocs_) cudaFree(p);
     cudaSetDevice(prev);
 }
@@ -1450,9 +1451,7 @@ void Plan::build() {
     b.build();
 }
 
-void Plan::run(cudaStream_t s, const float* in_override, float* out_override) {
-    (void)out_override;
-    cur_in_ = in_override;
+void Plan::run_steps(cudaStream_t s) {
     for (size_t i = 0; i < steps_.size(); ++i) {
         if (timing_) {
             cudaEvent_t a = take_event(), b = take_event();
@@ -1464,7 +1463,55 @@ void Plan::run(cudaStream_t s, const float* in_override, float* out_override) {
             steps_[i].run(s);
         }
     }
-    cur_in_ = nullptr;
+}
+
+void Plan::run(cudaStream_t s, const float* in_override, float* out_override) {
+    (void)out_override;
+    cur_in_ = in_override;
+    struct Reset { const float*& p; ~Reset() { p = nullptr; } } reset{cur_in_};
+    // Eager: timed runs, the legacy default stream (cannot be captured), the first run.
+    if (timing_ || !graphs_ || s == nullptr || eager_runs_ < 1) {
+        run_steps(s);
+        if (!timing_) ++eager_runs_;
+        return;
+    }
+    if (gexec_ && g_in_ == in_override) {
+        PB_CUDA(cudaGraphLaunch(gexec_, s));
+        return;
+    }
+    if (gexec_) {
+        cudaGraphExecDestroy(gexec_);
+        gexec_ = nullptr;
+    }
+    // Capture the launch sequence (kernel parameters, tensor maps included, are
+    // copied into the graph), then replay it. Any failure falls back to eager runs.
+    cudaGraph_t graph = nullptr;
+    if (cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+        cudaGetLastError();
+        graphs_ = false;
+        run_steps(s);
+        return;
+    }
+    try {
+        run_steps(s);
+    } catch (...) {
+        cudaStreamEndCapture(s, &graph);
+        if (graph) cudaGraphDestroy(graph);
+        cudaGetLastError();
+        throw;
+    }
+    cudaError_t e = cudaStreamEndCapture(s, &graph);
+    if (e == cudaSuccess) e = cudaGraphInstantiate(&gexec_, graph, 0);
+    if (graph) cudaGraphDestroy(graph);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        gexec_ = nullptr;
+        graphs_ = false;
+        run_steps(s);
+        return;
+    }
+    g_in_ = in_override;
+    PB_CUDA(cudaGraphLaunch(gexec_, s));
 }
 
 cudaEvent_t Plan::take_event() {

@@ -101,6 +101,14 @@ private:
     std::vector<std::vector<int64_t>> out_shapes_;
     std::vector<PlanStep> steps_;
     bool timing_ = false;
+    // CUDA graph of the launch sequence: captured on the second untimed run (the
+    // first, eager one makes every lazy allocation and attribute call) and replayed
+    // while the input buffer stays the same.
+    bool graphs_ = true;
+    int eager_runs_ = 0;
+    cudaGraphExec_t gexec_ = nullptr;
+    const float* g_in_ = nullptr;
+    void run_steps(cudaStream_t s);
     std::vector<cudaEvent_t> ev_pool_;
     std::vector<std::pair<int, std::pair<cudaEvent_t, cudaEvent_t>>> pending_;
     std::vector<double> step_ms_;

@@ -140,4 +140,15 @@ struct DecodeArgs {
 size_t decode_work_bytes(int64_t batch, int64_t anchors);
 void launch_decode_nms(const DecodeArgs& a, cudaStream_t s);
 
+// Letterbox preprocess geometry (imageloader/src/preprocess.cpp:22-54): target W x H,
+// source src_w x src_h, scaled size sw x sh placed at (px, py), inv = 1 / ratio.
+struct LetterboxGeom {
+    int W, H, src_w, src_h, sw, sh, px, py;
+    float ratio, inv, scale, pad;
+};
+LetterboxGeom letterbox_geometry(int src_w, int src_h, int W, int H, float scale, float pad);
+// d_src: [n, src_h, src_w, channels] uint8 (channels 1, 3 or 4) -> d_out [n, 3, H, W] f32.
+void launch_letterbox_u8(const uint8_t* d_src, int64_t n, int channels, const LetterboxGeom& g, float* d_out,
+                         cudaStream_t s);
+
 }  // namespace pb
