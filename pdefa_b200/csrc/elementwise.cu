@@ -312,6 +312,114 @@ __global__ void maxpool_vec_kernel(Pool2dArgs a, int64_t total, int vec) {
     }
 }
 
+// Stride-1 max pooling of one image's channel slice held in shared memory
+// (SPPF: 5x5, pad 2, on 20x20 maps): a row pass then a column pass over 16-byte
+// channel cells. Every window keeps at least one in-image tap (pad < k), so the
+// separable result is the 2-D window maximum exactly; values compare as float with
+// the reference's -FLT_MAX start (pooling.cpp:35-101), and are stored in the source
+// type (a maximum is one of its inputs, so nothing rounds).
+template <bool BF>
+__device__ __forceinline__ void cell_max(float* best, uint4 q) {
+    if (BF) {
+        const uint32_t u[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const __nv_bfloat162 h2 = *reinterpret_cast<const __nv_bfloat162*>(&u[j]);
+            const float lo = __low2float(h2), hi = __high2float(h2);
+            if (lo > best[2 * j]) best[2 * j] = lo;
+            if (hi > best[2 * j + 1]) best[2 * j + 1] = hi;
+        }
+    } else {
+        const float f[4] = {__uint_as_float(q.x), __uint_as_float(q.y), __uint_as_float(q.z), __uint_as_float(q.w)};
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            if (f[j] > best[j]) best[j] = f[j];
+    }
+}
+
+template <bool BF>
+__device__ __forceinline__ uint4 cell_pack(const float* best) {
+    if (BF) {
+        uint32_t u[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            __nv_bfloat162 h2 = __floats2bfloat162_rn(best[2 * j], best[2 * j + 1]);
+            u[j] = *reinterpret_cast<uint32_t*>(&h2);
+        }
+        return make_uint4(u[0], u[1], u[2], u[3]);
+    }
+    return make_uint4(__float_as_uint(best[0]), __float_as_uint(best[1]), __float_as_uint(best[2]),
+                      __float_as_uint(best[3]));
+}
+
+template <bool BF>
+__global__ void __launch_bounds__(256) maxpool_s1_tile_kernel(Pool2dArgs a, int gc) {
+    extern __shared__ uint4 cells[];        // [H][W][gc] input, then [H][Wo][gc] row maxima
+    constexpr int kVec = BF ? 8 : 4;
+    constexpr int kEsz = BF ? 2 : 4;
+    const int H = (int)a.in.shape[1], W = (int)a.in.shape[2];
+    const int Ho = (int)a.out.shape[1], Wo = (int)a.out.shape[2];
+    uint4* const rows = cells + H * W * gc;
+    const int64_t b = blockIdx.y;
+    const int g0 = blockIdx.x * gc;
+    const char* const in = static_cast<const char*>(a.in.ptr) + (b * a.in.img_stride + (int64_t)g0 * kVec) * kEsz;
+    char* const out = static_cast<char*>(const_cast<void*>(a.out.ptr)) + (b * a.out.img_stride + (int64_t)g0 * kVec) * kEsz;
+    for (int i = threadIdx.x; i < H * W * gc; i += blockDim.x) {
+        const int c = i % gc, pix = i / gc, h = pix / W, w = pix - h * W;
+        cells[i] = *reinterpret_cast<const uint4*>(in + (h * a.in.stride[1] + w * a.in.stride[2] + c * kVec) * kEsz);
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < H * Wo * gc; i += blockDim.x) {
+        const int c = i % gc, pix = i / gc, h = pix / Wo, wo = pix - h * Wo;
+        float best[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) best[j] = -FLT_MAX;
+        const int w0 = wo - a.pw;
+        for (int k = 0; k < a.kw; ++k) {
+            const int w = w0 + k;
+            if (w >= 0 && w < W) cell_max<BF>(best, cells[(h * W + w) * gc + c]);
+        }
+        rows[i] = cell_pack<BF>(best);
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < Ho * Wo * gc; i += blockDim.x) {
+        const int c = i % gc, pix = i / gc, ho = pix / Wo, wo = pix - ho * Wo;
+        float best[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) best[j] = -FLT_MAX;
+        const int h0 = ho - a.ph;
+        for (int k = 0; k < a.kh; ++k) {
+            const int h = h0 + k;
+            if (h >= 0 && h < H) cell_max<BF>(best, rows[(h * Wo + wo) * gc + c]);
+        }
+        *reinterpret_cast<uint4*>(out + (ho * a.out.stride[1] + wo * a.out.stride[2] + c * kVec) * kEsz) =
+            cell_pack<BF>(best);
+    }
+}
+
+// Nearest 2x upsample (out(h, w) = in(h / 2, w / 2), the reference's floor(h * Hin / H)
+// for an exact factor of two): one thread reads one 16-byte channel cell and writes
+// it to its four output pixels.
+__global__ void resize_nearest_2x_kernel(TView in, TView out, int cells, int G, int Wi, int Hi, int esz, int vec) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < cells; i += gridDim.x * blockDim.x) {
+        const int g = i % G;
+        int t = i / G;
+        const int wi = t % Wi;
+        t /= Wi;
+        const int hi = t % Hi;
+        const int64_t b = t / Hi;
+        const uint4 q = *reinterpret_cast<const uint4*>(static_cast<const char*>(in.ptr) +
+            (b * in.img_stride + hi * in.stride[1] + wi * in.stride[2] + (int64_t)g * vec) * esz);
+        char* const o = static_cast<char*>(const_cast<void*>(out.ptr)) +
+                        (b * out.img_stride + (int64_t)(2 * hi) * out.stride[1] + (int64_t)(2 * wi) * out.stride[2] +
+                         (int64_t)g * vec) * esz;
+        *reinterpret_cast<uint4*>(o) = q;
+        *reinterpret_cast<uint4*>(o + out.stride[2] * esz) = q;
+        *reinterpret_cast<uint4*>(o + out.stride[1] * esz) = q;
+        *reinterpret_cast<uint4*>(o + (out.stride[1] + out.stride[2]) * esz) = q;
+    }
+}
+
 bool rows_vectorisable(const TView& in, const TView& out, int64_t* row) {
     if (in.rank < 1 || in.stride[in.rank - 1] != 1 || out.stride[out.rank - 1] != 1) return false;
     const int64_t r = in.shape[in.rank - 1];
@@ -386,6 +494,30 @@ void launch_gather(const float* data, const int64_t* idx, float* out, int64_t ou
 void launch_pool2d(const Pool2dArgs& a, cudaStream_t s) {
     const int64_t total = a.out.shape[1] * a.out.shape[2] * a.out.shape[3] * a.batch;
     if (!total) return;
+    if (a.mode == 0 && a.in.dt == a.out.dt && nhwc_vec16(a.in) && nhwc_vec16(a.out) && a.sh == 1 && a.sw == 1 &&
+        a.ph < a.kh && a.pw < a.kw && a.batch <= 65535) {
+        // one CTA per image and slice of gc channel cells, both passes in shared memory
+        const int vec = a.in.dt == BF16 ? 8 : 4;
+        const int G = (int)(a.in.shape[3] / vec);
+        const int64_t per_cell = (a.in.shape[1] * a.in.shape[2] + a.in.shape[1] * a.out.shape[2]) * 16;
+        int gc = 0;
+        for (int d = G; d >= 1; --d)
+            if (G % d == 0 && per_cell * d <= 48 * 1024) { gc = d; break; }
+        // keep at least two CTAs per SM busy
+        while (gc > 1 && (G / gc) * a.batch < 296) {
+            int d = gc - 1;
+            while (d > 1 && G % d) --d;
+            gc = d;
+        }
+        if (gc > 0) {
+            const dim3 grid((unsigned)(G / gc), (unsigned)a.batch);
+            const size_t smem = (size_t)per_cell * gc;
+            if (a.in.dt == BF16) maxpool_s1_tile_kernel<true><<<grid, 256, smem, s>>>(a, gc);
+            else maxpool_s1_tile_kernel<false><<<grid, 256, smem, s>>>(a, gc);
+            PB_CUDA(cudaGetLastError());
+            return;
+        }
+    }
     if (a.mode == 0 && a.in.dt == a.out.dt && nhwc_vec16(a.in) && nhwc_vec16(a.out)) {
         const int vec = a.in.dt == BF16 ? 8 : 4;
         maxpool_vec_kernel<<<grid_for(total / vec, 256), 256, 0, s>>>(a, total / vec, vec);
@@ -401,6 +533,16 @@ void launch_resize_nearest(const TView& in, const TView& out, int64_t batch, cud
     if (!total) return;
     const float sy = (float)in.shape[1] / (float)out.shape[1];
     const float sx = (float)in.shape[2] / (float)out.shape[2];
+    if (in.dt == out.dt && nhwc_vec16(in) && nhwc_vec16(out) && out.shape[1] == 2 * in.shape[1] &&
+        out.shape[2] == 2 * in.shape[2] && in.shape[1] * in.shape[2] * in.shape[3] * batch < (int64_t(1) << 31)) {
+        const int vec = in.dt == BF16 ? 8 : 4;
+        const int G = (int)(in.shape[3] / vec);
+        const int cells = (int)(in.shape[1] * in.shape[2] * G * batch);
+        resize_nearest_2x_kernel<<<grid_for(cells, 256), 256, 0, s>>>(in, out, cells, G, (int)in.shape[2],
+                                                                       (int)in.shape[1], in.dt == BF16 ? 2 : 4, vec);
+        PB_CUDA(cudaGetLastError());
+        return;
+    }
     if (in.dt == out.dt && nhwc_vec16(in) && nhwc_vec16(out)) {
         const int vec = in.dt == BF16 ? 8 : 4;
         resize_nearest_vec_kernel<<<grid_for(total / vec, 256), 256, 0, s>>>(in, out, total / vec, sy, sx, vec);

@@ -62,12 +62,133 @@ __global__ void yolo_head_kernel(YoloHeadArgs a) {
     }
 }
 
+// Tiled variant for the usual layout (channels contiguous, 16-byte aligned pixel
+// rows, reg_max 16): a CTA stages the logit rows of 64 consecutive anchors of one
+// image in shared memory with coalesced 16-byte loads, then each thread decodes its
+// anchor from shared memory with the arithmetic of yolo_head_kernel (same operation
+// order, so the outputs are identical) and writes its 4 + nc output rows.
+constexpr int kHeadAnchors = 64;
+
+template <bool BF>
+__device__ __forceinline__ void unpack8(uint4 q, float* f) {
+    if (BF) {
+        const uint32_t u[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const __nv_bfloat162 h2 = *reinterpret_cast<const __nv_bfloat162*>(&u[j]);
+            f[2 * j] = __low2float(h2);
+            f[2 * j + 1] = __high2float(h2);
+        }
+    } else {
+        f[0] = __uint_as_float(q.x); f[1] = __uint_as_float(q.y);
+        f[2] = __uint_as_float(q.z); f[3] = __uint_as_float(q.w);
+    }
+}
+
+template <bool BF>
+__global__ void __launch_bounds__(kHeadAnchors) yolo_head_tile_kernel(YoloHeadArgs a, int tiles, int chunks,
+                                                                      int row_chunks) {
+    constexpr int kReg = 16;
+    constexpr int kPer = BF ? 8 : 4;                   // values per 16-byte chunk
+    extern __shared__ uint4 rows[];                    // [kHeadAnchors][row_chunks]
+    __shared__ const char* src[kHeadAnchors];
+    const int j = threadIdx.x;
+    const int64_t b = blockIdx.x / tiles;
+    const int64_t i = (int64_t)(blockIdx.x - b * tiles) * kHeadAnchors + j;
+    const int64_t A = a.A;
+    const int esz = BF ? 2 : 4;
+    if (i < A) {
+        int lvl = 0;
+        int64_t li = i;
+        while (lvl < a.nlevels - 1 && li >= a.level_anchors[lvl]) { li -= a.level_anchors[lvl]; ++lvl; }
+        const TView& v = a.level[lvl];
+        const int W = (int)v.shape[2];
+        const int h = (int)(li / W), w = (int)(li - (int64_t)h * W);
+        src[j] = static_cast<const char*>(v.ptr) + (b * v.img_stride + h * v.stride[1] + w * v.stride[2]) * esz;
+    } else {
+        src[j] = nullptr;
+    }
+    __syncthreads();
+    for (int idx = j; idx < kHeadAnchors * chunks; idx += kHeadAnchors) {
+        const int r = idx / chunks, q = idx - r * chunks;
+        const char* p = src[r];
+        if (p) rows[r * row_chunks + q] = __ldg(reinterpret_cast<const uint4*>(p) + q);
+    }
+    __syncthreads();
+    if (i >= A) return;
+    const uint4* const row = rows + j * row_chunks;
+    float dist[4];
+#pragma unroll
+    for (int side = 0; side < 4; ++side) {
+        float x[kReg];
+#pragma unroll
+        for (int c = 0; c < kReg / kPer; ++c) unpack8<BF>(row[side * (kReg / kPer) + c], x + c * kPer);
+        float mx = -1e30f;
+#pragma unroll
+        for (int k = 0; k < kReg; ++k) mx = fmaxf(mx, x[k]);
+        float sum = 0.0f;
+#pragma unroll
+        for (int k = 0; k < kReg; ++k) { x[k] = expf(x[k] - mx); sum += x[k]; }
+        const float inv = sum > 0.0f ? 1.0f / sum : 0.0f;
+        float d = 0.0f;
+#pragma unroll
+        for (int k = 0; k < kReg; ++k) d = fmaf(x[k] * inv, a.dfl_w[k], d);
+        dist[side] = d;
+    }
+    const float ax = a.anchors[i], ay = a.anchors[A + i], st = a.strides[i];
+    const float x1 = __fsub_rn(ax, dist[0]), y1 = __fsub_rn(ay, dist[1]);
+    const float x2 = __fadd_rn(ax, dist[2]), y2 = __fadd_rn(ay, dist[3]);
+    const float cx = __fdiv_rn(__fadd_rn(x1, x2), 2.0f), cy = __fdiv_rn(__fadd_rn(y1, y2), 2.0f);
+    const float bw = __fsub_rn(x2, x1), bh = __fsub_rn(y2, y1);
+    float* o = a.out + b * (int64_t)(4 + a.nc) * A + i;
+    o[0] = __fmul_rn(cx, st);
+    o[A] = __fmul_rn(cy, st);
+    o[2 * A] = __fmul_rn(bw, st);
+    o[3 * A] = __fmul_rn(bh, st);
+    const int cls_chunks = a.nc / kPer;
+    for (int c = 0; c < cls_chunks; ++c) {
+        float z[kPer];
+        unpack8<BF>(row[4 * kReg / kPer + c], z);
+#pragma unroll
+        for (int e = 0; e < kPer; ++e) o[(4 + c * kPer + e) * A] = 1.0f / (1.0f + expf(-z[e]));
+    }
+}
+
+bool head_tileable(const YoloHeadArgs& a) {
+    if (a.reg_max != 16 || a.nlevels < 1 || a.nlevels > 3) return false;
+    const int dt = a.level[0].dt;
+    const int esz = dt == BF16 ? 2 : 4;
+    if (dt != BF16 && dt != F32) return false;
+    if ((a.nc * esz) % 16) return false;
+    for (int l = 0; l < a.nlevels; ++l) {
+        const TView& v = a.level[l];
+        if (v.dt != dt || v.rank != 4 || v.stride[3] != 1 || ((uintptr_t)v.ptr) % 16) return false;
+        if ((v.stride[2] * esz) % 16 || (v.stride[1] * esz) % 16 || (v.img_stride * esz) % 16) return false;
+        if (v.shape[3] < 4 * a.reg_max + a.nc) return false;
+    }
+    return true;
+}
+
 }  // namespace
 
 void launch_yolo_head(const YoloHeadArgs& a, cudaStream_t s) {
     if (a.reg_max > 32) fail(ENGINE_ERR_NOT_IMPL, "yolo head: reg_max > 32");
     const int64_t total = a.A * a.batch;
     if (!total) return;
+    if (head_tileable(a)) {
+        const bool bf = a.level[0].dt == BF16;
+        const int chunks = (4 * a.reg_max + a.nc) * (bf ? 2 : 4) / 16;
+        const int row_chunks = chunks | 1;         // odd: conflict-free 16-byte reads of one row per thread
+        const int tiles = (int)((a.A + kHeadAnchors - 1) / kHeadAnchors);
+        const int64_t blocks = (int64_t)tiles * a.batch;
+        const size_t smem = (size_t)kHeadAnchors * row_chunks * 16;
+        if (blocks < (int64_t(1) << 31) && smem <= 48 * 1024) {
+            if (bf) yolo_head_tile_kernel<true><<<(unsigned)blocks, kHeadAnchors, smem, s>>>(a, tiles, chunks, row_chunks);
+            else yolo_head_tile_kernel<false><<<(unsigned)blocks, kHeadAnchors, smem, s>>>(a, tiles, chunks, row_chunks);
+            PB_CUDA(cudaGetLastError());
+            return;
+        }
+    }
     int64_t blocks = (total + 127) / 128;
     if (blocks > 148 * 64) blocks = 148 * 64;
     yolo_head_kernel<<<(unsigned)blocks, 128, 0, s>>>(a);
