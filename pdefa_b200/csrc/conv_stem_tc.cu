@@ -258,6 +258,229 @@ __global__ void __launch_bounds__(128, 8) conv_stem_tc_kernel(const StemParams P
     }
 }
 
+// The YOLO stem (3x3, stride 2, pad 1, Cin = 3, fp32 NCHW input with rows of a
+// multiple of 4 floats) on 2-D tiles of 8 x 16 output pixels. The tile's input
+// region, 17 rows of 33 columns per channel, is copied into shared memory as 9
+// aligned 16-byte pieces per row (columns 32*tw - 4 ... 32*tw + 31; zero fill outside
+// the image) with cp.async, one tile ahead, so the copy of tile t+1 overlaps the work
+// on tile t. Thread m reads its 27 taps from shared memory at offsets fixed at compile
+// time. The A rows, MMAs and epilogue are those of conv_stem_tc_kernel, so the
+// outputs are identical; only the gather changes.
+constexpr int kTileH = 8, kTileW = 16;
+constexpr int kRegH = (kTileH - 1) * 2 + 3;     // 17 input rows
+constexpr int kRegP = 9;                         // 16-byte pieces per region row (36 floats)
+constexpr int kRegW = 4 * kRegP;
+constexpr int kRegPlane = kRegH * kRegW;
+
+struct StemTileParams {
+    ConvArgs a;
+    int Ho, Wo, K;
+    int tiles_h, tiles_w;
+    int64_t tiles;
+    int RH, RW;           // input region of one tile (rows, columns)
+    int ncols;
+    int* err;
+};
+
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src, bool in) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(in ? 4 : 0) : "memory");
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool in) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(in ? 16 : 0) : "memory");
+}
+
+// Queue the input region of tile t into region buffer dst: 3 planes x 17 rows x 9
+// pieces of 16 bytes, piece j of a row holding input columns 32*tw - 4 + 4j ... + 3.
+__device__ __forceinline__ void stem_region_load(const StemTileParams& P, int64_t t, float* dst, int H, int W) {
+    const ConvArgs& a = P.a;
+    const int64_t per_img = (int64_t)P.tiles_h * P.tiles_w;
+    const int64_t b = t / per_img;
+    const int r = (int)(t - b * per_img);
+    const int th = r / P.tiles_w, tw = r - th * P.tiles_w;
+    const int h0 = th * (2 * kTileH) - 1, c0 = tw * (2 * kTileW) - 4;
+    const float* const in = static_cast<const float*>(a.in.ptr) + b * a.in.img_stride;
+    for (int i = threadIdx.x; i < 3 * kRegH * kRegP; i += blockDim.x) {
+        const int row = i / kRegP, j = i - row * kRegP;
+        const int c = row / kRegH, y = row - c * kRegH;
+        const int hi = h0 + y, wi = c0 + 4 * j;
+        const bool ok = hi >= 0 && hi < H && wi >= 0 && wi < W;     // W % 4 == 0: pieces are all in or all out
+        const float* src = ok ? in + (int64_t)hi * a.in.stride[1] + (int64_t)c * a.in.stride[3] + wi : in;
+        cp_async16(smem_u32(dst + row * kRegW + 4 * j), src, ok);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+__global__ void __launch_bounds__(128, 8) conv_stem_tile_kernel(const StemTileParams P) {
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base = (raw + 511u) & ~511u;
+    uint8_t* const smem = smem_raw + (base - raw);
+    const ConvArgs& a = P.a;
+    const int cout = a.cout;
+    // [A: 128 rows x 64 B | B: cout rows x 64 B | region x 2 | barrier, TMEM slot, flag]
+    uint8_t* const sA = smem;
+    uint8_t* const sB = smem + kRows * kRowBytes;
+    constexpr int rbytes = 3 * kRegPlane * 4;
+    float* const sR0 = reinterpret_cast<float*>(sB + ((cout * kRowBytes + 511) & ~511));
+    float* const sR1 = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(sR0) + rbytes);
+    uint64_t* const mbar = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(sR1) + rbytes);
+    uint32_t* const tmem_slot = reinterpret_cast<uint32_t*>(mbar + 1);
+    volatile int* const abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int tid = threadIdx.x, warp = tid >> 5;
+    if (tid == 0) *abort_flag = *reinterpret_cast<volatile int*>(P.err) != 0;
+    __syncthreads();
+    if (*abort_flag) return;
+
+    const int H = (int)a.in.shape[1], W = (int)a.in.shape[2];
+    if ((int64_t)blockIdx.x < P.tiles) stem_region_load(P, blockIdx.x, sR0, H, W);
+
+    const float* w = reinterpret_cast<const float*>(a.weight);
+    for (int i = tid; i < cout * 32; i += blockDim.x) {
+        const int n = i >> 5, k = i & 31;
+        const float v = k < P.K ? w[(int64_t)k * cout + n] : 0.0f;
+        __nv_bfloat16* row = reinterpret_cast<__nv_bfloat16*>(sB + sw64_off(n, k >> 3));
+        row[k & 7] = __float2bfloat16_rn(v);
+    }
+    if (tid == 0) {
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(mbar)) : "memory");
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                     ::"r"(smem_u32(tmem_slot)), "r"(P.ncols) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(cout >> 3) << 17) | ((uint32_t)(kRows >> 4) << 24);
+
+    const int py = tid / kTileW, px = tid - py * kTileW;
+    const bool fast_epi = cout == 16 && a.act == ACT_SILU && a.out.dt == BF16 && a.out.stride[3] == 1 &&
+                          ((uintptr_t)a.out.ptr % 16) == 0 && (a.out.stride[2] % 8) == 0 && (a.out.stride[1] % 8) == 0 &&
+                          (a.out.img_stride % 8) == 0;
+    const int rbase = 2 * py * kRegW + 2 * px + 3;          // this pixel's first tap (column 2*px - 1 -> piece offset 3)
+    const int64_t per_img = (int64_t)P.tiles_h * P.tiles_w;
+    const bool vec_out = a.out.stride[3] == 1 && ((uintptr_t)a.out.ptr % 16) == 0 && (a.out.stride[2] % 8) == 0 &&
+                         (a.out.stride[1] % 8) == 0 && (a.out.img_stride % 8) == 0;
+    const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16);
+    int it = 0;
+    bool failed = false;
+    for (int64_t t = blockIdx.x; t < P.tiles; t += gridDim.x, ++it) {
+        // queue the next tile's region, then wait for this one's
+        const int64_t tn = t + gridDim.x;
+        float* const cur = (it & 1) ? sR1 : sR0;
+        float* const nxt = (it & 1) ? sR0 : sR1;
+        if (tn < P.tiles) {
+            stem_region_load(P, tn, nxt, H, W);
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+        } else {
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
+        }
+        __syncthreads();          // region visible; previous tile's TMEM reads finished
+        {
+            float v[32];
+#pragma unroll
+            for (int c = 0; c < 3; ++c)
+#pragma unroll
+                for (int kr = 0; kr < 3; ++kr)
+#pragma unroll
+                    for (int ks = 0; ks < 3; ++ks)
+                        v[(kr * 3 + ks) * 3 + c] = cur[rbase + c * kRegPlane + kr * kRegW + ks];
+#pragma unroll
+            for (int k = 27; k < 32; ++k) v[k] = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                uint32_t wd[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    __nv_bfloat162 h2 = __floats2bfloat162_rn(v[8 * j + 2 * q], v[8 * j + 2 * q + 1]);
+                    wd[q] = *reinterpret_cast<uint32_t*>(&h2);
+                }
+                *reinterpret_cast<uint4*>(sA + sw64_off(tid, j)) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        }
+        __syncthreads();          // A rows complete; region `cur` free for the load after next
+        if (tid == 0) {
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint32_t a0 = smem_u32(sA), b0 = smem_u32(sB);
+            for (int k = 0; k < 2; ++k) {
+                const uint64_t da = sw64_desc(a0 + 32u * k), db = sw64_desc(b0 + 32u * k);
+                asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                             "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+                             ::"r"(tmem), "l"(da), "l"(db), "r"(idesc), "r"(k));
+            }
+            asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                         ::"r"(smem_u32(mbar)) : "memory");
+        }
+        bool ok = mbar_wait_bounded(mbar, (uint32_t)(it & 1), 200000000LL);
+        ok = __syncthreads_and(ok);
+        if (!ok) {
+            if (tid == 0) atomicExch(P.err, 8);
+            failed = true;
+            break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const int64_t b = t / per_img;
+        const int r = (int)(t - b * per_img);
+        const int th = r / P.tiles_w, tw = r - th * P.tiles_w;
+        const int ho = th * kTileH + py, wo = tw * kTileW + px;
+        const bool live = ho < P.Ho && wo < P.Wo;
+        const int64_t ob = b * a.out.img_stride + (int64_t)ho * a.out.stride[1] + (int64_t)wo * a.out.stride[2];
+        for (int c0 = 0; c0 < cout; c0 += 16) {
+            uint32_t rr[16];
+            asm volatile(
+                "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+                : "=r"(rr[0]), "=r"(rr[1]), "=r"(rr[2]), "=r"(rr[3]), "=r"(rr[4]), "=r"(rr[5]), "=r"(rr[6]), "=r"(rr[7]),
+                  "=r"(rr[8]), "=r"(rr[9]), "=r"(rr[10]), "=r"(rr[11]), "=r"(rr[12]), "=r"(rr[13]), "=r"(rr[14]), "=r"(rr[15])
+                : "r"(taddr + (uint32_t)c0));
+            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+            if (!live) continue;
+            float o[16];
+            if (fast_epi) {
+#pragma unroll
+                for (int i = 0; i < 16; ++i)
+                    o[i] = stem_act(__uint_as_float(rr[i]) + (a.bias ? __ldg(a.bias + i) : 0.0f), ACT_SILU, 0.f);
+            } else {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    float x = __uint_as_float(rr[i]) + (a.bias ? __ldg(a.bias + c0 + i) : 0.0f);
+                    o[i] = stem_act(x, a.act, a.slope);
+                }
+            }
+            if (vec_out && a.out.dt == BF16) {
+                uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(const_cast<void*>(a.out.ptr)) + ob + c0);
+#pragma unroll
+                for (int q = 0; q < 2; ++q) {
+                    uint32_t wd[4];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        __nv_bfloat162 h2 = __floats2bfloat162_rn(o[8 * q + 2 * j], o[8 * q + 2 * j + 1]);
+                        wd[j] = *reinterpret_cast<uint32_t*>(&h2);
+                    }
+                    dst[q] = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < 16; ++i)
+                    st_elem(const_cast<void*>(a.out.ptr), a.out.dt, ob + (int64_t)(c0 + i) * a.out.stride[3], o[i]);
+            }
+        }
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    if (failed && tid == 0) mbar_wait_bounded(mbar, (uint32_t)(it & 1), 200000000LL);
+    __syncthreads();
+    if (warp == 0) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(P.ncols) : "memory");
+    }
+}
+
 }  // namespace
 
 bool conv_stem_tc_supported(const ConvArgs& a) {
@@ -274,6 +497,44 @@ void launch_conv_stem_tc(const ConvArgs& a, int* err, cudaStream_t s) {
     P.K = a.kh * a.kw * a.cin;
     P.M = a.batch * P.Ho * P.Wo;
     if (P.M == 0) return;
+    P.ncols = 32;
+    while (P.ncols < a.cout) P.ncols <<= 1;
+    int dev0 = 0;
+    PB_CUDA(cudaGetDevice(&dev0));
+    const int esz_in = 4;
+    if (a.kh == 3 && a.kw == 3 && a.cin == 3 && a.in.dt == F32 && a.sh == 2 && a.sw == 2 && a.ph == 1 && a.pw == 1 &&
+        a.dh == 1 && a.dw == 1 && a.in.stride[2] == 1 && a.in.shape[2] % 4 == 0 && ((uintptr_t)a.in.ptr % 16) == 0 &&
+        (a.in.stride[1] * esz_in) % 16 == 0 && (a.in.stride[3] * esz_in) % 16 == 0 &&
+        (a.in.img_stride * esz_in) % 16 == 0) {
+        StemTileParams T;
+        T.a = a;
+        T.Ho = P.Ho; T.Wo = P.Wo; T.K = P.K;
+        T.tiles_h = (P.Ho + kTileH - 1) / kTileH;
+        T.tiles_w = (P.Wo + kTileW - 1) / kTileW;
+        T.tiles = (int64_t)T.tiles_h * T.tiles_w * a.batch;
+        T.RH = kRegH;
+        T.RW = kRegW;
+        T.ncols = P.ncols;
+        T.err = err;
+        const size_t rbytes = (size_t)3 * kRegPlane * 4;
+        const size_t smem = 512 + kRows * kRowBytes + ((a.cout * kRowBytes + 511) & ~511) + 2 * rbytes + 64;
+        if (smem <= 48 * 1024 && T.tiles < (int64_t(1) << 40)) {
+            static int sms_t[64] = {};
+            int sms = 148;
+            if (dev0 < 64) {
+                if (!sms_t[dev0]) PB_CUDA(cudaDeviceGetAttribute(&sms_t[dev0], cudaDevAttrMultiProcessorCount, dev0));
+                sms = sms_t[dev0];
+            }
+            // resident CTAs per SM: 8 by registers (64 a thread), 228 KB of shared memory
+            // (1 KB reserved per CTA), TMEM ncols columns each within 512
+            const int by_smem = (int)((228u * 1024u) / (smem + 1024));
+            const int per_sm = std::max(1, std::min({8, by_smem, 512 / T.ncols}));
+            const int64_t grid = std::min<int64_t>(T.tiles, (int64_t)sms * per_sm);
+            conv_stem_tile_kernel<<<(unsigned)grid, 128, smem, s>>>(T);
+            PB_CUDA(cudaGetLastError());
+            return;
+        }
+    }
     P.tiles = (P.M + kRows - 1) / kRows;
     P.ncols = 32;
     while (P.ncols < a.cout) P.ncols <<= 1;
