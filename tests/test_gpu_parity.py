@@ -137,11 +137,14 @@ def test_stem_rows_kernel_batched(engine_dir, prec, cout, hw, s):
 @pytest.mark.parametrize("prec", [pb.TF32, pb.BF16])
 @pytest.mark.parametrize("cin,cout,k,s,hw", [(64, 64, 3, 1, 20), (16, 48, 3, 2, 33), (80, 80, 1, 1, 12),
                                              (80, 80, 3, 1, 20), (48, 32, 1, 1, 24), (80, 64, 3, 2, 21),
-                                             (112, 32, 3, 1, 9)])
+                                             (112, 32, 3, 1, 9), (16, 16, 3, 1, 40), (32, 32, 3, 1, 37),
+                                             (16, 32, 3, 1, 61)])
 def test_single_conv_staged_input(engine_dir, prec, cin, cout, k, s, hw):
     """A conv fed directly by the fp32 NCHW graph input: the plan stages the input into
     the operand layout and runs the tensor-core kernel (no SIMT fallback). Cin = 48,
-    80 and 112 run in BF16 as zero-padded 64-channel chunks.
+    80 and 112 run in BF16 as zero-padded 64-channel chunks; the 16- and 32-channel
+    3x3 cases run in window mode with groups of M tiles sharing one window (full and
+    partial groups).
 
     The 3x3 stride-1 case takes the reference's Winograd SiLU, which jumps by up to
     ~0.04 where round(-x*log2 e) changes; a BF16/TF32 pre-activation on the other
