@@ -143,8 +143,8 @@ def test_single_conv_staged_input(engine_dir, prec, cin, cout, k, s, hw):
     """A conv fed directly by the fp32 NCHW graph input: the plan stages the input into
     the operand layout and runs the tensor-core kernel (no SIMT fallback). Cin = 48,
     80 and 112 run in BF16 as zero-padded 64-channel chunks; the 16- and 32-channel
-    3x3 cases run in window mode with groups of M tiles sharing one window (full and
-    partial groups).
+    3x3 cases run in window mode (zero-padded row windows, taps as shifted windows)
+    at sizes whose last tile is partial.
 
     The 3x3 stride-1 case takes the reference's Winograd SiLU, which jumps by up to
     ~0.04 where round(-x*log2 e) changes; a BF16/TF32 pre-activation on the other
