@@ -35,8 +35,10 @@ constexpr int kMaxKeys = 16384;
 constexpr int kMaxClasses = 1024;
 constexpr int kSub = 256;          // boxes settled per greedy sub-block
 constexpr int kKeptSmem = 512;     // kept boxes mirrored in shared memory
-constexpr size_t kNmsSmem = kMaxKeys * 8 + 2 * kMaxClasses * 4 + (kSub + kKeptSmem) * 48 +
-                            kSub * (kSub / 32) * 4 + kSub * 4;
+// keys | class first/group | raw chunk (kSub) + pending survivors (2 kSub) + kept mirror
+// (kKeptSmem) | in-block matrix | survivor flags
+constexpr size_t kNmsSmem = kMaxKeys * 8 + 2 * kMaxClasses * 4 + (3 * kSub + kKeptSmem) * 48 +
+                            kSub * (kSub / 32) * 4 + 2 * kSub * 4;
 
 struct Det {
     double x1, y1, x2, y2;
@@ -229,46 +231,85 @@ __global__ void __launch_bounds__(kThreads, 1) decode_nms_kernel(DecodeArgs p) {
     __syncthreads();
     bitonic_sort(keys, np);
 
-    // ---- 4. one greedy pass in output order, kSub boxes at a time ----
+    // ---- 4. one greedy pass in output order ----
     // A box's same-class predecessors in the reference's per-class order all come
     // before it in this order, so deciding boxes in this order keeps exactly the
     // boxes the per-class greedy keeps, and the first max_det kept are the output.
-    // Per sub-block: (a) stage its records in shared memory; (b) mark boxes that a box
-    // kept before the sub-block suppresses; (c) build the in-block suppression matrix
-    // (bit i of row j: box i < j of the same class with IoU not <= thres); (d) one
-    // warp settles the boxes in order with that matrix; (e) append the kept ones.
-    Det* sub = reinterpret_cast<Det*>(grp + kMaxClasses);              // kSub
-    Det* kept_s = sub + kSub;                                          // kKeptSmem
+    // Rounds: (a) raw chunks of kSub boxes in order are tested against every box kept
+    // so far (one warp per box, lanes over the kept ones) and the survivors appended,
+    // in order, to a pending list until it holds kSub boxes or the order is exhausted;
+    // (b) the in-block suppression matrix of the first m <= kSub pending boxes (bit i of
+    // row j: box i < j of the same class with IoU not <= thres); (c) one warp settles
+    // them in order with the matrix; (d) kept ones are appended to the output, and the
+    // pending boxes beyond m are tested against the boxes just kept. Boxes suppressed
+    // by earlier rounds never reach the matrix, so with heavy suppression the
+    // sequential settle runs over few boxes.
+    Det* raw = reinterpret_cast<Det*>(grp + kMaxClasses);              // kSub
+    Det* sub = raw + kSub;                                             // 2 * kSub pending
+    Det* kept_s = sub + 2 * kSub;                                      // kKeptSmem
     uint32_t* mask = reinterpret_cast<uint32_t*>(kept_s + kKeptSmem);  // kSub * kSub / 32
-    int* pre = reinterpret_cast<int*>(mask + kSub * (kSub / 32));      // kSub
+    int* flag = reinterpret_cast<int*>(mask + kSub * (kSub / 32));     // 2 * kSub
     __shared__ uint32_t kbits[kSub / 32];
+    __shared__ int s_np;
+    constexpr int kWarps = kThreads / 32;
     // 2 ulp(thr) for thr in (0, 1) (used only there)
     const double two_ulp = p.iou > 0.0 && p.iou < 1.0
         ? 2.0 * (__longlong_as_double(__double_as_longlong(p.iou) + 1) - p.iou) : 0.0;
-    for (int base = 0; base < n && s_kept < p.max_det; base += kSub) {
-        const int cnt = n - base < kSub ? n - base : kSub;
-        const int kept0 = s_kept;
-        for (int i = tid; i < kSub; i += kThreads) {
-            if (i < cnt) sub[i] = cand[keys[base + i] & 0xFFFF];
-            pre[i] = 0;
-        }
-        if (tid < kSub / 32) kbits[tid] = 0;
-        __syncthreads();
-        constexpr int kWarps = kThreads / 32;
-        // (b) boxes kept before this sub-block: one warp per candidate, lanes over kept
+    // flag[j] = 1 when box j of `list` (cnt boxes) is suppressed by a kept box in [k0, k1)
+    auto test_kept = [&](const Det* list, int cnt, int k0, int k1) {
         for (int j = warp; j < cnt; j += kWarps) {
-            const Det c = sub[j];
+            const Det c = list[j];
             bool sup = false;
-            for (int r = lane; r < kept0 && !sup; r += 32) {
+            for (int r = k0 + lane; r < k1 && !sup; r += 32) {
                 const Det& o = r < kKeptSmem ? kept_s[r] : out[r];
                 sup = o.cls == c.cls && iou_exceeds(o, c, p.iou, two_ulp);
             }
             sup = __any_sync(0xffffffffu, sup);
-            if (lane == 0) pre[j] = sup ? 1 : 0;
+            if (lane == 0) flag[j] = sup ? 1 : 0;
         }
-        // (c) in-block suppression matrix: one warp per row j, a ballot per 32 columns;
+    };
+    // appends the unflagged boxes of list[0..cnt) to sub[dst..], in order (cnt <= kThreads)
+    auto append_survivors = [&](const Det* list, int cnt, int dst) {
+        const bool keep = tid < cnt && !flag[tid];
+        Det d;
+        if (keep) d = list[tid];
+        const unsigned bal = __ballot_sync(0xffffffffu, keep);
+        if (lane == 0) warp_tot[warp] = __popc(bal);
+        __syncthreads();
+        if (warp == 0) {
+            int v = warp_tot[lane];
+            for (int o = 1; o < 32; o <<= 1) {
+                const int t2 = __shfl_up_sync(0xffffffffu, v, o);
+                if (lane >= o) v += t2;
+            }
+            warp_tot[lane] = v;
+        }
+        __syncthreads();
+        if (keep) sub[dst + (warp ? warp_tot[warp - 1] : 0) + __popc(bal & ((1u << lane) - 1u))] = d;
+        if (tid == 0) s_np = dst + warp_tot[31];
+        __syncthreads();
+    };
+    if (tid == 0) s_np = 0;
+    __syncthreads();
+    int cursor = 0;
+    while (s_kept < p.max_det && (cursor < n || s_np > 0)) {
+        // (a) fill the pending list
+        while (s_np < kSub && cursor < n) {
+            const int cnt = n - cursor < kSub ? n - cursor : kSub;
+            for (int i = tid; i < cnt; i += kThreads) raw[i] = cand[keys[cursor + i] & 0xFFFF];
+            __syncthreads();
+            test_kept(raw, cnt, 0, s_kept);
+            __syncthreads();
+            append_survivors(raw, cnt, s_np);
+            cursor += cnt;
+        }
+        const int np = s_np;
+        const int m = np < kSub ? np : kSub;
+        const int kept0 = s_kept;
+        if (tid < kSub / 32) kbits[tid] = 0;
+        // (b) in-block suppression matrix: one warp per row j, a ballot per 32 columns;
         //     only the words holding some i < j are written (the sweep reads no other)
-        for (int j = warp; j < cnt; j += kWarps) {
+        for (int j = warp; j < m; j += kWarps) {
             const Det c = sub[j];
             for (int w = 0; 32 * w < j; ++w) {
                 const int i = 32 * w + lane;
@@ -282,12 +323,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_nms_kernel(DecodeArgs p) {
             }
         }
         __syncthreads();
-        // (d) settle the boxes in order: warp 0, lane w < 8 holds the kept bits of word w
+        // (c) settle the boxes in order: warp 0, lane w < 8 holds the kept bits of word w
         if (warp == 0) {
             uint32_t kbw = 0;
             int k = kept0;
-            for (int q = 0; q < cnt && k < p.max_det; ++q) {
-                if (pre[q]) continue;
+            for (int q = 0; q < m && k < p.max_det; ++q) {
                 const uint32_t row = lane < kSub / 32 ? mask[q * (kSub / 32) + lane] : 0u;
                 if (!__any_sync(0xffffffffu, (row & kbw) != 0u)) {
                     if (lane == (q >> 5)) kbw |= 1u << (q & 31);
@@ -298,13 +338,26 @@ __global__ void __launch_bounds__(kThreads, 1) decode_nms_kernel(DecodeArgs p) {
             if (lane == 0) s_kept = k;
         }
         __syncthreads();
-        if (tid < cnt && ((kbits[tid >> 5] >> (tid & 31)) & 1u)) {
+        // (d) append the kept boxes
+        if (tid < m && ((kbits[tid >> 5] >> (tid & 31)) & 1u)) {
             int pos = kept0 + __popc(kbits[tid >> 5] & ((1u << (tid & 31)) - 1u));
             for (int w = 0; w < (tid >> 5); ++w) pos += __popc(kbits[w]);
             out[pos] = sub[tid];
             if (pos < kKeptSmem) kept_s[pos] = sub[tid];
         }
         __syncthreads();
+        // pending boxes beyond m: test against the boxes kept in this round, keep the rest
+        const int rest = np - m;
+        if (rest > 0 && s_kept < p.max_det) {
+            for (int i = tid; i < rest; i += kThreads) raw[i] = sub[m + i];
+            __syncthreads();
+            test_kept(raw, rest, kept0, s_kept);
+            __syncthreads();
+            append_survivors(raw, rest, 0);
+        } else {
+            if (tid == 0) s_np = 0;
+            __syncthreads();
+        }
     }
     if (tid == 0) p.counts[b] = s_kept;
 }
