@@ -216,21 +216,19 @@ __global__ void __launch_bounds__(kThreads, 1) decode_nms_kernel(DecodeArgs p) {
     }
     __syncthreads();
 
-    // ---- 3. sort by the final output order: (conf desc, class group, index) ----
-    int np = 1;
-    while (np < n) np <<= 1;
-    for (int i = tid; i < np; i += kThreads) {
-        if (i < n) {
-            const Det& d = cand[i];
-            keys[i] = ((unsigned long long)desc_key(d.conf) << 26) | ((unsigned long long)grp[d.cls] << 16) |
-                      (unsigned long long)i;
-        } else {
-            keys[i] = ~0ull;
-        }
-    }
-    __syncthreads();
-    bitonic_sort(keys, np);
-
+    // ---- 3. the output order: (conf desc, class group, index) ----
+    // The greedy pass below settles boxes in this order and stops at max_det kept, so
+    // with many candidates it usually needs only a prefix of the order: segment 0 is
+    // the prefix {conf key <= T}, T the conf key of the R-th box (radix select over the
+    // 32-bit conf keys; ties at T keep it a prefix); only when the pass runs out of it
+    // before max_det boxes are kept is segment 1, the rest, sorted and the pass
+    // continued on it. Without selection segment 0 is all n boxes.
+    __shared__ int hist[256];
+    __shared__ uint32_t s_prefix;
+    __shared__ int s_rem, s_sel;
+    const int R = p.max_det * 8 > 4096 ? p.max_det * 8 : 4096;
+    const bool select = n > R && R <= kMaxKeys / 2;
+    uint32_t T = 0xFFFFFFFFu;
     // ---- 4. one greedy pass in output order ----
     // A box's same-class predecessors in the reference's per-class order all come
     // before it in this order, so deciding boxes in this order keeps exactly the
@@ -289,13 +287,77 @@ __global__ void __launch_bounds__(kThreads, 1) decode_nms_kernel(DecodeArgs p) {
         if (tid == 0) s_np = dst + warp_tot[31];
         __syncthreads();
     };
+    for (int seg = 0; seg < 2; ++seg) {
+    for (int i = tid; i < n; i += kThreads) {
+        const Det& d = cand[i];
+        keys[i] = ((unsigned long long)desc_key(d.conf) << 26) | ((unsigned long long)grp[d.cls] << 16) |
+                  (unsigned long long)i;
+    }
+    __syncthreads();
+    if (select && seg == 0) {
+        if (tid == 0) { s_prefix = 0; s_rem = R; }
+        __syncthreads();
+        for (int shift = 24; shift >= 0; shift -= 8) {
+            for (int i = tid; i < 256; i += kThreads) hist[i] = 0;
+            __syncthreads();
+            const uint32_t pre_k = s_prefix;
+            for (int i = tid; i < n; i += kThreads) {
+                const uint32_t dk = (uint32_t)(keys[i] >> 26);
+                if (shift == 24 || (dk >> (shift + 8)) == pre_k) atomicAdd(&hist[(dk >> shift) & 255], 1);
+            }
+            __syncthreads();
+            if (warp == 0) {
+                // the bin holding the s_rem-th key; lane l owns bins 8l .. 8l+7
+                int v[8], tot = 0;
+#pragma unroll
+                for (int q = 0; q < 8; ++q) { v[q] = hist[lane * 8 + q]; tot += v[q]; }
+                int incl = tot;
+                for (int o = 1; o < 32; o <<= 1) {
+                    const int t2 = __shfl_up_sync(0xffffffffu, incl, o);
+                    if (lane >= o) incl += t2;
+                }
+                const int rem = s_rem;
+                int excl = incl - tot;
+                if (excl < rem && rem <= incl) {
+                    int q = 0;
+                    while (excl + v[q] < rem) { excl += v[q]; ++q; }
+                    s_prefix = (pre_k << 8) | (uint32_t)(lane * 8 + q);
+                    s_rem = rem - excl;
+                }
+            }
+            __syncthreads();
+        }
+        T = s_prefix;
+    }
+    int ns = n;
+    if (select) {
+        // keep segment seg's keys: gathered into registers, then written to keys[0 .. ns)
+        unsigned long long mine[kMaxKeys / kThreads];
+        int cnt_mine = 0;
+        for (int i = tid; i < n; i += kThreads) {
+            const bool in0 = (uint32_t)(keys[i] >> 26) <= T;
+            if (in0 == (seg == 0)) mine[cnt_mine++] = keys[i];
+        }
+        if (tid == 0) s_sel = 0;
+        __syncthreads();
+        const int pos = cnt_mine ? atomicAdd(&s_sel, cnt_mine) : 0;
+        for (int q = 0; q < cnt_mine; ++q) keys[pos + q] = mine[q];
+        __syncthreads();
+        ns = s_sel;
+    }
+    int np = 1;
+    while (np < ns) np <<= 1;
+    for (int i = ns + tid; i < np; i += kThreads) keys[i] = ~0ull;
+    __syncthreads();
+    bitonic_sort(keys, np);
+
     if (tid == 0) s_np = 0;
     __syncthreads();
     int cursor = 0;
-    while (s_kept < p.max_det && (cursor < n || s_np > 0)) {
+    while (s_kept < p.max_det && (cursor < ns || s_np > 0)) {
         // (a) fill the pending list
-        while (s_np < kSub && cursor < n) {
-            const int cnt = n - cursor < kSub ? n - cursor : kSub;
+        while (s_np < kSub && cursor < ns) {
+            const int cnt = ns - cursor < kSub ? ns - cursor : kSub;
             for (int i = tid; i < cnt; i += kThreads) raw[i] = cand[keys[cursor + i] & 0xFFFF];
             __syncthreads();
             test_kept(raw, cnt, 0, s_kept);
@@ -323,16 +385,32 @@ __global__ void __launch_bounds__(kThreads, 1) decode_nms_kernel(DecodeArgs p) {
             }
         }
         __syncthreads();
-        // (c) settle the boxes in order: warp 0, lane w < 8 holds the kept bits of word w
+        // (c) settle the boxes in order, one 32-box word at a time (warp 0; lane w < 8
+        //     ends up with the kept bits of word w): every lane first tests its box
+        //     against the boxes kept in earlier words, then the word is resolved in order
+        //     with each box's in-word row bits, broadcast by shuffles.
         if (warp == 0) {
             uint32_t kbw = 0;
             int k = kept0;
-            for (int q = 0; q < m && k < p.max_det; ++q) {
-                const uint32_t row = lane < kSub / 32 ? mask[q * (kSub / 32) + lane] : 0u;
-                if (!__any_sync(0xffffffffu, (row & kbw) != 0u)) {
-                    if (lane == (q >> 5)) kbw |= 1u << (q & 31);
-                    ++k;
+            for (int W = 0; 32 * W < m && k < p.max_det; ++W) {
+                const int q = 32 * W + lane;
+                bool sup = q >= m;
+                for (int w = 0; w < W; ++w) {
+                    const uint32_t kw_w = __shfl_sync(0xffffffffu, kbw, w);
+                    if (!sup && (mask[q * (kSub / 32) + w] & kw_w)) sup = true;
                 }
+                // bits of rows i < q of this word (word W of row q is written when lane > 0)
+                const uint32_t intra = (q < m && lane > 0) ? mask[q * (kSub / 32) + W] : 0u;
+                const uint32_t cand_bits = __ballot_sync(0xffffffffu, !sup);
+                uint32_t kw = 0;
+                for (int bq = 0; bq < 32; ++bq) {
+                    const uint32_t row = __shfl_sync(0xffffffffu, intra, bq);
+                    if (((cand_bits >> bq) & 1u) && !(row & kw) && k < p.max_det) {
+                        kw |= 1u << bq;
+                        ++k;
+                    }
+                }
+                if (lane == W) kbw = kw;
             }
             if (lane < kSub / 32) kbits[lane] = kbw;
             if (lane == 0) s_kept = k;
@@ -358,6 +436,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_nms_kernel(DecodeArgs p) {
             if (tid == 0) s_np = 0;
             __syncthreads();
         }
+    }
+    if (!select || s_kept >= p.max_det) break;
+    __syncthreads();
     }
     if (tid == 0) p.counts[b] = s_kept;
 }
