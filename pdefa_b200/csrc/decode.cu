@@ -87,14 +87,73 @@ __device__ __forceinline__ double clamp_ref(double v, double hi) {
     return v < 0.0 ? 0.0 : (v > hi ? hi : v);
 }
 
-// Bitonic sort of np (a power of two) keys, ascending; every thread takes whole
-// compare-exchange pairs, so all threads work in every pass.
+// Bitonic sort of np (a power of two) keys, ascending. Strides of 128 and more run
+// in shared memory with a barrier per pass (every thread takes whole compare-exchange
+// pairs); the strides below 128 of every stage run in registers: warp w holds
+// 128-key groups g = w, w + 32, ... as 4 consecutive keys per lane, strides 1 and 2
+// within a lane, 4 ... 64 across lanes by shuffles, with one barrier per stage.
+__device__ __forceinline__ void cmp_swap_reg(unsigned long long& lo, unsigned long long& hi, bool asc) {
+    if ((lo > hi) == asc) { const unsigned long long t = lo; lo = hi; hi = t; }
+}
+
 __device__ void bitonic_sort(unsigned long long* keys, int np) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (np < 128) {
+        const int half = np >> 1;
+        for (int k = 2; k <= np; k <<= 1) {
+            for (int j = k >> 1; j > 0; j >>= 1) {
+                for (int t = threadIdx.x; t < half; t += kThreads) {
+                    const int i = ((t & ~(j - 1)) << 1) | (t & (j - 1));
+                    const int ixj = i | j;
+                    const unsigned long long a = keys[i], b = keys[ixj];
+                    const bool asc = (i & k) == 0;
+                    if ((a > b) == asc) { keys[i] = b; keys[ixj] = a; }
+                }
+                __syncthreads();
+            }
+        }
+        return;
+    }
     const int half = np >> 1;
+    // stages k (sequence length): register passes for strides min(k/2, 64) ... 1
+    auto reg_passes = [&](int k) {
+        for (int g = warp; g < (np >> 7); g += kThreads / 32) {
+            const int e0 = g * 128 + lane * 4;          // this lane's first key
+            unsigned long long v[4];
+#pragma unroll
+            for (int r = 0; r < 4; ++r) v[r] = keys[e0 + r];
+            for (int j = (k >> 1) < 64 ? (k >> 1) : 64; j > 0; j >>= 1) {
+                if (j >= 4) {
+                    const int lx = j >> 2;              // partner lane distance
+#pragma unroll
+                    for (int r = 0; r < 4; ++r) {
+                        const int e = e0 + r;
+                        const unsigned long long o = __shfl_xor_sync(0xffffffffu, v[r], lx);
+                        const bool asc = (e & k) == 0;
+                        const bool lower = (e & j) == 0;
+                        // the lower element keeps the smaller key when ascending
+                        const bool take_min = lower == asc;
+                        v[r] = take_min ? (o < v[r] ? o : v[r]) : (o > v[r] ? o : v[r]);
+                    }
+                } else if (j == 2) {
+                    const bool asc0 = (e0 & k) == 0;     // keys e0 .. e0+3 share bit log2(k) >= 2
+                    cmp_swap_reg(v[0], v[2], asc0);
+                    cmp_swap_reg(v[1], v[3], asc0);
+                } else {
+                    // stride 1: for k = 2 the pairs (0, 1) and (2, 3) sort in opposite directions
+                    cmp_swap_reg(v[0], v[1], (e0 & k) == 0);
+                    cmp_swap_reg(v[2], v[3], ((e0 + 2) & k) == 0);
+                }
+            }
+#pragma unroll
+            for (int r = 0; r < 4; ++r) keys[e0 + r] = v[r];
+        }
+        __syncthreads();
+    };
     for (int k = 2; k <= np; k <<= 1) {
-        for (int j = k >> 1; j > 0; j >>= 1) {
+        for (int j = k >> 1; j >= 128; j >>= 1) {
             for (int t = threadIdx.x; t < half; t += kThreads) {
-                const int i = ((t & ~(j - 1)) << 1) | (t & (j - 1));   // bit log2(j) of i is 0
+                const int i = ((t & ~(j - 1)) << 1) | (t & (j - 1));
                 const int ixj = i | j;
                 const unsigned long long a = keys[i], b = keys[ixj];
                 const bool asc = (i & k) == 0;
@@ -102,6 +161,7 @@ __device__ void bitonic_sort(unsigned long long* keys, int np) {
             }
             __syncthreads();
         }
+        reg_passes(k);
     }
 }
 
@@ -253,18 +313,31 @@ __global__ void __launch_bounds__(kThreads, 1) decode_nms_kernel(DecodeArgs p) {
     // 2 ulp(thr) for thr in (0, 1) (used only there)
     const double two_ulp = p.iou > 0.0 && p.iou < 1.0
         ? 2.0 * (__longlong_as_double(__double_as_longlong(p.iou) + 1) - p.iou) : 0.0;
-    // flag[j] = 1 when box j of `list` (cnt boxes) is suppressed by a kept box in [k0, k1)
+    // flag[j] = 1 when box j of `list` (cnt <= kSub boxes) is suppressed by a kept box in
+    // [k0, k1). Lanes take the boxes (32 per warp); the warps sharing a group of 32 split
+    // the kept range, so every kept box is read by all lanes at once (a broadcast).
     auto test_kept = [&](const Det* list, int cnt, int k0, int k1) {
-        for (int j = warp; j < cnt; j += kWarps) {
-            const Det c = list[j];
-            bool sup = false;
-            for (int r = k0 + lane; r < k1 && !sup; r += 32) {
-                const Det& o = r < kKeptSmem ? kept_s[r] : out[r];
-                sup = o.cls == c.cls && iou_exceeds(o, c, p.iou, two_ulp);
+        if (tid < cnt) flag[tid] = 0;
+        __syncthreads();
+        const int groups = (cnt + 31) >> 5;
+        if (groups > 0) {
+            const int slices = kWarps / groups;
+            const int gsel = warp % groups, slice = warp / groups;
+            const int j = gsel * 32 + lane;
+            const bool valid = j < cnt && slice < slices;
+            Det c;
+            if (valid) c = list[j];
+            bool sup = !valid;
+            if (slice < slices) {
+                for (int r = k0 + slice; r < k1; r += slices) {
+                    const Det& o = r < kKeptSmem ? kept_s[r] : out[r];
+                    if (!sup && o.cls == c.cls && iou_exceeds(o, c, p.iou, two_ulp)) sup = true;
+                    if (((r - k0) & 7) == 7 && __all_sync(0xffffffffu, sup)) break;
+                }
             }
-            sup = __any_sync(0xffffffffu, sup);
-            if (lane == 0) flag[j] = sup ? 1 : 0;
+            if (valid && sup) flag[j] = 1;
         }
+        __syncthreads();
     };
     // appends the unflagged boxes of list[0..cnt) to sub[dst..], in order (cnt <= kThreads)
     auto append_survivors = [&](const Det* list, int cnt, int dst) {
