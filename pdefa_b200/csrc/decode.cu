@@ -286,7 +286,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_nms_kernel(DecodeArgs p) {
     __shared__ int hist[256];
     __shared__ uint32_t s_prefix;
     __shared__ int s_rem, s_sel;
-    const int R = p.max_det * 8 > 4096 ? p.max_det * 8 : 4096;
+    // R a little under a power of two, so that ties at T rarely double the sort size
+    const int R = p.max_det * 8 > 3968 ? p.max_det * 8 : 3968;
     const bool select = n > R && R <= kMaxKeys / 2;
     uint32_t T = 0xFFFFFFFFu;
     // ---- 4. one greedy pass in output order ----
