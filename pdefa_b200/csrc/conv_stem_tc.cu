@@ -295,8 +295,9 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool i
 __device__ __forceinline__ void stem_region_load(const StemTileParams& P, int64_t t, float* dst, int H, int W) {
     const ConvArgs& a = P.a;
     const int64_t per_img = (int64_t)P.tiles_h * P.tiles_w;
-    const int64_t b = t / per_img;
-    const int r = (int)(t - b * per_img);
+    // tile counts stay below 2^31 (host-checked): 32-bit divisions
+    const uint32_t b = (uint32_t)t / (uint32_t)per_img;
+    const int r = (int)((uint32_t)t - b * (uint32_t)per_img);
     const int th = r / P.tiles_w, tw = r - th * P.tiles_w;
     const int h0 = th * (2 * kTileH) - 1, c0 = tw * (2 * kTileW) - 4;
     const float* const in = static_cast<const float*>(a.in.ptr) + b * a.in.img_stride;
@@ -425,8 +426,8 @@ __global__ void __launch_bounds__(128, 8) conv_stem_tile_kernel(const StemTilePa
             break;
         }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const int64_t b = t / per_img;
-        const int r = (int)(t - b * per_img);
+        const uint32_t b = (uint32_t)t / (uint32_t)per_img;
+        const int r = (int)((uint32_t)t - b * (uint32_t)per_img);
         const int th = r / P.tiles_w, tw = r - th * P.tiles_w;
         const int ho = th * kTileH + py, wo = tw * kTileW + px;
         const bool live = ho < P.Ho && wo < P.Wo;
@@ -518,7 +519,7 @@ void launch_conv_stem_tc(const ConvArgs& a, int* err, cudaStream_t s) {
         T.err = err;
         const size_t rbytes = (size_t)3 * kRegPlane * 4;
         const size_t smem = 512 + kRows * kRowBytes + ((a.cout * kRowBytes + 511) & ~511) + 2 * rbytes + 64;
-        if (smem <= 48 * 1024 && T.tiles < (int64_t(1) << 40)) {
+        if (smem <= 48 * 1024 && T.tiles < (int64_t(1) << 31)) {
             static int sms_t[64] = {};
             int sms = 148;
             if (dev0 < 64) {

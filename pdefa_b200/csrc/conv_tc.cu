@@ -239,8 +239,17 @@ __device__ __forceinline__ void epilogue_math(const TcParams& p, float (&v)[16],
             v[4 * q] += b.x; v[4 * q + 1] += b.y; v[4 * q + 2] += b.z; v[4 * q + 3] += b.w;
         }
     }
+    if (ACT == ACT_SILU_WINO) {
 #pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] = tc_act<ACT>(v[i], p.slope);
+        for (int i = 0; i < 16; i += 2) {
+            const float2 y = silu_wino_fast2(make_float2(v[i], v[i + 1]));
+            v[i] = y.x;
+            v[i + 1] = y.y;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] = tc_act<ACT>(v[i], p.slope);
+    }
     if (p.res) {
         if (p.res_dt == BF16) {
 #pragma unroll

@@ -83,6 +83,32 @@ __device__ __forceinline__ float silu_wino_fast(float x) {
     return y;
 }
 
+// silu_wino_fast on two values with the packed fp32x2 pipe of sm_100 (each lane of a
+// packed multiply/add/fma rounds like the scalar instruction, so the results equal
+// silu_wino_fast's bit for bit; rint, clamp, the exponent bits and the divide stay
+// per lane).
+__device__ __forceinline__ float2 silu_wino_fast2(float2 x) {
+    const float2 fx = __fmul2_rn(x, make_float2(-1.44269504088896341f, -1.44269504088896341f));
+    const float n0 = fminf(fmaxf(rintf(fx.x), -126.0f), 127.0f);
+    const float n1 = fminf(fmaxf(rintf(fx.y), -126.0f), 127.0f);
+    const float2 f = __fadd2_rn(fx, make_float2(-n0, -n1));
+    float2 p = make_float2(1.9875691500e-4f, 1.9875691500e-4f);
+    p = __ffma2_rn(p, f, make_float2(1.3981999507e-3f, 1.3981999507e-3f));
+    p = __ffma2_rn(p, f, make_float2(8.3334519073e-3f, 8.3334519073e-3f));
+    p = __ffma2_rn(p, f, make_float2(4.1665795894e-2f, 4.1665795894e-2f));
+    p = __ffma2_rn(p, f, make_float2(1.6666665459e-1f, 1.6666665459e-1f));
+    p = __ffma2_rn(p, f, make_float2(5.0000001201e-1f, 5.0000001201e-1f));
+    p = __ffma2_rn(p, f, make_float2(1.0f, 1.0f));
+    const float2 scale = make_float2(__int_as_float(((int)n0 + 127) << 23), __int_as_float(((int)n1 + 127) << 23));
+    const float2 den = __ffma2_rn(p, scale, make_float2(1.0f, 1.0f));
+    float y0 = __fdividef(x.x, den.x), y1 = __fdividef(x.y, den.y);
+    y0 = x.x > 88.37626f ? x.x : y0;
+    y0 = x.x < -88.37626f ? 0.0f : y0;
+    y1 = x.y > 88.37626f ? x.y : y1;
+    y1 = x.y < -88.37626f ? 0.0f : y1;
+    return make_float2(y0, y1);
+}
+
 __device__ __forceinline__ float apply_act(float v, int act, float p0, float p1) {
     switch (act) {
         case ACT_RELU: return v > 0.0f ? v : 0.0f;

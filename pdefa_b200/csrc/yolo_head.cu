@@ -40,7 +40,7 @@ __global__ void yolo_head_kernel(YoloHeadArgs a) {
             }
             float sum = 0.0f;
             for (int k = 0; k < reg; ++k) { x[k] = expf(x[k] - mx); sum += x[k]; }
-            const float inv = sum > 0.0f ? 1.0f / sum : 0.0f;
+            const float inv = sum > 0.0f ? __frcp_rn(sum) : 0.0f;   // = 1.0f / sum (both correctly rounded)
             float d = 0.0f;
             for (int k = 0; k < reg; ++k) d = fmaf(x[k] * inv, a.dfl_w[k], d);
             dist[side] = d;
@@ -57,7 +57,7 @@ __global__ void yolo_head_kernel(YoloHeadArgs a) {
         o[3 * A] = __fmul_rn(bh, st);
         for (int c = 0; c < nc; ++c) {
             const float z = ld_elem(v.ptr, v.dt, base + (4 * reg + c) * v.stride[3]);
-            o[(4 + c) * A] = 1.0f / (1.0f + expf(-z));
+            o[(4 + c) * A] = __frcp_rn(1.0f + expf(-z));   // = 1.0f / (1.0f + e), correctly rounded
         }
     }
 }
@@ -129,7 +129,7 @@ __global__ void __launch_bounds__(kHeadAnchors) yolo_head_tile_kernel(YoloHeadAr
         float sum = 0.0f;
 #pragma unroll
         for (int k = 0; k < kReg; ++k) { x[k] = expf(x[k] - mx); sum += x[k]; }
-        const float inv = sum > 0.0f ? 1.0f / sum : 0.0f;
+        const float inv = sum > 0.0f ? __frcp_rn(sum) : 0.0f;   // = 1.0f / sum (both correctly rounded)
         float d = 0.0f;
 #pragma unroll
         for (int k = 0; k < kReg; ++k) d = fmaf(x[k] * inv, a.dfl_w[k], d);
@@ -150,7 +150,7 @@ __global__ void __launch_bounds__(kHeadAnchors) yolo_head_tile_kernel(YoloHeadAr
         float z[kPer];
         unpack8<BF>(row[4 * kReg / kPer + c], z);
 #pragma unroll
-        for (int e = 0; e < kPer; ++e) o[(4 + c * kPer + e) * A] = 1.0f / (1.0f + expf(-z[e]));
+        for (int e = 0; e < kPer; ++e) o[(4 + c * kPer + e) * A] = __frcp_rn(1.0f + expf(-z[e]));
     }
 }
 
