@@ -35,10 +35,11 @@ constexpr int kMaxKeys = 16384;
 constexpr int kMaxClasses = 1024;
 constexpr int kSub = 256;          // boxes settled per greedy sub-block
 constexpr int kKeptSmem = 512;     // kept boxes mirrored in shared memory
-// keys | class first/group | raw chunk (kSub) + pending survivors (2 kSub) + kept mirror
-// (kKeptSmem) | in-block matrix | survivor flags
-constexpr size_t kNmsSmem = kMaxKeys * 8 + 2 * kMaxClasses * 4 + (3 * kSub + kKeptSmem) * 48 +
-                            kSub * (kSub / 32) * 4 + 2 * kSub * 4;
+// keys | class first/group | raw chunk (kSub) + pending survivors (2 kSub) Det records |
+// kept boxes' float bounds + classes (kKeptSmem) | pending boxes' float bounds (2 kSub) |
+// in-block matrix | survivor flags
+constexpr size_t kNmsSmem = kMaxKeys * 8 + 2 * kMaxClasses * 4 + 3 * kSub * 48 + kKeptSmem * 20 +
+                            2 * kSub * 16 + kSub * (kSub / 32) * 4 + 2 * kSub * 4;
 
 struct Det {
     double x1, y1, x2, y2;
@@ -81,6 +82,18 @@ __device__ __forceinline__ bool iou_exceeds(const Det& a, const Det& b, double t
         if (e > __dmul_rn(two_ulp_thr, D)) return true;
     }
     return !(__ddiv_rn(inter, D) <= thr);
+}
+
+// Float bounds of a box, rounded outwards (x1, y1 down; x2, y2 up), and the test that
+// two such boxes cannot overlap: then the exact boxes cannot either (or one is empty),
+// so the reference's IoU is 0. NaN bounds never pass the test.
+__device__ __forceinline__ float4 outer_bounds(const Det& d) {
+    return make_float4(__double2float_rd(d.x1), __double2float_rd(d.y1), __double2float_ru(d.x2),
+                       __double2float_ru(d.y2));
+}
+__device__ __forceinline__ bool apart(const float4& a, const float4& b) {
+    return a.z <= b.x || b.z <= a.x || a.w <= b.y || b.w <= a.y || a.z <= a.x || a.w <= a.y || b.z <= b.x ||
+           b.w <= b.y;
 }
 
 __device__ __forceinline__ double clamp_ref(double v, double hi) {
@@ -305,8 +318,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_nms_kernel(DecodeArgs p) {
     // sequential settle runs over few boxes.
     Det* raw = reinterpret_cast<Det*>(grp + kMaxClasses);              // kSub
     Det* sub = raw + kSub;                                             // 2 * kSub pending
-    Det* kept_s = sub + 2 * kSub;                                      // kKeptSmem
-    uint32_t* mask = reinterpret_cast<uint32_t*>(kept_s + kKeptSmem);  // kSub * kSub / 32
+    float4* kept_f = reinterpret_cast<float4*>(sub + 2 * kSub);         // kKeptSmem float bounds
+    int* kept_c = reinterpret_cast<int*>(kept_f + kKeptSmem);          // kKeptSmem classes
+    float4* sub_f = reinterpret_cast<float4*>(kept_c + kKeptSmem);     // 2 * kSub float bounds
+    uint32_t* mask = reinterpret_cast<uint32_t*>(sub_f + 2 * kSub);    // kSub * kSub / 32
+    // non-overlapping pairs skip the float64 IoU when IoU 0 cannot exceed the threshold
+    const bool prefilter = p.iou >= 0.0;
     int* flag = reinterpret_cast<int*>(mask + kSub * (kSub / 32));     // 2 * kSub
     __shared__ uint32_t kbits[kSub / 32];
     __shared__ int s_np;
@@ -328,11 +345,20 @@ __global__ void __launch_bounds__(kThreads, 1) decode_nms_kernel(DecodeArgs p) {
             const bool valid = j < cnt && slice < slices;
             Det c;
             if (valid) c = list[j];
+            const float4 cf = valid ? outer_bounds(c) : make_float4(0.f, 0.f, 0.f, 0.f);
             bool sup = !valid;
             if (slice < slices) {
                 for (int r = k0 + slice; r < k1; r += slices) {
-                    const Det& o = r < kKeptSmem ? kept_s[r] : out[r];
-                    if (!sup && o.cls == c.cls && iou_exceeds(o, c, p.iou, two_ulp)) sup = true;
+                    if (!sup) {
+                        if (r < kKeptSmem) {
+                            if (kept_c[r] == c.cls && !(prefilter && apart(kept_f[r], cf)) &&
+                                iou_exceeds(out[r], c, p.iou, two_ulp))
+                                sup = true;
+                        } else {
+                            const Det& o = out[r];
+                            if (o.cls == c.cls && iou_exceeds(o, c, p.iou, two_ulp)) sup = true;
+                        }
+                    }
                     if (((r - k0) & 7) == 7 && __all_sync(0xffffffffu, sup)) break;
                 }
             }
@@ -357,7 +383,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_nms_kernel(DecodeArgs p) {
             warp_tot[lane] = v;
         }
         __syncthreads();
-        if (keep) sub[dst + (warp ? warp_tot[warp - 1] : 0) + __popc(bal & ((1u << lane) - 1u))] = d;
+        if (keep) {
+            const int q = dst + (warp ? warp_tot[warp - 1] : 0) + __popc(bal & ((1u << lane) - 1u));
+            sub[q] = d;
+            sub_f[q] = outer_bounds(d);
+        }
         if (tid == 0) s_np = dst + warp_tot[31];
         __syncthreads();
     };
@@ -447,12 +477,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_nms_kernel(DecodeArgs p) {
         //     only the words holding some i < j are written (the sweep reads no other)
         for (int j = warp; j < m; j += kWarps) {
             const Det c = sub[j];
+            const float4 cf = sub_f[j];
             for (int w = 0; 32 * w < j; ++w) {
                 const int i = 32 * w + lane;
                 bool sup = false;
                 if (i < j) {
                     const Det& o = sub[i];
-                    sup = o.cls == c.cls && iou_exceeds(o, c, p.iou, two_ulp);
+                    sup = o.cls == c.cls && !(prefilter && apart(sub_f[i], cf)) && iou_exceeds(o, c, p.iou, two_ulp);
                 }
                 const uint32_t bits = __ballot_sync(0xffffffffu, sup);
                 if (lane == 0) mask[j * (kSub / 32) + w] = bits;
@@ -495,7 +526,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_nms_kernel(DecodeArgs p) {
             int pos = kept0 + __popc(kbits[tid >> 5] & ((1u << (tid & 31)) - 1u));
             for (int w = 0; w < (tid >> 5); ++w) pos += __popc(kbits[w]);
             out[pos] = sub[tid];
-            if (pos < kKeptSmem) kept_s[pos] = sub[tid];
+            if (pos < kKeptSmem) {
+                kept_f[pos] = sub_f[tid];
+                kept_c[pos] = sub[tid].cls;
+            }
         }
         __syncthreads();
         // pending boxes beyond m: test against the boxes kept in this round, keep the rest
