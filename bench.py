@@ -286,12 +286,30 @@ def main():
         by_kind[k] = by_kind.get(k, 0.0) + step_ms[i] / args.steps
     tc_flops = (flops_img - 2 * 3 * 16 * 9 * (args.imgsz // 2) ** 2) * B
     achieved = tc_flops / (tc_ms / 1e3) / 1e12 if tc_ms > 0 else None
+    # per-layer roofline: each conv's time bound is max(FLOPs / tensor peak, bytes /
+    # HBM bandwidth), bytes = activations in (fp32 for the stem's graph input, bf16
+    # otherwise) + out (bf16) once; the fraction is the sum of the bounds over the
+    # sum of the measured conv times
+    layer_of = {name: (cin, cout, k, s, h, w) for name, cin, cout, k, s, h, w in info["convs"]}
+    ideal_ms = meas_ms = 0.0
+    for i, (kd, name) in enumerate(summary):
+        key = name.strip("/").replace("/conv/Conv", "")
+        if not kd.startswith("conv") or key not in layer_of:
+            continue
+        cin, cout, k, s, h, w = layer_of[key]
+        ho, wo = (h + 2 * (k // 2) - k) // s + 1, (w + 2 * (k // 2) - k) // s + 1
+        fl = 2.0 * cin * cout * k * k * ho * wo * B
+        by = ((4 if kd == "conv_stem_tc" else 2) * cin * h * w + 2 * cout * ho * wo) * B
+        ideal_ms += max(fl / (peak_sus * 1e12), by / (hbm * 1e9)) * 1e3
+        meas_ms += step_ms[i] / args.steps
     roofline = {"bound": "tensor", "achieved": achieved, "peak": peak_sus, "unit": "TFLOP/s",
                 "frac": (achieved / peak_sus) if achieved else None,
                 "traffic": conv_tc_traffic_per_launch(B) if args.imgsz == 640 else None,
                 "traffic_unit": "DRAM bytes per conv_tc launch (ncu, averaged over the 62 launches of a step)",
                 "kernel": "conv_tc_bf16 (62 launches/step)", "peak_source": f"{peak_src} bf16 sustained",
                 "conv_tflops_all_convs": flops_img * B / (conv_ms_all / 1e3) / 1e12 if conv_ms_all else None,
+                "conv_per_layer_roofline_frac": ideal_ms / meas_ms if meas_ms else None,
+                "conv_per_layer_roofline_ms": {"bound": round(ideal_ms, 4), "measured": round(meas_ms, 4)},
                 "ms_by_kernel_kind": {k: round(v, 4) for k, v in by_kind.items()},
                 "decode_ms": ms_max / args.steps - sum(by_kind.values())}
 

@@ -18,7 +18,15 @@ import numpy as np
 from pdefa_b200.engine_file import EngineGraph, OP_NAME
 
 
-def conv2d_nchw(x, w, b, stride, pad):
+def conv2d_nchw(x, w, b, stride, pad, groups=1):
+    """ONNX Conv (dilation 1); groups > 1 splits input and output channels into
+    `groups` independent convolutions (the reference's depthwise / grouped paths,
+    PDEFA1.0/src/ops/conv2d.cpp:164-393)."""
+    if groups > 1:
+        xs = np.split(x, groups, axis=1)
+        ws = np.split(w, groups, axis=0)
+        bs = np.split(b, groups) if b is not None else [None] * groups
+        return np.concatenate([conv2d_nchw(xs[i], ws[i], bs[i], stride, pad) for i in range(groups)], axis=1)
     n, c, h, wd = x.shape
     co, ci, kh, kw = w.shape
     xp = np.pad(x, ((0, 0), (0, 0), (pad[0], pad[0]), (pad[1], pad[1])))
@@ -133,7 +141,7 @@ def run(g: EngineGraph, inputs, dtype=np.float64, reference_silu=True):
         ins = [get(i) for i in n.inputs]
         if op == 'Conv2d':
             y = conv2d_nchw(ins[0], ins[1], ins[2] if len(ins) > 2 else None,
-                            (p['stride_h'], p['stride_w']), (p['pad_h'], p['pad_w']))
+                            (p['stride_h'], p['stride_w']), (p['pad_h'], p['pad_w']), max(1, p['groups']))
             if k in fused:
                 w = ins[1]
                 path = ref_conv_path(w.shape[1], w.shape[2], w.shape[3], p['stride_h'], p['stride_w'],

@@ -273,8 +273,9 @@ struct PlanBuilder {
                 set_out(n, 0, {is[0], ws[0], is[2], is[3]}, F32, ni);
                 return;
             }
-            if (groups != 1) fail(ENGINE_ERR_NOT_IMPL, "grouped/depthwise conv is not supported by this build");
-            if (is[3] != ci_w) fail(ENGINE_ERR_INVALID_SHAPE, "conv '" + n.name + "': channel mismatch");
+            if (groups != 1 && (is[3] != ci_w * groups || ws[0] % groups))
+                fail(ENGINE_ERR_INVALID_SHAPE, "conv '" + n.name + "': channels do not match the groups");
+            if (groups == 1 && is[3] != ci_w) fail(ENGINE_ERR_INVALID_SHAPE, "conv '" + n.name + "': channel mismatch");
             auto osz = [](int64_t in, int64_t k, int64_t s, int64_t p, int64_t d) {
                 return (in + 2 * p - ((k - 1) * d + 1)) / s + 1;
             };
@@ -1234,6 +1235,41 @@ struct PlanBuilder {
         if (conv_res[ni] >= 0) a.res = view(conv_res[ni]);
         a.bias = bias;
         a.cin = (int)Ci; a.cout = (int)Co; a.kh = (int)KH; a.kw = (int)KW;
+        const int64_t groups = n.params.groups > 0 ? n.params.groups : 1;
+        if (groups > 1) {
+            // grouped / depthwise (conv2d.cpp:164-393): fp32 weights [Cout][kh][kw][Cin/groups]
+            a.cin = (int)(Ci * groups);
+            a.sh = (int)n.params.stride_h; a.sw = (int)n.params.stride_w;
+            a.ph = (int)n.params.pad_h; a.pw = (int)n.params.pad_w;
+            a.dh = (int)n.params.dil_h; a.dw = (int)n.params.dil_w;
+            a.act = act == ACT_SILU_WINO ? ACT_SILU : act;
+            a.slope = conv_slope[ni];
+            a.batch = B;
+            const float* wf0 = W.f32();
+            std::vector<float> w0;
+            if (!wf0) { w0.resize(W.numel()); for (int64_t i = 0; i < W.numel(); ++i) w0[i] = (float)W.value(i); wf0 = w0.data(); }
+            std::vector<float> h((size_t)Co * KH * KW * Ci);
+            for (int64_t co = 0; co < Co; ++co)
+                for (int64_t ci = 0; ci < Ci; ++ci)
+                    for (int64_t r = 0; r < KH; ++r)
+                        for (int64_t s2 = 0; s2 < KW; ++s2)
+                            h[((size_t)(co * KH + r) * KW + s2) * Ci + ci] = wf0[((co * Ci + ci) * KH + r) * KW + s2];
+            void* d = P.alloc(h.size() * 4);
+            if (!P.dry_) PB_CUDA(cudaMemcpy(d, h.data(), h.size() * 4, cudaMemcpyHostToDevice));
+            a.weight = d;
+            const int g = (int)groups;
+            kind("conv_grouped");
+            add_step(n.name, [a, g, ext, pp](cudaStream_t s) mutable {
+                if (ext && pp->cur_in_) a.in.ptr = pp->cur_in_;
+                launch_conv_grouped(a, g, s);
+            });
+            if (tanh_after) {
+                const TView ov = out;
+                const int64_t bt = B;
+                add_step(n.name + "/tanh", [=](cudaStream_t s) { launch_unary(UN_TANH, ov, ov, bt, 0.0f, 0, s); });
+            }
+            return;
+        }
         a.sh = (int)n.params.stride_h; a.sw = (int)n.params.stride_w;
         a.ph = (int)n.params.pad_h; a.pw = (int)n.params.pad_w;
         a.dh = (int)n.params.dil_h; a.dw = (int)n.params.dil_w;

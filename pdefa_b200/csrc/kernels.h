@@ -81,6 +81,11 @@ struct ConvArgs {
 // Strict fp32 SIMT implicit GEMM. weight: fp32 [kh][kw][cin][cout].
 void launch_conv_simt(const ConvArgs& a, cudaStream_t s);
 
+// Grouped / depthwise conv: a.cin and a.cout are the full channel counts, each of the
+// `groups` groups maps cin/groups input to cout/groups output channels; weight: fp32
+// [cout][kh][kw][cin/groups].
+void launch_conv_grouped(const ConvArgs& a, int groups, cudaStream_t s);
+
 // Direct conv for tiny Cin (<= 8) and Cout <= 64 (the stem): fp32 FMA, weight
 // packing as for launch_conv_simt.
 bool conv_direct_supported(const ConvArgs& a);

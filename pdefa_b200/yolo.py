@@ -53,15 +53,16 @@ class _Builder:
         return self.g.add_weight(name, np.asarray(arr, dtype=np.float32))
 
     # -- layers ---------------------------------------------------------
-    def conv(self, x, shp, cout, k, s, name, act=True, bias=True):
+    def conv(self, x, shp, cout, k, s, name, act=True, bias=True, groups=1):
         cin, h, w = shp
         p = k // 2
-        wi = self.rand_weight(f"{name}.weight", (cout, cin, k, k), math.sqrt(2.0 / (cin * k * k)))
+        cg = cin // groups
+        wi = self.rand_weight(f"{name}.weight", (cout, cg, k, k), math.sqrt(2.0 / (cg * k * k)))
         ins = [x, wi]
         if bias:
             ins.append(self.rand_weight(f"{name}.bias", (cout,), 0.1))
         (y,) = self.g.add_node('Conv2d', f"/{name}/conv/Conv", ins,
-                               stride_h=s, stride_w=s, pad_h=p, pad_w=p)
+                               stride_h=s, stride_w=s, pad_h=p, pad_w=p, groups=groups)
         ho, wo = (h + 2 * p - k) // s + 1, (w + 2 * p - k) // s + 1
         self.convs.append((name, cin, cout, k, s, h, w))
         if act:
@@ -218,13 +219,14 @@ def build_yolov8(scale: str = 'n', imgsz: int = 640, nc: int = 80, seed: int = 0
 
 
 def build_single_conv(cin: int = 3, cout: int = 16, k: int = 3, s: int = 2, hw: int = 640,
-                      seed: int = 0, act: bool = True) -> Tuple[EngineGraph, Dict]:
-    """Conv-BN-SiLU stem layer as a 3-node graph (Conv -> Sigmoid -> Mul)."""
+                      seed: int = 0, act: bool = True, groups: int = 1) -> Tuple[EngineGraph, Dict]:
+    """Conv-BN-SiLU stem layer as a 3-node graph (Conv -> Sigmoid -> Mul); groups > 1
+    makes it a grouped (groups = cin = cout: depthwise) convolution."""
     b = _Builder(seed)
     g = b.g
     g.graph_inputs = [-1]
     g.input_infos = [TensorInfo("images", [1, cin, hw, hw])]
-    y, shp = b.conv(-1, (cin, hw, hw), cout, k, s, "model.0", act=act)
+    y, shp = b.conv(-1, (cin, hw, hw), cout, k, s, "model.0", act=act, groups=groups)
     g.graph_outputs = [y]
     g.output_infos = [TensorInfo("output0", [1, cout, shp[1], shp[2]])]
     return g, dict(convs=b.convs)

@@ -340,3 +340,24 @@ def test_batch_inference_pipelined_micro_batches(y8n_128):
     for b in range(3):
         assert [(e["x1"], e["y1"], e["x2"], e["y2"], e["conf"], e["cls"]) for e in lists[b]] == \
             [(r["x1"], r["y1"], r["x2"], r["y2"], float(r["conf"]), int(r["cls"])) for r in d_ref[b, :c_ref[b]]]
+
+
+# ------------------------------------------------------------- grouped / depthwise conv
+@pytest.mark.parametrize("prec", PRECS)
+@pytest.mark.parametrize("cin,cout,k,s,groups,hw", [(16, 16, 3, 1, 16, 40), (64, 64, 3, 2, 64, 33),
+                                                    (32, 64, 3, 2, 4, 29), (24, 24, 5, 1, 24, 17)])
+def test_grouped_conv_against_reference_engine(engine_dir, prec, cin, cout, k, s, groups, hw):
+    """Depthwise and grouped convs (the reference's conv2d.cpp:164-393 paths) with the
+    fused SiLU, against the compiled reference engine and the numpy restatement."""
+    from oracle import onnx_numpy
+    g, _ = build_single_conv(cin=cin, cout=cout, k=k, s=s, hw=hw, seed=6, groups=groups)
+    p = str(engine_dir / f"grouped_{cin}_{cout}_{k}_{s}_{groups}_{hw}.engine")
+    write_engine(p, g)
+    x = np.random.default_rng(8).random((3, cin, hw, hw), dtype=np.float32) - 0.5
+    y = run_engine(p, x, prec)
+    ref = onnx_numpy.run(g, [x])[0]
+    assert normwise(y, ref) <= TOL[prec]
+    if R.available():
+        for i in range(3):
+            r = R.RefSession(p).run(x[i:i + 1])
+            assert normwise(y[i:i + 1], r) <= TOL[prec]

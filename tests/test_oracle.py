@@ -68,3 +68,21 @@ def test_silu_winograd_flavour_is_not_exact_silu():
     # integral log2 points (f == 0) are exact up to float rounding
     xi = np.array([0.0, -np.log(2) * 3], dtype=np.float32)
     np.testing.assert_allclose(onnx_numpy.silu_winograd_flavor(xi), xi / (1 + np.exp(-xi)), rtol=1e-5, atol=1e-7)
+
+
+@pytest.mark.parametrize("cin,cout,k,s,groups,hw", [(16, 16, 3, 1, 16, 12), (32, 64, 3, 2, 4, 13),
+                                                    (24, 24, 5, 2, 24, 11)])
+def test_numpy_grouped_conv_matches_reference_engine(tmp_path, cin, cout, k, s, groups, hw):
+    """Grouped and depthwise convs (conv2d.cpp:164-393) in the numpy restatement agree
+    with the compiled reference engine, when it is built on this host."""
+    from oracle import ref_engine as R
+    from pdefa_b200.engine_file import write_engine
+    if not R.available():
+        pytest.skip("reference engine not built on this host")
+    g, _ = build_single_conv(cin=cin, cout=cout, k=k, s=s, hw=hw, seed=4, groups=groups)
+    p = str(tmp_path / "grouped.engine")
+    write_engine(p, g)
+    x = np.random.default_rng(1).random((1, cin, hw, hw), dtype=np.float32) - 0.5
+    ref = R.RefSession(p).run(x)
+    y = onnx_numpy.run(g, [x])[0]
+    assert normwise(y, ref) <= 1e-6

@@ -57,3 +57,13 @@ def test_stem_plan(tmp_path):
     write_engine(p, g)
     steps = pb.Model(pb.Context(), p).plan_summary(pb.BF16, 1)
     assert [k for k, _ in steps] == ["conv_stem_tc", "copy"]     # conv + NHWC->NCHW output
+
+
+@pytest.mark.parametrize("prec", [pb.FP32, pb.TF32, pb.BF16])
+def test_grouped_conv_plan(tmp_path, prec):
+    """Depthwise / grouped convs lower to the grouped-conv kernel in every precision."""
+    g, _ = build_single_conv(cin=32, cout=32, k=3, s=1, hw=40, groups=32)
+    p = str(tmp_path / "dw.engine")
+    write_engine(p, g)
+    kinds = [k for k, _ in pb.Model(pb.Context(), p).plan_summary(prec, 2)]
+    assert "conv_grouped" in kinds and not any(k.startswith("conv_tc") for k in kinds)

@@ -58,7 +58,7 @@ def _rank_main(rank, world, port, out):
 def test_two_gloo_ranks_reduce_max_time_and_total_images():
     world = 2
     port = _free_port()
-    with mp.Manager() as m:
+    with mp.get_context("spawn").Manager() as m:
         out = m.dict()
         mp.spawn(_rank_main, args=(world, port, out), nprocs=world, join=True)
         res = dict(out)
