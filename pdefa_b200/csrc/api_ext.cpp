@@ -394,9 +394,13 @@ EngineStatus run_batch(PdefaBatchRunner* r, const BatchInput& in, int64_t n_imag
                     // Micro-batches of at most max_per_device images alternate between the two
                     // lanes: the copy stream brings micro-batch i+1 onto the GPU while the
                     // compute stream runs inference + decode of micro-batch i.
+                    // The first micro-batch of a shard is a quarter of the others, so the
+                    // pipeline fills after a short copy; then full micro-batches.
+                    const int64_t mfull = r->max_per_device;
+                    const int64_t mfirst = (hi - lo > mfull && mfull >= 8) ? mfull / 4 : mfull;
                     int64_t i = 0;
-                    for (int64_t c0 = lo; c0 < hi; c0 += r->max_per_device, ++i) {
-                        const int64_t nb = std::min(r->max_per_device, hi - c0);
+                    for (int64_t c0 = lo, nb = 0; c0 < hi; c0 += nb, ++i) {
+                        nb = std::min(i == 0 ? mfirst : mfull, hi - c0);
                         auto& l = rp.lanes[i & 1];
                         retire(l);    // the lane's buffers are free once its previous micro-batch is done
                         auto it = l.plans.find(nb);
