@@ -541,8 +541,11 @@ __device__ __forceinline__ void mma_issuer(const TcParams& p, const MmaSmem& m, 
 //   warps 2..EPI+1:   epilogue (see epilogue_loop).
 // Tiles are taken round-robin (tile = blockIdx.x + i*gridDim.x), N-tiles innermost
 // so CTAs working on the same pixel rows run close together (A re-reads hit L2).
-template <int KIND, int EPI>
-__global__ void __launch_bounds__(conv_threads<EPI>(), EPI == 8 ? 2 : 4)
+// MINB: resident CTAs per SM the launch plans for (the register budget per thread is
+// 64K / (threads * MINB)); a launch with fewer CTAs per SM uses the variant with the
+// larger budget, so the epilogue does not spill.
+template <int KIND, int EPI, int MINB>
+__global__ void __launch_bounds__(conv_threads<EPI>(), MINB)
 conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                const __grid_constant__ CUtensorMap tmOut, const TcParams p) {
     extern __shared__ uint8_t smem_raw[];
@@ -1031,11 +1034,15 @@ void launch_conv_tc(const ConvArgs& a, int op_dt, int* err, cudaStream_t s) {
     }
     const int64_t tiles = p.m_tiles * p.n_tiles;
     dim3 grid((unsigned)std::min<int64_t>(tiles, (int64_t)sms * ctas));
-    static bool attr[4][64] = {};
+    static bool attr[10][64] = {};
     const int kind = op_dt == BF16 ? 0 : 1;
-    const int variant = kind * 2 + (epi == 8 ? 1 : 0);
-    void (*const fns[4])(CUtensorMap, CUtensorMap, CUtensorMap, TcParams) = {
-        conv_tc_kernel<0, 4>, conv_tc_kernel<0, 8>, conv_tc_kernel<1, 4>, conv_tc_kernel<1, 8>};
+    // register-budget variant: EPI 4 at 4, 3 or <= 2 CTAs per SM; EPI 8 at 2 or 1
+    const int vsub = epi == 8 ? (ctas >= 2 ? 3 : 4) : (ctas >= 4 ? 0 : (ctas == 3 ? 1 : 2));
+    const int variant = kind * 5 + vsub;
+    void (*const fns[10])(CUtensorMap, CUtensorMap, CUtensorMap, TcParams) = {
+        conv_tc_kernel<0, 4, 4>, conv_tc_kernel<0, 4, 3>, conv_tc_kernel<0, 4, 2>, conv_tc_kernel<0, 8, 2>,
+        conv_tc_kernel<0, 8, 1>, conv_tc_kernel<1, 4, 4>, conv_tc_kernel<1, 4, 3>, conv_tc_kernel<1, 4, 2>,
+        conv_tc_kernel<1, 8, 2>, conv_tc_kernel<1, 8, 1>};
     if (dev < 64 && !attr[variant][dev]) {
         PB_CUDA(cudaFuncSetAttribute(fns[variant], cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
         attr[variant][dev] = true;
