@@ -2,9 +2,10 @@
  *
  * Signatures and structs follow the reference pdefa/include/pdefa_c_api.h
  * (line numbers below) and the export list pdefa/pdefa.def:4-23.
- * Image decoding is outside this library's GPU hot path: pdefa_image_load and the
- * functions that read image files report ENGINE_ERR_NOT_IMPL / NULL with a message
- * in pdefa_last_error(). Box and point unmapping are implemented.
+ * pdefa_image_load decodes PNG files (the same pixels as the reference's decoder);
+ * JPEG files return NULL with a message in pdefa_last_error(). pdefa_preprocess_letterbox
+ * and pdefa_prepare_for_engine letterbox on the GPU, bit-identical to the reference.
+ * Box and point unmapping are implemented.
  */
 #ifndef PDEFA_B200_PDEFA_C_API_H
 #define PDEFA_B200_PDEFA_C_API_H

@@ -8,7 +8,7 @@ __version__ = "1.0.3-b200"
 
 from .api import (  # noqa: F401
     BF16, FP32, TF32,
-    Box, Context, EngineModel, Model, PdefaError, PreprocessMeta, Session, Tensor, TensorInfo,
+    Box, Context, EngineModel, Image, Model, PdefaError, PreprocessMeta, Session, Tensor, TensorInfo,
     _model_input_shape, cpu_brand, decode_yolo, decode_yolo_arrays, device_count, empty, from_list,
     letterbox_meta, letterbox_u8, load, load_image, load_image_as_tensor, map_box_to_original, map_point_to_original, ones,
     ops_add, ops_argmax, ops_clip, ops_concat, ops_div, ops_gather, ops_gelu, ops_matmul, ops_mul,
@@ -20,7 +20,7 @@ from .api import (  # noqa: F401
 from .batch import BatchInference  # noqa: F401
 
 __all__ = [
-    "PdefaError", "PreprocessMeta", "Box", "Tensor", "TensorInfo", "Context", "Model", "Session",
+    "PdefaError", "PreprocessMeta", "Box", "Tensor", "TensorInfo", "Context", "Model", "Session", "Image",
     "version", "simd_level", "cpu_brand", "device_count",
     "load_image", "preprocess_letterbox", "prepare_for_engine", "load_image_as_tensor",
     "map_box_to_original", "map_point_to_original", "decode_yolo", "decode_yolo_arrays", "prepare_for_model",

@@ -108,6 +108,9 @@ _SIGS = {
     "engine_random_rand": ([P(i64), i32, u64, P(vp)], C.c_int),
     # pdefa
     "pdefa_image_load": ([C.c_char_p], vp), "pdefa_image_free": ([vp], None),
+    "pdefa_image_width": ([vp], i32), "pdefa_image_height": ([vp], i32), "pdefa_image_channels": ([vp], i32),
+    "pdefa_image_format": ([vp], i32), "pdefa_image_pixels": ([vp, P(sz)], vp),
+    "pdefa_preprocess_letterbox": ([vp, P(PreConfig), P(vp), P(PreMeta)], C.c_int),
     "pdefa_prepare_for_engine": ([C.c_char_p, i32, i32, f32, f32, P(vp), P(PreMeta)], C.c_int),
     "pdefa_load_image_as_tensor": ([C.c_char_p, i32, i32, P(vp)], C.c_int),
     "pdefa_map_box_to_original": ([P(f32), P(PreMeta), P(f32)], C.c_int),

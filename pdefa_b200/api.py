@@ -9,9 +9,9 @@ Differences from the reference:
   [B, 4+nc, A] output with B > 1 it returns one list per image;
 * Context.set_precision / set_device select strict FP32, TF32 or BF16 arithmetic
   and the GPU; Session.run_device runs on device pointers;
-* image decoding is not part of this library: load_image / prepare_for_engine
-  raise PdefaError; decoded 8-bit images are letterboxed on the GPU by
-  letterbox_u8 (bit-identical to the reference's preprocess_letterbox) or inside
+* image files: PNG is decoded on the host (the reference's pixels), JPEG raises
+  PdefaError; letterboxing runs on the GPU (bit-identical to the reference's
+  preprocess_letterbox), also for decoded 8-bit arrays (letterbox_u8) and inside
   BatchInference.detect_u8.
 """
 from __future__ import annotations
@@ -562,21 +562,83 @@ class Session:
 # ----------------------------------------------------------------------------
 # Images (outside this library) and box mapping
 # ----------------------------------------------------------------------------
-def load_image(path: str):
-    raise PdefaError("load_image: image decoding is not part of the pdefa B200 library")
+class Image:
+    """Decoded image (pdefa/python/src/pdefa/_bindings.py:693-733): width, height,
+    channels, format (PdefaPixelFormat: 0 GRAY8, 1 RGB8, 2 RGBA8, 3 GRAY16) and the
+    tightly packed row-major pixel bytes."""
+
+    def __init__(self, handle):
+        self._handle = handle
+
+    def __del__(self):
+        h = getattr(self, "_handle", None)
+        if h and N._lib is not None:
+            N._lib.pdefa_image_free(h)
+            self._handle = None
+
+    @property
+    def width(self) -> int:
+        return int(N.lib().pdefa_image_width(self._handle))
+
+    @property
+    def height(self) -> int:
+        return int(N.lib().pdefa_image_height(self._handle))
+
+    @property
+    def channels(self) -> int:
+        return int(N.lib().pdefa_image_channels(self._handle))
+
+    @property
+    def format(self) -> int:
+        return int(N.lib().pdefa_image_format(self._handle))
+
+    def pixels_bytes(self) -> bytes:
+        n = C.c_size_t(0)
+        ptr = N.lib().pdefa_image_pixels(self._handle, C.byref(n))
+        return C.string_at(ptr, n.value) if ptr and n.value else b""
+
+    def to_numpy(self):
+        """uint8 [h, w, C] (GRAY16: [h, w, 2] big-endian byte pairs)."""
+        import numpy as np
+        a = np.frombuffer(self.pixels_bytes(), np.uint8)
+        per = 2 if self.format == 3 else self.channels
+        return a.reshape(self.height, self.width, per)
 
 
-def preprocess_letterbox(*args, **kw):
-    raise PdefaError("preprocess_letterbox: image decoding is not part of the pdefa B200 library")
+def load_image(path: str) -> Image:
+    """Decode an image file (PNG; JPEG files raise PdefaError)."""
+    h = N.lib().pdefa_image_load(path.encode("utf-8"))
+    if not h:
+        raise PdefaError(f"load_image({path}): {(N.lib().pdefa_last_error() or b'').decode()}")
+    return Image(h)
+
+
+def preprocess_letterbox(img: Image, target_w: int = 640, target_h: int = 640, scale: float = 1.0 / 255.0,
+                         pad_value: float = 0.0) -> Tuple["Tensor", PreprocessMeta]:
+    """Letterbox on the GPU -> ([1, 3, H, W] fp32 Tensor, meta), bit-identical to the
+    reference's preprocess_letterbox (imageloader/src/preprocess.cpp:15-147)."""
+    t = C.c_void_p()
+    m = N.PreMeta()
+    _check(N.lib().pdefa_preprocess_letterbox(img._handle, C.byref(N.PreConfig(target_w, target_h, scale, pad_value)),
+                                              C.byref(t), C.byref(m)), "preprocess_letterbox")
+    return Tensor(t, owns=True), PreprocessMeta.from_c(m)
 
 
 def prepare_for_engine(path: str, target_w: int = 640, target_h: int = 640, scale: float = 1.0 / 255.0,
-                       pad_value: float = 0.0):
-    raise PdefaError("prepare_for_engine: image decoding is not part of the pdefa B200 library")
+                       pad_value: float = 0.0) -> Tuple["Tensor", PreprocessMeta]:
+    """Image file -> letterboxed [1, 3, H, W] fp32 Tensor + meta."""
+    t = C.c_void_p()
+    m = N.PreMeta()
+    _check(N.lib().pdefa_prepare_for_engine(path.encode("utf-8"), target_w, target_h, scale, pad_value,
+                                            C.byref(t), C.byref(m)), "prepare_for_engine")
+    return Tensor(t, owns=True), PreprocessMeta.from_c(m)
 
 
-def load_image_as_tensor(path: str, target_w: int = 640, target_h: int = 640):
-    raise PdefaError("load_image_as_tensor: image decoding is not part of the pdefa B200 library")
+def load_image_as_tensor(path: str, target_w: int = 640, target_h: int = 640) -> "Tensor":
+    t = C.c_void_p()
+    _check(N.lib().pdefa_load_image_as_tensor(path.encode("utf-8"), target_w, target_h, C.byref(t)),
+           "load_image_as_tensor")
+    return Tensor(t, owns=True)
 
 
 def _u8_batch(images):

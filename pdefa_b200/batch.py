@@ -105,14 +105,17 @@ class BatchInference:
         return out
 
     def run(self, image_paths: List[str], target_w: int = 640, target_h: int = 640) -> List[Tuple[Tensor, PreprocessMeta]]:
-        """Reference signature (image files -> raw outputs). Needs host image decoding."""
+        """Reference signature (batch.py:45-60): image files -> [(raw output Tensor,
+        letterbox meta)], one Session per image like the reference (PNG files)."""
         out = []
         for p in image_paths:
             t, meta = prepare_for_engine(p, target_w, target_h)
             s = Session(self.ctx, self.model)
             s.set_input(0, t)
             s.run()
-            out.append((s.output(0), meta))
+            y = s.output(0)
+            y._session = s      # the output is borrowed from the session: keep it alive
+            out.append((y, meta))
         return out
 
     def close(self):

@@ -64,7 +64,7 @@ def build(force: bool = False, jobs: int = 0) -> str:
         objs = list(ex.map(lambda s: compile_one(s, force), srcs))
     if (force or not os.path.exists(LIB)
             or max(os.path.getmtime(o) for o in objs) > os.path.getmtime(LIB)):
-        cmd = [nvcc(), "-shared", *ARCH, "-cudart", "static", "-o", LIB + ".tmp", *objs, "-lpthread", "-ldl", "-lrt"]
+        cmd = [nvcc(), "-shared", *ARCH, "-cudart", "static", "-o", LIB + ".tmp", *objs, "-lpthread", "-ldl", "-lrt", "-lz"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")

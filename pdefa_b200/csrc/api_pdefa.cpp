@@ -1,12 +1,19 @@
 // pdefa_* C ABI (pdefa/include/pdefa_c_api.h:25-91, export list pdefa/pdefa.def:4-23).
 //
-// Image decoding and letterboxing (imageloader/) are host-side IO that is not part
-// of this library's GPU hot path: the image entry points report ENGINE_ERR_NOT_IMPL
-// (or NULL) with an explanation in pdefa_last_error(). The letterbox coordinate
+// Images (imageloader/): PNG files are decoded on the host (image_png.cpp, the same
+// pixels as the reference's decoder); JPEG files are reported as unsupported with a
+// message in pdefa_last_error(). Letterboxing runs on the GPU (letterbox.cu),
+// bit-identical to imageloader/src/preprocess.cpp. The letterbox coordinate
 // unmapping is implemented with the reference arithmetic
 // (imageloader/src/engine_api.cpp:59-90): (v - pad) / ratio in float, clamped to
 // [0, orig].
-#include "../../include/pdefa_c_api.h"
+#include <cstdio>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "../../include/pdefa_b200_ext.h"
+#include "image_io.h"
 #include "runtime.h"
 
 using namespace pb;
@@ -15,8 +22,54 @@ namespace {
 // One error slot is shared with the engine_* half, so pdefa_last_error() (the only
 // one the Python layer reads, _bindings.py:480-483) also reports engine errors.
 void perr(const char* m) { pb::set_error(m); }
-const char* kNoImages = "image decoding is not part of the pdefa B200 library; decode images on the host "
-                        "and pass NCHW float tensors";
+void perr(const std::string& m) { pb::set_error(m); }
+
+bool read_file(const char* path, std::vector<uint8_t>& buf) {
+    FILE* fp = std::fopen(path, "rb");
+    if (!fp) return false;
+    std::fseek(fp, 0, SEEK_END);
+    const long n = std::ftell(fp);
+    std::fseek(fp, 0, SEEK_SET);
+    bool ok = n >= 0;
+    if (ok) {
+        buf.resize((size_t)n);
+        ok = n == 0 || std::fread(buf.data(), 1, (size_t)n, fp) == (size_t)n;
+    }
+    std::fclose(fp);
+    return ok;
+}
+
+// channel count the reference reports (imageloader/include/imageloader/image.hpp:20-28)
+int channels_of_format(int f) { return f == kFmtRGB8 ? 3 : (f == kFmtRGBA8 ? 4 : 1); }
+
+// Letterbox an image on the GPU (bit-identical to imageloader/src/preprocess.cpp) into
+// an owned [1, 3, H, W] fp32 tensor. A 16-bit gray image goes through as the
+// reference reads it: one byte per sample, rows of `width` bytes.
+EngineStatus letterbox_image(const PdefaImage* img, const PdefaPreprocessConfig* cfg, EngineTensor** out,
+                             PdefaPreprocessMeta* meta);
+}  // namespace
+
+struct PdefaImage {
+    pb::DecodedImage im;
+};
+
+namespace {
+EngineStatus letterbox_image(const PdefaImage* img, const PdefaPreprocessConfig* cfg, EngineTensor** out,
+                             PdefaPreprocessMeta* meta) {
+    const int ch = channels_of_format(img->im.format);
+    const int W = cfg->target_w, H = cfg->target_h;
+    if (W <= 0 || H <= 0) { perr("preprocess: target size must be positive"); return ENGINE_ERR_INVALID_ARG; }
+    std::vector<float> buf((size_t)3 * W * H);
+    PdefaPreprocessMeta m{};
+    const EngineStatus rc = pdefa_letterbox(img->im.pixels.data(), 1, (int32_t)img->im.height,
+                                            (int32_t)img->im.width, ch, cfg, buf.data(), &m, pb::default_device());
+    if (rc != ENGINE_OK) return rc;
+    const int64_t shape[4] = {1, 3, H, W};
+    const EngineStatus rt = engine_tensor_create_from_data(out, shape, 4, ENGINE_F32, buf.data(), buf.size() * 4);
+    if (rt != ENGINE_OK) return rt;
+    if (meta) *meta = m;
+    return ENGINE_OK;
+}
 }  // namespace
 
 extern "C" {
@@ -24,37 +77,62 @@ extern "C" {
 PDEFA_API const char* pdefa_version(void) { return engine_version(); }
 PDEFA_API const char* pdefa_last_error(void) { return engine_last_error(); }
 
+// Decodes PNG files (image_png.cpp); JPEG files are reported as unsupported.
 PDEFA_API PdefaImage* pdefa_image_load(const char* path) {
-    (void)path;
-    perr(kNoImages);
-    return nullptr;
+    if (!path) { perr("null arg"); return nullptr; }
+    try {
+        pb::clear_error();
+        std::vector<uint8_t> data;
+        if (!read_file(path, data)) { perr(std::string("load_image: cannot read file: ") + path); return nullptr; }
+        auto img = std::make_unique<PdefaImage>();
+        std::string err;
+        if (data.size() >= 3 && data[0] == 0xFF && data[1] == 0xD8 && data[2] == 0xFF) {
+            perr("load_image: JPEG decoding is not part of this build (PNG files are decoded)");
+            return nullptr;
+        }
+        if (!pb::decode_png(data.data(), data.size(), img->im, err)) { perr("load_image: " + err); return nullptr; }
+        return img.release();
+    } catch (const std::exception& e) {
+        perr(e.what());
+        return nullptr;
+    }
 }
-PDEFA_API void pdefa_image_free(PdefaImage* img) { (void)img; }
-PDEFA_API int32_t pdefa_image_width(const PdefaImage* img) { (void)img; return 0; }
-PDEFA_API int32_t pdefa_image_height(const PdefaImage* img) { (void)img; return 0; }
-PDEFA_API int32_t pdefa_image_channels(const PdefaImage* img) { (void)img; return 0; }
-PDEFA_API int32_t pdefa_image_format(const PdefaImage* img) { (void)img; return -1; }
+PDEFA_API void pdefa_image_free(PdefaImage* img) { delete img; }
+PDEFA_API int32_t pdefa_image_width(const PdefaImage* img) { return img ? (int32_t)img->im.width : 0; }
+PDEFA_API int32_t pdefa_image_height(const PdefaImage* img) { return img ? (int32_t)img->im.height : 0; }
+PDEFA_API int32_t pdefa_image_channels(const PdefaImage* img) { return img ? channels_of_format(img->im.format) : 0; }
+PDEFA_API int32_t pdefa_image_format(const PdefaImage* img) { return img ? img->im.format : -1; }
 PDEFA_API const uint8_t* pdefa_image_pixels(const PdefaImage* img, size_t* out_bytes) {
-    (void)img;
-    if (out_bytes) *out_bytes = 0;
-    return nullptr;
+    if (!img) {
+        if (out_bytes) *out_bytes = 0;
+        return nullptr;
+    }
+    if (out_bytes) *out_bytes = img->im.pixels.size();
+    return img->im.pixels.data();
 }
 
 PDEFA_API EngineStatus pdefa_preprocess_letterbox(const PdefaImage* img, const PdefaPreprocessConfig* cfg,
                                                   EngineTensor** out_tensor, PdefaPreprocessMeta* out_meta) {
-    (void)out_meta;
     if (!img || !cfg || !out_tensor) { perr("null arg"); return ENGINE_ERR_NULL_PTR; }
     *out_tensor = nullptr;
-    perr(kNoImages);
-    return ENGINE_ERR_NOT_IMPL;
+    try {
+        pb::clear_error();
+        return letterbox_image(img, cfg, out_tensor, out_meta);
+    } catch (const std::exception& e) {
+        perr(e.what());
+        return ENGINE_ERR_RUNTIME;
+    }
 }
 PDEFA_API EngineStatus pdefa_prepare_for_engine(const char* path, int32_t target_w, int32_t target_h, float scale,
                                                 float pad_value, EngineTensor** out_tensor, PdefaPreprocessMeta* out_meta) {
-    (void)target_w; (void)target_h; (void)scale; (void)pad_value; (void)out_meta;
     if (!path || !out_tensor) { perr("null arg"); return ENGINE_ERR_NULL_PTR; }
     *out_tensor = nullptr;
-    perr(kNoImages);
-    return ENGINE_ERR_NOT_IMPL;
+    PdefaImage* img = pdefa_image_load(path);
+    if (!img) return ENGINE_ERR_INVALID_ARG;
+    PdefaPreprocessConfig cfg{target_w, target_h, scale, pad_value};
+    const EngineStatus rc = pdefa_preprocess_letterbox(img, &cfg, out_tensor, out_meta);
+    pdefa_image_free(img);
+    return rc;
 }
 PDEFA_API EngineStatus pdefa_load_image_as_tensor(const char* image_path, int32_t target_w, int32_t target_h,
                                                   EngineTensor** out_tensor) {

@@ -159,4 +159,11 @@ def test_box_mapping_and_images():
     with pytest.raises(pb.PdefaError):
         pb.prepare_for_engine("x.jpg", 640, 640)
     assert N.lib().pdefa_image_load(b"x.png") is None
-    assert b"not part of" in N.lib().pdefa_last_error()
+    assert b"cannot read file" in N.lib().pdefa_last_error()
+
+
+def test_jpeg_files_are_reported(tmp_path):
+    p = tmp_path / "a.jpg"
+    p.write_bytes(b"\xff\xd8\xff\xe0" + bytes(64))
+    assert N.lib().pdefa_image_load(str(p).encode()) is None
+    assert b"JPEG decoding is not part of this build" in N.lib().pdefa_last_error()

@@ -88,3 +88,78 @@ def test_detect_u8_matches_letterbox_session_decode(engine_dir):
         assert len(exp) == counts[b]
         assert [(e["x1"], e["y1"], e["x2"], e["y2"], e["cls"]) for e in exp] == \
             [(r["x1"], r["y1"], r["x2"], r["y2"], int(r["cls"])) for r in got]
+
+
+def _ref_prepare(path, tw, th, scale, pad):
+    """The reference's pdefa_prepare_for_engine (compiled from its sources)."""
+    import ctypes as C
+    from tests.golden import make_letterbox_golden as g
+    L = C.CDLL(os.path.join(os.path.dirname(os.path.dirname(__file__)), "oracle", "_ref", "libpdefa_ref.so"))
+    L.pdefa_prepare_for_engine.argtypes = [C.c_char_p, C.c_int32, C.c_int32, C.c_float, C.c_float,
+                                           C.POINTER(C.c_void_p), C.POINTER(g.Meta)]
+    L.engine_tensor_data.argtypes = [C.c_void_p, C.POINTER(C.c_void_p), C.POINTER(C.c_size_t)]
+    L.engine_tensor_destroy.argtypes = [C.c_void_p]
+    t, m = C.c_void_p(), g.Meta()
+    assert L.pdefa_prepare_for_engine(path.encode(), tw, th, scale, pad, C.byref(t), C.byref(m)) == 0
+    d, nb = C.c_void_p(), C.c_size_t()
+    L.engine_tensor_data(t, C.byref(d), C.byref(nb))
+    out = np.ctypeslib.as_array((C.c_float * (3 * th * tw)).from_address(d.value)).copy().reshape(1, 3, th, tw)
+    L.engine_tensor_destroy(t)
+    return out, [m.target_w, m.target_h, m.orig_w, m.orig_h, m.pad_x, m.pad_y, m.scaled_w, m.scaled_h], m.ratio
+
+
+@pytest.mark.parametrize("ct,bd,hw,target", [(2, 8, (48, 64), 96), (6, 8, (33, 20), 64), (0, 16, (17, 23), 40),
+                                             (3, 4, (29, 31), 56), (0, 8, (50, 41), 64)])
+def test_prepare_for_engine_png_matches_reference(tmp_path, ct, bd, hw, target):
+    """PNG file -> letterboxed tensor: decode on the host + letterbox on the GPU equal the
+    reference's prepare_for_engine bit for bit (16-bit gray included, which the
+    reference letterboxes one byte per sample)."""
+    from tests.test_image_png_cpu import CHANNELS, write_png
+    ref_lib = os.path.join(os.path.dirname(os.path.dirname(__file__)), "oracle", "_ref", "libpdefa_ref.so")
+    rng = np.random.default_rng(ct * 100 + bd)
+    palette = None
+    if ct == 3:
+        palette = rng.integers(0, 256, (16, 3))
+        samples = rng.integers(0, 16, hw + (1,))
+    else:
+        samples = rng.integers(0, 1 << bd, hw + (CHANNELS[ct],))
+    p = str(tmp_path / "img.png")
+    write_png(p, samples, ct, bd, palette, seed=5)
+    t, meta = pb.prepare_for_engine(p, target, target, 1 / 255, 114 / 255)
+    y = t.to_numpy()
+    assert y.shape == (1, 3, target, target)
+    assert meta.orig_w == hw[1] and meta.orig_h == hw[0]
+    if os.path.exists(ref_lib):
+        ref, m, ratio = _ref_prepare(p, target, target, 1 / 255, 114 / 255)
+        np.testing.assert_array_equal(y, ref)
+        assert [getattr(meta, k) for k in META_FIELDS] == m and np.float32(meta.ratio) == np.float32(ratio)
+    img = pb.load_image(p)
+    t2, meta2 = pb.preprocess_letterbox(img, target, target, 1 / 255, 114 / 255)
+    np.testing.assert_array_equal(t2.to_numpy(), y)
+    assert meta2 == meta
+
+
+def test_batch_inference_run_on_png_files(tmp_path, engine_dir):
+    """BatchInference.run(paths), the reference's image-file signature, gives each file's
+    raw model output and letterbox meta."""
+    from tests.test_image_png_cpu import write_png
+    g, _ = build_yolov8("n", imgsz=128, seed=0)
+    p = str(engine_dir / "y8n_128_run.engine")
+    write_engine(p, g)
+    ctx = pb.Context(precision=pb.BF16)
+    m = pb.Model(ctx, p)
+    rng = np.random.default_rng(4)
+    paths = []
+    for i, hw in enumerate([(96, 128), (128, 100)]):
+        f = str(tmp_path / f"f{i}.png")
+        write_png(f, rng.integers(0, 256, hw + (3,)), 2, 8, seed=i)
+        paths.append(f)
+    with pb.BatchInference(ctx, m, batch_size=2, devices=[0]) as bi:
+        res = bi.run(paths, 128, 128)
+    for f, (out, meta) in zip(paths, res):
+        x, meta2 = pb.prepare_for_engine(f, 128, 128)
+        s = pb.Session(ctx, m)
+        s.set_input(0, x)
+        s.run()
+        np.testing.assert_array_equal(out.to_numpy(), s.output(0).to_numpy())
+        assert meta == meta2
