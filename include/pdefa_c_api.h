@@ -2,8 +2,9 @@
  *
  * Signatures and structs follow the reference pdefa/include/pdefa_c_api.h
  * (line numbers below) and the export list pdefa/pdefa.def:4-23.
- * pdefa_image_load decodes PNG files (the same pixels as the reference's decoder);
- * JPEG files return NULL with a message in pdefa_last_error(). pdefa_preprocess_letterbox
+ * pdefa_image_load decodes PNG and baseline JPEG files on the host (the same pixels
+ * as the reference's decoders; failures return NULL with a message in
+ * pdefa_last_error()). pdefa_preprocess_letterbox
  * and pdefa_prepare_for_engine letterbox on the GPU, bit-identical to the reference.
  * Box and point unmapping are implemented.
  */

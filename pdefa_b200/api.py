@@ -9,8 +9,8 @@ Differences from the reference:
   [B, 4+nc, A] output with B > 1 it returns one list per image;
 * Context.set_precision / set_device select strict FP32, TF32 or BF16 arithmetic
   and the GPU; Session.run_device runs on device pointers;
-* image files: PNG is decoded on the host (the reference's pixels), JPEG raises
-  PdefaError; letterboxing runs on the GPU (bit-identical to the reference's
+* image files: PNG and baseline JPEG are decoded on the host (the reference's
+  pixels); letterboxing runs on the GPU (bit-identical to the reference's
   preprocess_letterbox), also for decoded 8-bit arrays (letterbox_u8) and inside
   BatchInference.detect_u8.
 """
@@ -606,7 +606,7 @@ class Image:
 
 
 def load_image(path: str) -> Image:
-    """Decode an image file (PNG; JPEG files raise PdefaError)."""
+    """Decode a PNG or baseline JPEG file to the reference's pixels (imageloader/src/loader.cpp:60-67)."""
     h = N.lib().pdefa_image_load(path.encode("utf-8"))
     if not h:
         raise PdefaError(f"load_image({path}): {(N.lib().pdefa_last_error() or b'').decode()}")

@@ -106,7 +106,7 @@ class BatchInference:
 
     def run(self, image_paths: List[str], target_w: int = 640, target_h: int = 640) -> List[Tuple[Tensor, PreprocessMeta]]:
         """Reference signature (batch.py:45-60): image files -> [(raw output Tensor,
-        letterbox meta)], one Session per image like the reference (PNG files)."""
+        letterbox meta)], one Session per image like the reference (PNG and JPEG files)."""
         out = []
         for p in image_paths:
             t, meta = prepare_for_engine(p, target_w, target_h)

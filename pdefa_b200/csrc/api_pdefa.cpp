@@ -8,6 +8,7 @@
 // (imageloader/src/engine_api.cpp:59-90): (v - pad) / ratio in float, clamped to
 // [0, orig].
 #include <cstdio>
+#include <cstring>
 #include <memory>
 #include <string>
 #include <vector>
@@ -86,11 +87,16 @@ PDEFA_API PdefaImage* pdefa_image_load(const char* path) {
         if (!read_file(path, data)) { perr(std::string("load_image: cannot read file: ") + path); return nullptr; }
         auto img = std::make_unique<PdefaImage>();
         std::string err;
-        if (data.size() >= 3 && data[0] == 0xFF && data[1] == 0xD8 && data[2] == 0xFF) {
-            perr("load_image: JPEG decoding is not part of this build (PNG files are decoded)");
-            return nullptr;
-        }
-        if (!pb::decode_png(data.data(), data.size(), img->im, err)) { perr("load_image: " + err); return nullptr; }
+        // Format by signature, PNG first (imageloader/src/loader.cpp:12-19,60-67).
+        static const uint8_t kPng[8] = {0x89, 'P', 'N', 'G', 0x0D, 0x0A, 0x1A, 0x0A};
+        const uint8_t* d = data.data();
+        const size_t n = data.size();
+        bool ok;
+        if (n < 4) { perr("load_image: file too small"); return nullptr; }
+        if (n >= 8 && std::memcmp(d, kPng, 8) == 0) ok = pb::decode_png(d, n, img->im, err);
+        else if (d[0] == 0xFF && d[1] == 0xD8 && d[2] == 0xFF) ok = pb::decode_jpeg(d, n, img->im, err);
+        else { perr(std::string("load_image: unsupported format: ") + path); return nullptr; }
+        if (!ok) { perr("load_image: " + err); return nullptr; }
         return img.release();
     } catch (const std::exception& e) {
         perr(e.what());

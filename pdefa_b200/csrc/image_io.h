@@ -19,4 +19,7 @@ struct DecodedImage {
 // PNG file bytes -> pixels; false with a message in err on malformed input.
 bool decode_png(const uint8_t* data, size_t n, DecodedImage& img, std::string& err);
 
+// Baseline JPEG file bytes -> RGB8 pixels; false with a message in err.
+bool decode_jpeg(const uint8_t* data, size_t n, DecodedImage& img, std::string& err);
+
 }  // namespace pb

@@ -162,8 +162,14 @@ def test_box_mapping_and_images():
     assert b"cannot read file" in N.lib().pdefa_last_error()
 
 
-def test_jpeg_files_are_reported(tmp_path):
+def test_malformed_and_unknown_files_are_reported(tmp_path):
     p = tmp_path / "a.jpg"
-    p.write_bytes(b"\xff\xd8\xff\xe0" + bytes(64))
+    p.write_bytes(b"\xff\xd8\xff\xe0" + bytes(64))          # APP0 with a zero length
     assert N.lib().pdefa_image_load(str(p).encode()) is None
-    assert b"JPEG decoding is not part of this build" in N.lib().pdefa_last_error()
+    assert N.lib().pdefa_last_error().startswith(b"load_image: jpeg:")
+    p.write_bytes(b"GIF89a" + bytes(64))
+    assert N.lib().pdefa_image_load(str(p).encode()) is None
+    assert b"unsupported format" in N.lib().pdefa_last_error()
+    p.write_bytes(b"\xff\xd8")
+    assert N.lib().pdefa_image_load(str(p).encode()) is None
+    assert b"too small" in N.lib().pdefa_last_error()

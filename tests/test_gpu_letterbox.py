@@ -163,3 +163,25 @@ def test_batch_inference_run_on_png_files(tmp_path, engine_dir):
         s.run()
         np.testing.assert_array_equal(out.to_numpy(), s.output(0).to_numpy())
         assert meta == meta2
+
+
+@pytest.mark.parametrize("name", ["rgb420_q75_odd", "gray_q90", "rgb422_rst"])
+def test_prepare_for_engine_jpeg_matches_reference(tmp_path, name):
+    """JPEG file -> letterboxed tensor equals the reference's prepare_for_engine, and
+    the GPU letterbox of the pinned reference pixels (tests/golden/jpeg_ref.npz)."""
+    ref_lib = os.path.join(os.path.dirname(os.path.dirname(__file__)), "oracle", "_ref", "libpdefa_ref.so")
+    z = np.load(os.path.join(os.path.dirname(__file__), "golden", "jpeg_ref.npz"))
+    p = str(tmp_path / f"{name}.jpg")
+    with open(p, "wb") as f:
+        f.write(z[f"{name}.jpg"].tobytes())
+    w, h, _ = (int(v) for v in z[f"{name}.whf"])
+    t, meta = pb.prepare_for_engine(p, 64, 64, 1 / 255, 114 / 255)
+    y = t.to_numpy()
+    assert (meta.orig_w, meta.orig_h) == (w, h)
+    pixels = z[f"{name}.rgb"].reshape(h, w, 3)
+    y2, meta2 = pb.letterbox_u8(pixels, 64, 64, 1 / 255, 114 / 255)
+    np.testing.assert_array_equal(np.asarray(y2)[0], y[0])
+    if os.path.exists(ref_lib):
+        ref, m, ratio = _ref_prepare(p, 64, 64, 1 / 255, 114 / 255)
+        np.testing.assert_array_equal(y, ref)
+        assert [getattr(meta, k) for k in META_FIELDS] == m
