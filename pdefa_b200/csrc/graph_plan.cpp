@@ -289,14 +289,17 @@ struct PlanBuilder {
             need(2);
             const auto a = V[input_vid(n, 0)].shape;
             const auto b = V[input_vid(n, 1)].shape;
-            if (a.size() == 4 && b.size() == 2 && a[3] == b[0]) {
+            if (a.size() == 4 && b.size() == 4 && b[0] == a[0] && b[1] == a[2] && b[3] == a[3]) {
+                nt.mode = 2;   // head-batched attention product (session_ops_nn.inc:75-108)
+                set_out(n, 0, {a[0], a[1], b[2], a[3]}, F32, ni);
+            } else if (a.size() == 4 && b.size() == 2 && a[3] == b[0]) {
                 nt.mode = 1;
                 set_out(n, 0, {a[0], a[1], a[2], b[1]}, act_dt, ni);
             } else if (a.size() == 2 && b.size() == 2 && a[1] == b[0]) {
                 nt.mode = 0;
                 set_out(n, 0, {a[0], b[1]}, F32, ni);
             } else {
-                fail(ENGINE_ERR_NOT_IMPL, "MatMul '" + n.name + "': only 2-D and 4-D x 2-D forms are supported");
+                fail(ENGINE_ERR_NOT_IMPL, "MatMul '" + n.name + "': only the 2-D, 4-D x 2-D and head-batched 4-D x 4-D forms are supported");
             }
             return;
         }
@@ -319,7 +322,9 @@ struct PlanBuilder {
                 if (da != db && da != 1 && db != 1) fail(ENGINE_ERR_INVALID_SHAPE, "broadcast mismatch in '" + n.name + "'");
                 o[d] = std::max(da, db);
             }
-            set_out(n, 0, o, dt_for(o), ni);
+            // bf16 activations stay bf16; fp32 operands (attention scores) stay fp32
+            const bool any_bf16 = V[input_vid(n, 0)].dt == BF16 || V[input_vid(n, 1)].dt == BF16;
+            set_out(n, 0, o, any_bf16 ? dt_for(o) : F32, ni);
             return;
         }
         case Op::Concat: {
@@ -1377,6 +1382,31 @@ struct PlanBuilder {
         TView O = view(o);
         const auto as = V[a].shape;
         const auto wsh = V[w].shape;
+        if (note[ni].mode == 2) {
+            const int64_t M = as[1], K = as[2], N = wsh[2], H = as[3], nb = B * as[0];
+            const bool odense = dense(o) && V[o].dt == F32;
+            float* op = static_cast<float*>(const_cast<void*>(O.ptr));
+            float* tmp = odense ? op : static_cast<float*>(P.alloc(std::max<size_t>((size_t)nb * M * N * H * 4, 16)));
+            const float* ap = static_cast<const float*>(A.ptr);
+            const float* bp = static_cast<const float*>(Wt.ptr);
+            // a constant operand (img_stride 0) is shared by every image
+            if ((A.img_stride == 0 || Wt.img_stride == 0) && as[0] != 1)
+                fail(ENGINE_ERR_NOT_IMPL, "MatMul '" + n.name + "': constant operand with a batch dimension");
+            const int64_t sa = A.img_stride == 0 ? 0 : M * K * H, sb = Wt.img_stride == 0 ? 0 : K * N * H;
+            kind("matmul_heads");
+            add_step(n.name, [=](cudaStream_t s) {
+                launch_matmul_heads(ap, bp, tmp, nb, M, K, N, H, sa, sb, M * N * H, s);
+            });
+            if (!odense) {
+                TView src = O;
+                src.ptr = tmp; src.dt = F32;
+                const auto st = dense_strides(V[o].shape);
+                for (int d = 0; d < src.rank; ++d) src.stride[d] = st[d];
+                src.img_stride = numel_of(V[o].shape);
+                add_copy(src, O, n.name + "/store");
+            }
+            return;
+        }
         int64_t M, K = wsh[0], N = wsh[1];
         if (note[ni].mode == 1) M = as[0] * as[1] * as[2]; else M = as[0];
         const float* bias = nullptr;

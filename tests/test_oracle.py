@@ -86,3 +86,21 @@ def test_numpy_grouped_conv_matches_reference_engine(tmp_path, cin, cout, k, s, 
     ref = R.RefSession(p).run(x)
     y = onnx_numpy.run(g, [x])[0]
     assert normwise(y, ref) <= 1e-6
+
+
+def test_yolo11_graphs_flops_and_reference_engine(tmp_path):
+    """YOLO11 builders: conv FLOPs equal the published 6.5 / 21.5 / 68.0 / 86.9 GFLOPs
+    (n/s/m/l at 640), and the reference engine runs the C2PSA attention graph."""
+    from oracle import ref_engine as R
+    from pdefa_b200.engine_file import write_engine
+    from pdefa_b200.yolo import build_c2psa, build_yolo11, conv_flops
+    for sc, gf in (("n", 6.5), ("s", 21.5), ("m", 68.0), ("l", 86.9)):
+        _, info = build_yolo11(sc, imgsz=640)
+        assert abs(conv_flops(info) / 1e9 - gf) < 0.06, sc
+    if not R.available():
+        pytest.skip("reference engine not built on this host")
+    g, _ = build_c2psa(c=128, hw=8, seed=1)
+    p = str(tmp_path / "c2psa.engine")
+    write_engine(p, g)
+    y = R.RefSession(p).run(np.random.default_rng(0).random((1, 128, 8, 8), dtype=np.float32))
+    assert y.shape == (1, 128, 8, 8) and np.isfinite(y).all()

@@ -67,3 +67,19 @@ def test_grouped_conv_plan(tmp_path, prec):
     write_engine(p, g)
     kinds = [k for k, _ in pb.Model(pb.Context(), p).plan_summary(prec, 2)]
     assert "conv_grouped" in kinds and not any(k.startswith("conv_tc") for k in kinds)
+
+
+def test_yolo11n_plan_lowers_attention(tmp_path):
+    """YOLO11n: C3k2 and the Detect head on tcgen05 (depthwise class branches on the
+    grouped-conv kernel), the C2PSA attention on matmul_heads + softmax."""
+    from pdefa_b200.yolo import build_yolo11
+    g, _ = build_yolo11("n", imgsz=640)
+    p = str(tmp_path / "y11n.engine")
+    write_engine(p, g)
+    m = pb.Model(pb.Context(), p)
+    for prec in (pb.BF16, pb.TF32, pb.FP32):
+        kinds = Counter(k for k, _ in m.plan_summary(prec, batch=8))
+        assert kinds["matmul_heads"] == 2 and kinds["softmax"] == 1 and kinds["binary"] == 1
+        assert kinds["conv_grouped"] == 7 and kinds["yolo_head"] == 1 and kinds["resize"] == 2
+    kinds = Counter(k for k, _ in m.plan_summary(pb.BF16, batch=8))
+    assert kinds["conv_stem_tc"] == 1 and kinds["conv_tc_bf16"] == 77
