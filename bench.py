@@ -114,15 +114,23 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-def cpu_reference(images: int, threads: int):
+def build_model(name: str, imgsz: int):
+    """(graph, info) of the benchmarked model: yolov8n (the headline config), yolov8m
+    (configs[4], run with --precision tf32 --batch 64) or yolo11n."""
+    from pdefa_b200.yolo import build_yolo11, build_yolov8
+    if name == "yolo11n":
+        return build_yolo11("n", imgsz=imgsz, seed=0)
+    return build_yolov8(name[-1], imgsz=imgsz, seed=0)
+
+
+def cpu_reference(images: int, threads: int, model: str = "yolov8n"):
     """Reference CPU path on `images` images: engine (oracle/_ref) batch-1 + decode restatement."""
     import numpy as np
     from oracle import decode_ref, ref_engine as R
     from pdefa_b200.engine_file import write_engine
-    from pdefa_b200.yolo import build_yolov8
     if not R.available():
         return None
-    g, _ = build_yolov8("n", imgsz=640, seed=0)
+    g, _ = build_model(model, 640)
     p = os.path.join(tempfile.mkdtemp(), "y8n_ref.engine")
     write_engine(p, g)
     sess = R.RefSession(p, threads=threads)
@@ -142,7 +150,7 @@ def run_reference_arm(args, rank):
     if rank != 0:
         return
     threads = os.cpu_count() or 1
-    step = cpu_reference(args.ref_images, threads)
+    step = cpu_reference(args.ref_images, threads, args.model)
     if step is None:
         print(json.dumps({"impl": "reference", "unavailable": "reference engine not built (oracle/_ref missing)"}))
         return
@@ -164,9 +172,10 @@ def run_reference_arm(args, rank):
 
 
 def config(args, world):
-    return {"workload": "configs[3]: YOLOv8n-640 random-init, BF16 tcgen05 convs + GPU decode/NMS "
+    name = {"yolov8n": "configs[3]: YOLOv8n", "yolov8m": "configs[4]: YOLOv8m", "yolo11n": "YOLO11n"}[args.model]
+    return {"workload": f"{name}-{args.imgsz} random-init, {args.precision.upper()} tcgen05 convs + GPU decode/NMS "
                         "(conf 0.25, IoU 0.45, max_det 300), independent replicas",
-            "model": "yolov8n", "imgsz": args.imgsz, "per_gpu_batch": args.batch, "global_batch": args.batch * world,
+            "model": args.model, "imgsz": args.imgsz, "per_gpu_batch": args.batch, "global_batch": args.batch * world,
             "parallelism": f"replicas x{world}", "precision": args.precision,
             "l2": "inputs larger than L2 (1.26 GB per GPU)"}
 
@@ -180,6 +189,8 @@ def main():
     ap.add_argument("--batch", type=int, default=256)
     ap.add_argument("--imgsz", type=int, default=640)
     ap.add_argument("--precision", default="bf16", choices=["bf16", "tf32", "fp32"])
+    ap.add_argument("--model", default="yolov8n", choices=["yolov8n", "yolov8m", "yolo11n"],
+                    help="yolov8n is the headline configuration")
     ap.add_argument("--e2e-steps", type=int, default=0, help="steps for the e2e leg (default: --steps)")
     ap.add_argument("--e2e-micro", type=int, default=64,
                     help="micro-batch of the e2e leg's pipelined batch runner (images per GPU launch)")
@@ -206,16 +217,16 @@ def main():
     from pdefa_b200 import _native as N
     from pdefa_b200.engine_file import write_engine
     from pdefa_b200.replicas import job_throughput, reduce_job
-    from pdefa_b200.yolo import build_yolov8, conv_flops
+    from pdefa_b200.yolo import conv_flops
 
     torch.cuda.set_device(local)
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
     L = N.lib()
     prec = {"bf16": pb.BF16, "tf32": pb.TF32, "fp32": pb.FP32}[args.precision]
-    g, info = build_yolov8("n", imgsz=args.imgsz, seed=0)
+    g, info = build_model(args.model, args.imgsz)
     tmp = tempfile.mkdtemp()
-    path = os.path.join(tmp, "yolov8n.engine")
+    path = os.path.join(tmp, args.model + ".engine")
     write_engine(path, g)
     ctx = pb.Context(precision=prec, device=local)
     model = pb.Model(ctx, path)
@@ -284,7 +295,12 @@ def main():
     by_kind = {}
     for i, (k, _) in enumerate(summary):
         by_kind[k] = by_kind.get(k, 0.0) + step_ms[i] / args.steps
-    tc_flops = (flops_img - 2 * 3 * 16 * 9 * (args.imgsz // 2) ** 2) * B
+    # the stem (graph input, Cin 3) runs on its own kernel: excluded from the conv_tc family
+    _, s_cin, s_cout, s_k, s_s, s_h, s_w = info["convs"][0]
+    tc_flops = (flops_img - 2 * s_cin * s_cout * s_k * s_k * (s_h // s_s) * (s_w // s_s)) * B
+    # TF32 tcgen05 runs at half the BF16 rate: its peak is half the measured BF16 figure
+    peak_sus = peak_sus / 2 if args.precision == "tf32" else peak_sus
+    abytes = 4 if args.precision != "bf16" else 2
     achieved = tc_flops / (tc_ms / 1e3) / 1e12 if tc_ms > 0 else None
     # per-layer roofline: each conv's time bound is max(FLOPs / tensor peak, bytes /
     # HBM bandwidth), bytes = activations in (fp32 for the stem's graph input, bf16
@@ -299,14 +315,16 @@ def main():
         cin, cout, k, s, h, w = layer_of[key]
         ho, wo = (h + 2 * (k // 2) - k) // s + 1, (w + 2 * (k // 2) - k) // s + 1
         fl = 2.0 * cin * cout * k * k * ho * wo * B
-        by = ((4 if kd == "conv_stem_tc" else 2) * cin * h * w + 2 * cout * ho * wo) * B
+        by = ((4 if kd.startswith("conv_stem") or kd == "conv_direct" else abytes) * cin * h * w
+              + abytes * cout * ho * wo) * B
         ideal_ms += max(fl / (peak_sus * 1e12), by / (hbm * 1e9)) * 1e3
         meas_ms += step_ms[i] / args.steps
     roofline = {"bound": "tensor", "achieved": achieved, "peak": peak_sus, "unit": "TFLOP/s",
                 "frac": (achieved / peak_sus) if achieved else None,
-                "traffic": conv_tc_traffic_per_launch(B) if args.imgsz == 640 else None,
+                "traffic": conv_tc_traffic_per_launch(B) if args.imgsz == 640 and args.model == "yolov8n" else None,
                 "traffic_unit": "DRAM bytes per conv_tc launch (ncu, averaged over the 62 launches of a step)",
-                "kernel": "conv_tc_bf16 (62 launches/step)", "peak_source": f"{peak_src} bf16 sustained",
+                "kernel": f"conv_tc_{args.precision} ({sum(1 for k, _ in summary if k.startswith('conv_tc'))} launches/step)",
+                "peak_source": f"{peak_src} bf16 sustained" + (" / 2 (tf32)" if args.precision == "tf32" else ""),
                 "conv_tflops_all_convs": flops_img * B / (conv_ms_all / 1e3) / 1e12 if conv_ms_all else None,
                 "conv_per_layer_roofline_frac": ideal_ms / meas_ms if meas_ms else None,
                 "conv_per_layer_roofline_ms": {"bound": round(ideal_ms, 4), "measured": round(meas_ms, 4)},
@@ -348,7 +366,7 @@ def main():
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
-        stepf = cpu_reference(args.cpu_images, threads)
+        stepf = cpu_reference(args.cpu_images, threads, args.model)
         if stepf is not None:
             secs = stepf(args.cpu_images)
             cpu = {"value": args.cpu_images / secs, "unit": "images/s", "cores": threads, "kind": "reference",

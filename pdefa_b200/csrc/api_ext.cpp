@@ -1,6 +1,7 @@
 // Additive entry points (include/pdefa_b200_ext.h): precision/device selection,
 // device-pointer execution, tensor-core GEMM, batched GPU decode/NMS and the
 // multi-GPU batch runner (one replica per device, contiguous shards, no collective).
+#include <cstdlib>
 #include <cstring>
 #include <thread>
 
@@ -73,6 +74,7 @@ struct PdefaBatchRunner {
         PdefaDetection* h_dets = nullptr;
         size_t dets_cap = 0;
         cudaEvent_t h2d = nullptr, ran = nullptr, done = nullptr;
+        cudaStream_t compute = nullptr;  // letterbox + inference of this lane's micro-batches
         bool busy = false;           // results of (c0, nb) pending
         int64_t c0 = 0, nb = 0;
         void* pixels = nullptr;      // device copy of an 8-bit micro-batch (pdefa_batch_run_u8)
@@ -80,7 +82,8 @@ struct PdefaBatchRunner {
     };
     struct Replica {
         int device = 0;
-        cudaStream_t stream = nullptr;   // letterbox + inference
+        cudaStream_t stream = nullptr;   // letterbox + inference (lane 0; lane 1 too when shared)
+        cudaStream_t stream1 = nullptr;  // lane 1's compute stream when the lanes run concurrently
         cudaStream_t copy = nullptr;     // image copies onto the GPU
         cudaStream_t post = nullptr;     // decode + result copies (overlap the next inference)
         Lane lanes[2];
@@ -332,6 +335,13 @@ ENGINE_API EngineStatus pdefa_batch_create(EngineModel* model, int32_t n_devices
             PB_CUDA(cudaStreamCreateWithFlags(&rp.stream, cudaStreamNonBlocking));
             PB_CUDA(cudaStreamCreateWithFlags(&rp.copy, cudaStreamNonBlocking));
             PB_CUDA(cudaStreamCreateWithFlags(&rp.post, cudaStreamNonBlocking));
+            // Each lane infers on its own stream, so one micro-batch's layers can fill the
+            // SMs the other's small layers and grid tails leave idle (PDEFA_LANE_STREAMS=0:
+            // one shared compute stream).
+            const char* ls = std::getenv("PDEFA_LANE_STREAMS");
+            if (!(ls && ls[0] == '0')) PB_CUDA(cudaStreamCreateWithFlags(&rp.stream1, cudaStreamNonBlocking));
+            rp.lanes[0].compute = rp.stream;
+            rp.lanes[1].compute = rp.stream1 ? rp.stream1 : rp.stream;
             for (auto& l : rp.lanes) {
                 PB_CUDA(cudaEventCreateWithFlags(&l.h2d, cudaEventDisableTiming));
                 PB_CUDA(cudaEventCreateWithFlags(&l.ran, cudaEventDisableTiming));
@@ -427,7 +437,7 @@ EngineStatus run_batch(PdefaBatchRunner* r, const BatchInput& in, int64_t n_imag
                             PB_CUDA(cudaMemcpyAsync(p.input_buffer(0), in.f32 + c0 * (ibytes / 4 / nb), ibytes,
                                                     cudaMemcpyHostToDevice, rp.copy));
                             PB_CUDA(cudaEventRecord(l.h2d, rp.copy));
-                            PB_CUDA(cudaStreamWaitEvent(rp.stream, l.h2d, 0));
+                            PB_CUDA(cudaStreamWaitEvent(l.compute, l.h2d, 0));
                         } else {
                             // 8-bit pixels cross PCIe (a quarter of the float32 bytes for RGB) and
                             // are letterboxed into the plan's input on the GPU
@@ -444,14 +454,14 @@ EngineStatus run_batch(PdefaBatchRunner* r, const BatchInput& in, int64_t n_imag
                             PB_CUDA(cudaMemcpyAsync(l.pixels, in.u8 + c0 * pb_img, pb_img * nb, cudaMemcpyHostToDevice,
                                                     rp.copy));
                             PB_CUDA(cudaEventRecord(l.h2d, rp.copy));
-                            PB_CUDA(cudaStreamWaitEvent(rp.stream, l.h2d, 0));
+                            PB_CUDA(cudaStreamWaitEvent(l.compute, l.h2d, 0));
                             launch_letterbox_u8(static_cast<const uint8_t*>(l.pixels), nb, in.channels, in.geo,
-                                                p.input_buffer(0), rp.stream);
+                                                p.input_buffer(0), l.compute);
                         }
-                        p.run(rp.stream);
+                        p.run(l.compute);
                         // decode on its own stream: one CTA per image leaves most SMs to the
                         // next micro-batch's convolutions
-                        PB_CUDA(cudaEventRecord(l.ran, rp.stream));
+                        PB_CUDA(cudaEventRecord(l.ran, l.compute));
                         PB_CUDA(cudaStreamWaitEvent(rp.post, l.ran, 0));
                         decode_on_device(p.output_buffer(0), nb, ch, A, metas ? metas + c0 : nullptr, conf_thres,
                                          iou_thres, max_det, static_cast<int32_t*>(l.counts), l.dets, l.work,
@@ -477,6 +487,7 @@ EngineStatus run_batch(PdefaBatchRunner* r, const BatchInput& in, int64_t n_imag
                     }
                     cudaStreamSynchronize(rp.copy);
                     cudaStreamSynchronize(rp.stream);
+                    if (rp.stream1) cudaStreamSynchronize(rp.stream1);
                     cudaStreamSynchronize(rp.post);
                 }
             });
@@ -592,6 +603,7 @@ ENGINE_API void pdefa_batch_destroy(PdefaBatchRunner* r) {
     for (auto& rp : r->reps) {
         cudaSetDevice(rp.device);
         if (rp.stream) cudaStreamSynchronize(rp.stream);
+        if (rp.stream1) cudaStreamSynchronize(rp.stream1);
         if (rp.copy) cudaStreamSynchronize(rp.copy);
         if (rp.post) cudaStreamSynchronize(rp.post);
         for (auto& l : rp.lanes) {
@@ -602,6 +614,7 @@ ENGINE_API void pdefa_batch_destroy(PdefaBatchRunner* r) {
             if (l.done) cudaEventDestroy(l.done);
         }
         if (rp.stream) cudaStreamDestroy(rp.stream);
+        if (rp.stream1) cudaStreamDestroy(rp.stream1);
         if (rp.copy) cudaStreamDestroy(rp.copy);
         if (rp.post) cudaStreamDestroy(rp.post);
     }

@@ -220,6 +220,22 @@ def test_yolov8n_640_against_reference_engine(y8n_640, prec):
     assert normwise(y, ref) <= TOL[prec]
 
 
+@pytest.mark.parametrize("prec", [pb.TF32, pb.BF16])
+def test_yolov8m_640_against_reference_engine(engine_dir, prec):
+    """YOLOv8m (width 0.75, depth 0.67; convs up to 768 channels, K up to
+    5184) on the tensor-core paths, batch 2, each image against the reference engine."""
+    if not R.available():
+        pytest.skip("reference engine not built on this host")
+    g, _ = build_yolov8("m", imgsz=640, seed=0)
+    p = str(engine_dir / "y8m_640.engine")
+    write_engine(p, g)
+    x = np.random.default_rng(2).random((2, 3, 640, 640), dtype=np.float32)
+    y = run_engine(p, x, prec)
+    sess = R.RefSession(p)
+    for i in range(2):
+        assert normwise(y[i], sess.run(x[i:i + 1])[0]) <= TOL[prec]
+
+
 def test_tiny_classifier_graph(golden, engine_dir):
     import tests.golden.make_golden as mg
     d = golden("tiny.npz")
