@@ -14,7 +14,7 @@ Printed JSON line (rank 0):
   detections: 8-bit RGB frames letterboxed on the GPU (BatchInference.detect_u8 ->
   pdefa_batch_run_u8), and under e2e.f32_input float32 NCHW tensors
   (detect_arrays -> pdefa_batch_run); the runner pipelines micro-batches of
-  --e2e-micro images (copy of one overlapping the inference of the previous);
+  --e2e-micro (128) images (copy of one overlapping the inference of the previous);
 * roofline: the tcgen05 convolution kernels of the step (the dominant kernel
   family): conv FLOPs / their CUDA-event time measured inside the timed region,
   against the measured sustained BF16 peak;
@@ -192,7 +192,7 @@ def main():
     ap.add_argument("--model", default="yolov8n", choices=["yolov8n", "yolov8m", "yolo11n"],
                     help="yolov8n is the headline configuration")
     ap.add_argument("--e2e-steps", type=int, default=0, help="steps for the e2e leg (default: --steps)")
-    ap.add_argument("--e2e-micro", type=int, default=64,
+    ap.add_argument("--e2e-micro", type=int, default=128,
                     help="micro-batch of the e2e leg's pipelined batch runner (images per GPU launch)")
     ap.add_argument("--cpu-images", type=int, default=48, help="images in the bounded CPU baseline sample")
     ap.add_argument("--ref-images", type=int, default=4, help="images per step of the reference arm")

@@ -92,7 +92,9 @@ struct PlanBuilder {
         int mode = 0;
         std::vector<int64_t> a, b, c;   // mode-specific integer payloads
         bool dfl_fix = false;
+        float scale = 1.0f;             // MatMul mode 2: scalar Mul folded into the product
     };
+    std::unordered_map<int, int> folded_transpose;   // value read through permuted strides -> Transpose node
     std::vector<Note> note;
     std::unordered_map<int, void*> wdev;        // weight index -> device fp32 copy
 
@@ -716,6 +718,86 @@ struct PlanBuilder {
         }
     }
 
+    // Attention products (MatMul mode 2): a Transpose whose only reader is the product
+    // is not materialised (the product reads its input through permuted strides), and
+    // a Mul by a scalar constant that is the product's only reader is applied to the
+    // product's sums (out = sum * s, the reference's separate Mul rounding once the
+    // same way).
+    void fold_attention() {
+        for (size_t i = 0; i < nodes.size(); ++i) {
+            if (skip[i] || nodes[i].op != Op::MatMul || note[i].mode != 2) continue;
+            for (int side = 0; side < 2; ++side) {
+                const int32_t t = nodes[i].inputs[side];
+                if (consumers[t] != 1) continue;
+                const int k = producer_node(t);
+                if (k < 0 || nodes[k].op != Op::Transpose || note[k].mode != 1) continue;
+                if (V[input_vid(nodes[k], 0)].shape.size() != 4) continue;
+                skip[k] = 1;
+                folded_transpose[vid[t]] = k;
+            }
+            const int32_t ot = nodes[i].outputs[0];
+            if (consumers[ot] != 1) continue;
+            for (size_t m = i + 1; m < nodes.size(); ++m) {
+                const Node& mn = nodes[m];
+                if (skip[m] || mn.op != Op::Mul || mn.inputs.size() != 2) continue;
+                const int side = mn.inputs[0] == ot ? 0 : (mn.inputs[1] == ot ? 1 : -1);
+                if (side < 0) continue;
+                const int sv = vid[mn.inputs[1 - side]];
+                const int mo = vid[mn.outputs[0]];
+                if (V[sv].weight >= 0 && numel_of(V[sv].shape) == 1 && V[mo].shape == V[vid[ot]].shape &&
+                    V[mo].dt == F32) {
+                    note[i].scale = (float)g.weights[V[sv].weight].value(0);
+                    nodes[i].outputs[0] = mn.outputs[0];
+                    V[mo].producer = (int)i;
+                    skip[m] = 1;
+                }
+                break;
+            }
+        }
+    }
+
+    // Tensor-core convs need Cout % 16 == 0 and >= 32-byte channel rows. A conv with
+    // a narrow output (e.g. the 8-channel bottleneck of a YOLO11n C3k2) whose only
+    // readers are convs gets its output stored with Cout rounded up to 16 (zero
+    // weights and bias in the extra channels, whose activation is then exactly 0) and
+    // each reader gets zero weights for those channels: both run on tcgen05 instead of
+    // the SIMT kernels, with the same values (an exact 0 adds nothing to a sum).
+    // FP32 plans keep the strict SIMT path and are not padded.
+    void pad_narrow_channels() {
+        if (prec == PREC_FP32) return;
+        const char* off = std::getenv("PDEFA_NO_CHANNEL_PAD");
+        if (off && *off && *off != '0') return;
+        auto conv_reader = [&](size_t k, int32_t t) {
+            const Node& c = nodes[k];
+            if (c.op != Op::Conv2d || skip[k] || note[k].mode != 0 || note[k].dfl_fix) return false;
+            if ((c.params.groups > 0 ? c.params.groups : 1) != 1) return false;
+            for (size_t j = 1; j < c.inputs.size(); ++j) if (c.inputs[j] == t) return false;
+            return c.inputs[0] == t;
+        };
+        for (size_t i = 0; i < nodes.size(); ++i) {
+            const Node& n = nodes[i];
+            if (n.op != Op::Conv2d || skip[i] || note[i].mode != 0 || note[i].dfl_fix || conv_res[i] >= 0) continue;
+            if ((n.params.groups > 0 ? n.params.groups : 1) != 1) continue;
+            const int act = conv_act[i];
+            if (act != ACT_NONE && act != ACT_RELU && act != ACT_LEAKY && act != ACT_SILU) continue;
+            const int32_t t = n.outputs[0];
+            const int o = vid[t];
+            auto& sh = V[o].shape;
+            if (sh.size() != 4 || sh[3] % 16 == 0 || sh[3] > 256 || is_graph_output(o)) continue;
+            int readers = 0;
+            bool ok = true;
+            for (size_t k = 0; k < nodes.size() && ok; ++k) {
+                if (k == i || nodes[k].op == Op::Input) continue;
+                bool reads = false;
+                for (int32_t in : nodes[k].inputs) reads |= in == t;
+                if (!reads) continue;
+                if (conv_reader(k, t)) ++readers;
+                else ok = false;
+            }
+            if (ok && readers > 0) sh[3] = (sh[3] + 15) / 16 * 16;
+        }
+    }
+
     // -------------------------------------------------------------------
     // 5. placement
     bool is_graph_output(int v) {
@@ -1189,7 +1271,8 @@ struct PlanBuilder {
         const int o = vid[n.outputs[0]];
         const Weight& W = wt(w);
         const auto& ws = W.shape;
-        const int64_t Co = ws[0], Ci = ws[1], KH = ws[2], KW = ws[3];
+        int64_t Co = ws[0], Ci = ws[1];
+        const int64_t KH = ws[2], KW = ws[3];
         const float* bias = nullptr;
         if (bv >= 0) {
             const Weight& bw = wt(bv);
@@ -1283,6 +1366,29 @@ struct PlanBuilder {
         const float* wf = W.f32();
         std::vector<float> wtmp;
         if (!wf) { wtmp.resize(W.numel()); for (int64_t i = 0; i < W.numel(); ++i) wtmp[i] = (float)W.value(i); wf = wtmp.data(); }
+        // channels padded by pad_narrow_channels: zero weights (and bias) for them
+        const int64_t Co_e = (nt.mode == 0 && !nt.dfl_fix && V[o].shape.size() == 4) ? V[o].shape[3] : Co;
+        const int64_t Ci_e = (nt.mode == 0 && !nt.dfl_fix && V[x].shape.size() == 4) ? V[x].shape[3] : Ci;
+        std::vector<float> wpad;
+        if ((Co_e > Co || Ci_e > Ci) && Co_e >= Co && Ci_e >= Ci) {
+            wpad.assign((size_t)Co_e * Ci_e * KH * KW, 0.0f);
+            for (int64_t co = 0; co < Co; ++co)
+                for (int64_t ci = 0; ci < Ci; ++ci)
+                    for (int64_t r = 0; r < KH * KW; ++r)
+                        wpad[((size_t)co * Ci_e + ci) * KH * KW + r] = wf[((size_t)co * Ci + ci) * KH * KW + r];
+            if (bias && Co_e > Co) {
+                std::vector<float> bp((size_t)Co_e, 0.0f);
+                const Weight& bw = wt(bv);
+                for (int64_t c = 0; c < Co; ++c) bp[c] = (float)bw.value(c);
+                void* db = P.alloc(bp.size() * 4);
+                if (!P.dry_) PB_CUDA(cudaMemcpy(db, bp.data(), bp.size() * 4, cudaMemcpyHostToDevice));
+                a.bias = static_cast<const float*>(db);
+            }
+            wf = wpad.data();
+            Co = Co_e;
+            Ci = Ci_e;
+            a.cin = (int)Ci; a.cout = (int)Co;
+        }
         bool tc = false;
         const char* why = "fp32 precision";
         const int op_dt = prec == PREC_BF16 ? BF16 : F32;
@@ -1377,25 +1483,41 @@ struct PlanBuilder {
         const Node& n = nodes[ni];
         const int a = input_vid(n, 0), w = input_vid(n, 1), o = vid[n.outputs[0]];
         const int bv = n.inputs.size() > 2 ? input_vid(n, 2) : -1;
-        TView A = dense_f32(a, n.name + "/a");
-        TView Wt = dense_f32(w, n.name + "/b");
         TView O = view(o);
         const auto as = V[a].shape;
         const auto wsh = V[w].shape;
         if (note[ni].mode == 2) {
-            const int64_t M = as[1], K = as[2], N = wsh[2], H = as[3], nb = B * as[0];
+            const int64_t M = as[1], K = as[2], N = wsh[2], H = as[3];
+            if (as[0] != 1) fail(ENGINE_ERR_NOT_IMPL, "MatMul '" + n.name + "': batched 4-D product with a leading dimension > 1");
             const bool odense = dense(o) && V[o].dt == F32;
             float* op = static_cast<float*>(const_cast<void*>(O.ptr));
-            float* tmp = odense ? op : static_cast<float*>(P.alloc(std::max<size_t>((size_t)nb * M * N * H * 4, 16)));
-            const float* ap = static_cast<const float*>(A.ptr);
-            const float* bp = static_cast<const float*>(Wt.ptr);
-            // a constant operand (img_stride 0) is shared by every image
-            if ((A.img_stride == 0 || Wt.img_stride == 0) && as[0] != 1)
-                fail(ENGINE_ERR_NOT_IMPL, "MatMul '" + n.name + "': constant operand with a batch dimension");
-            const int64_t sa = A.img_stride == 0 ? 0 : M * K * H, sb = Wt.img_stride == 0 ? 0 : K * N * H;
+            float* tmp = odense ? op : static_cast<float*>(P.alloc(std::max<size_t>((size_t)B * M * N * H * 4, 16)));
+            // operand views: the value itself, or the input of a folded Transpose with its
+            // dimensions permuted
+            auto operand = [&](int v) {
+                TView t;
+                auto it = folded_transpose.find(v);
+                if (it != folded_transpose.end()) {
+                    const Node& tn = nodes[it->second];
+                    const TView src = view(input_vid(tn, 0));
+                    t = src;
+                    for (int d = 0; d < 4; ++d) { t.shape[d] = src.shape[note[it->second].a[d]]; t.stride[d] = src.stride[note[it->second].a[d]]; }
+                } else {
+                    t = view(v);
+                }
+                HeadOperand h;
+                h.p = t.ptr;
+                h.bf = t.dt == BF16;
+                h.s1 = t.stride[1]; h.s2 = t.stride[2]; h.s3 = t.stride[3];
+                h.sb = t.img_stride;
+                return h;
+            };
+            const HeadOperand ha = operand(a), hb = operand(w);
+            const float scale = note[ni].scale;
+            const int64_t nb = B;
             kind("matmul_heads");
             add_step(n.name, [=](cudaStream_t s) {
-                launch_matmul_heads(ap, bp, tmp, nb, M, K, N, H, sa, sb, M * N * H, s);
+                launch_matmul_heads(ha, hb, tmp, nb, M, K, N, H, scale, M * N * H, s);
             });
             if (!odense) {
                 TView src = O;
@@ -1407,6 +1529,8 @@ struct PlanBuilder {
             }
             return;
         }
+        TView A = dense_f32(a, n.name + "/a");
+        TView Wt = dense_f32(w, n.name + "/b");
         int64_t M, K = wsh[0], N = wsh[1];
         if (note[ni].mode == 1) M = as[0] * as[1] * as[2]; else M = as[0];
         const float* bias = nullptr;
@@ -1440,6 +1564,8 @@ struct PlanBuilder {
         infer();
         match_head();
         fuse_residuals();
+        fold_attention();
+        pad_narrow_channels();
         place();
         emit();
         if (verbose()) {

@@ -108,11 +108,17 @@ void launch_conv_tc(const ConvArgs& a, int op_dt, int* err, cudaStream_t s);
 void launch_gemm_f32(const float* A, const float* B, float* C, const float* bias,
                      int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc,
                      int64_t batch, int64_t sA, int64_t sB, int64_t sC, cudaStream_t s);
-// Attention MatMul on head-last 4-D tensors: C[b,i,j,h] = sum_k A[b,i,k,h] * B[b,k,j,h]
-// (A: [batch][M][K][H], B: [batch][K][N][H], C: [batch][M][N][H], dense; batch
-// strides sA/sB/sC); fp32 fma over k in ascending order.
-void launch_matmul_heads(const float* A, const float* B, float* C, int64_t batch, int64_t M, int64_t K,
-                         int64_t N, int64_t H, int64_t sA, int64_t sB, int64_t sC, cudaStream_t s);
+// Attention MatMul on head-last 4-D tensors: C[b,i,j,h] = scale * sum_k A[b,i,k,h] * B[b,k,j,h]
+// (fp32 fma over k in ascending order). Operands are strided views: element (b, r, c, h)
+// of an operand is at p[b*sb + r*s1 + c*s2 + h*s3], fp32 or bf16 (bf = 1). C is dense
+// [batch][M][N][H] with batch stride sC.
+struct HeadOperand {
+    const void* p = nullptr;
+    int bf = 0;
+    int64_t s1 = 0, s2 = 0, s3 = 0, sb = 0;
+};
+void launch_matmul_heads(const HeadOperand& A, const HeadOperand& B, float* C, int64_t batch, int64_t M, int64_t K,
+                         int64_t N, int64_t H, float scale, int64_t sC, cudaStream_t s);
 // Tensor-core GEMM for ops_matmul (TF32 or BF16 operands, fp32 accumulate/output).
 // scratch must hold M*K + N*K operand-sized elements.
 void launch_gemm_tc(const float* A, const float* B, float* C, int64_t M, int64_t N, int64_t K,

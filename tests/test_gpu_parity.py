@@ -377,3 +377,32 @@ def test_grouped_conv_against_reference_engine(engine_dir, prec, cin, cout, k, s
         for i in range(3):
             r = R.RefSession(p).run(x[i:i + 1])
             assert normwise(y[i:i + 1], r) <= TOL[prec]
+
+
+@pytest.mark.parametrize("prec", [pb.FP32, pb.BF16])
+def test_depthwise3x3_kernel_equals_generic(engine_dir, prec):
+    """The depthwise 3x3 kernel (two channels x four rows per thread) sums each output
+    in the generic grouped kernel's order: identical bits, stride 1 and 2, odd sizes,
+    fused SiLU and a residual."""
+    from pdefa_b200.engine_file import TensorInfo
+    from pdefa_b200.yolo import _Builder
+    b = _Builder(4)
+    g = b.g
+    g.graph_inputs = [-1]
+    g.input_infos = [TensorInfo("images", [1, 8, 37, 29])]
+    y, s = b.conv(-1, (8, 37, 29), 48, 1, 1, "m.0")
+    z, s = b.conv(y, s, 48, 3, 1, "m.1", groups=48)
+    (z,) = g.add_node('Add', "/m.1/Add", [y, z])
+    z, s = b.conv(z, s, 48, 3, 2, "m.2", groups=48)
+    z, s = b.conv(z, s, 48, 3, 1, "m.3", groups=48, act=False)
+    g.graph_outputs = [z]
+    g.output_infos = [TensorInfo("output0", [1, 48, s[1], s[2]])]
+    p = str(engine_dir / "dw_chain.engine")
+    write_engine(p, g)
+    x = np.random.default_rng(9).random((3, 8, 37, 29), dtype=np.float32) - 0.5
+    fast = run_engine(p, x, prec)
+    generic = run_engine(p, x, prec, env={"PDEFA_NO_DW3": "1"})
+    np.testing.assert_array_equal(fast, generic)
+    if R.available():
+        for i in range(3):
+            assert normwise(fast[i:i + 1], R.RefSession(p).run(x[i:i + 1])) <= TOL[prec]

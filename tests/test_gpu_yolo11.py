@@ -104,3 +104,14 @@ def test_yolo11n_batch_inference_detect(engine_dir):
             assert a["cls"] == b["cls"]
             np.testing.assert_allclose([a[k] for k in ("x1", "y1", "x2", "y2", "conf")],
                                        [b[k] for k in ("x1", "y1", "x2", "y2", "conf")], rtol=1e-6, atol=1e-4)
+
+
+@pytest.mark.parametrize("prec", [pb.TF32, pb.BF16])
+def test_yolo11n_channel_padding_and_folds_keep_results(engine_dir, prec):
+    """Padding the 8-channel convs to 16 for tcgen05 changes only the accumulation
+    blocking: the outputs stay within the tensor-core tolerance of the unpadded plan."""
+    p = _engine(engine_dir, "y11n_128p.engine", build_yolo11("n", imgsz=128, seed=0)[0])
+    x = _x(4, (2, 3, 128, 128))
+    padded = run_engine(p, x, prec)
+    plain = run_engine(p, x, prec, env={"PDEFA_NO_CHANNEL_PAD": "1"})
+    assert normwise(padded, plain) <= 5e-3

@@ -79,7 +79,11 @@ def test_yolo11n_plan_lowers_attention(tmp_path):
     m = pb.Model(pb.Context(), p)
     for prec in (pb.BF16, pb.TF32, pb.FP32):
         kinds = Counter(k for k, _ in m.plan_summary(prec, batch=8))
-        assert kinds["matmul_heads"] == 2 and kinds["softmax"] == 1 and kinds["binary"] == 1
+        # the scale Mul and both Transposes fold into the attention products
+        assert kinds["matmul_heads"] == 2 and kinds["softmax"] == 1 and kinds["binary"] == 0
         assert kinds["conv_grouped"] == 7 and kinds["yolo_head"] == 1 and kinds["resize"] == 2
+    # the 8-channel C3k2 bottleneck convs (16->8 1x1, 8->16 3x3) are padded to 16
+    # channels and join the other 77 convs on tcgen05
     kinds = Counter(k for k, _ in m.plan_summary(pb.BF16, batch=8))
-    assert kinds["conv_stem_tc"] == 1 and kinds["conv_tc_bf16"] == 77
+    assert kinds["conv_stem_tc"] == 1 and kinds["conv_tc_bf16"] == 79 and kinds["conv_simt"] == 0
+    assert kinds["conv_direct"] == 0
