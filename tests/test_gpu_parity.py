@@ -358,6 +358,25 @@ def test_batch_inference_pipelined_micro_batches(y8n_128):
             [(r["x1"], r["y1"], r["x2"], r["y2"], float(r["conf"]), int(r["cls"])) for r in d_ref[b, :c_ref[b]]]
 
 
+def test_batch_inference_shards_across_devices(y8n_128):
+    """The batch split over every visible GPU (one replica and one native thread per
+    device, contiguous shards, no collective) returns, image for image, what one GPU
+    returns. Needs two or more GPUs."""
+    n = pb.device_count()
+    if n < 2:
+        pytest.skip("needs two or more GPUs")
+    ctx = pb.Context(precision=pb.BF16)
+    m = pb.Model(ctx, y8n_128)
+    x = np.random.default_rng(13).random((2 * n + 1, 3, 128, 128), dtype=np.float32)
+    with pb.BatchInference(ctx, m, batch_size=2, devices=[0]) as bi:
+        c_ref, d_ref = bi.detect_arrays(x, conf_thres=0.2, iou_thres=0.5, max_det=50)
+    with pb.BatchInference(ctx, m, batch_size=2, devices=list(range(n))) as bi:
+        c, d = bi.detect_arrays(x, conf_thres=0.2, iou_thres=0.5, max_det=50)
+    np.testing.assert_array_equal(c, c_ref)
+    for b in range(len(x)):
+        np.testing.assert_array_equal(d[b, :c[b]], d_ref[b, :c_ref[b]])
+
+
 # ------------------------------------------------------------- grouped / depthwise conv
 @pytest.mark.parametrize("prec", PRECS)
 @pytest.mark.parametrize("cin,cout,k,s,groups,hw", [(16, 16, 3, 1, 16, 40), (64, 64, 3, 2, 64, 33),
