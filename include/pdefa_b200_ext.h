@@ -164,6 +164,24 @@ ENGINE_API EngineStatus pdefa_batch_run_u8(PdefaBatchRunner* runner, const uint8
                                            const PdefaPreprocessConfig* cfg, double conf_thres, double iou_thres,
                                            int32_t max_det, int32_t* out_counts, PdefaDetection* out_dets,
                                            PdefaPreprocessMeta* out_meta);
+/* Pipelined form of pdefa_batch_run_u8 (no counterpart in the reference, whose
+ * BatchInference.run in pdefa/python/src/pdefa/batch.py:45-60 blocks per call). The
+ * call returns once its copies, letterbox, inference and decode are queued, so the
+ * next call's image copies overlap this call's last micro-batches. *out_ticket
+ * numbers the call. Its results are in out_counts / out_dets once
+ * pdefa_batch_wait(runner, ticket) returns, or once a later submit or run on the same
+ * runner returns. Until then, images, out_counts and out_dets must stay allocated and
+ * unchanged. out_meta is written before the call returns. pdefa_batch_destroy
+ * drops results that are still pending. */
+ENGINE_API EngineStatus pdefa_batch_submit_u8(PdefaBatchRunner* runner, const uint8_t* images, int64_t n_images,
+                                              int32_t src_h, int32_t src_w, int32_t channels,
+                                              const PdefaPreprocessConfig* cfg, double conf_thres,
+                                              double iou_thres, int32_t max_det, int32_t* out_counts,
+                                              PdefaDetection* out_dets, PdefaPreprocessMeta* out_meta,
+                                              int64_t* out_ticket);
+/* Completes every queued call up to and including `ticket` (all of them when
+ * ticket <= 0): their results land in the arrays they were given. */
+ENGINE_API EngineStatus pdefa_batch_wait(PdefaBatchRunner* runner, int64_t ticket);
 
 #ifdef __cplusplus
 }

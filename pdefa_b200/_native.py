@@ -121,6 +121,9 @@ _SIGS = {
     "pdefa_batch_destroy": ([vp], None),
     "pdefa_batch_run_u8": ([vp, vp, i64, i32, i32, i32, P(PreConfig), f64, f64, i32, P(i32), P(Detection),
                             P(PreMeta)], C.c_int),
+    "pdefa_batch_submit_u8": ([vp, vp, i64, i32, i32, i32, P(PreConfig), f64, f64, i32, P(i32), P(Detection),
+                               P(PreMeta), P(i64)], C.c_int),
+    "pdefa_batch_wait": ([vp, i64], C.c_int),
     "pdefa_letterbox_meta": ([i32, i32, P(PreConfig), P(PreMeta)], C.c_int),
     "pdefa_letterbox_device": ([vp, i64, i32, i32, i32, P(PreConfig), vp, vp], C.c_int),
     "pdefa_letterbox": ([vp, i64, i32, i32, i32, P(PreConfig), vp, P(PreMeta), i32], C.c_int),

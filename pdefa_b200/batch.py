@@ -91,6 +91,39 @@ class BatchInference:
                                           dets.ctypes.data_as(C.POINTER(N.Detection)), C.byref(m)), "batch_run_u8")
         return counts[:n], dets[:n, :md], PreprocessMeta.from_c(m)
 
+    def submit_u8(self, images, target_w: int = 640, target_h: int = 640, scale: float = 1.0 / 255.0,
+                  pad_value: float = 0.0, conf_thres: float = 0.25, iou_thres: float = 0.45,
+                  max_det: int = 300) -> "PendingDetections":
+        """detect_u8 without waiting: the frames are queued (copies, GPU letterbox,
+        inference, decode) and a PendingDetections comes back at once; its result()
+        gives what detect_u8 would have returned. Submitting the next frames before
+        asking for the result lets their copies onto the GPU overlap the end of this
+        call's work. The pending object keeps `images` and its output arrays alive;
+        the caller must not modify `images` until result() returns."""
+        import numpy as np
+        a = np.ascontiguousarray(images, dtype=np.uint8)
+        if a.ndim == 3:
+            a = a[..., None]
+        if a.ndim != 4 or a.shape[3] not in (1, 3, 4):
+            raise PdefaError("submit_u8: images must be uint8 [N, h, w] or [N, h, w, C] with C = 1, 3 or 4")
+        n, h, w, ch = a.shape
+        md = max(int(max_det), 0)
+        counts = np.zeros(max(n, 1), dtype=np.int32)
+        dets = np.zeros((max(n, 1), max(md, 1)), dtype=self.DET_DTYPE)
+        m = N.PreMeta()
+        cfg = N.PreConfig(int(target_w), int(target_h), float(scale), float(pad_value))
+        ticket = C.c_int64(0)
+        _check(N.lib().pdefa_batch_submit_u8(self._handle, a.ctypes.data, n, h, w, ch, C.byref(cfg),
+                                             float(conf_thres), float(iou_thres), md,
+                                             counts.ctypes.data_as(C.POINTER(N.i32)),
+                                             dets.ctypes.data_as(C.POINTER(N.Detection)), C.byref(m),
+                                             C.byref(ticket)), "batch_submit_u8")
+        return PendingDetections(self, ticket.value, a, counts[:n], dets[:n, :md], PreprocessMeta.from_c(m))
+
+    def wait(self):
+        """Completes every call queued by submit_u8 so far."""
+        _check(N.lib().pdefa_batch_wait(self._handle, 0), "batch_wait")
+
     def detect(self, images, metas: Optional[Sequence[PreprocessMeta]] = None, conf_thres: float = 0.25,
                iou_thres: float = 0.45, max_det: int = 300) -> List[List[dict]]:
         """images: [N, 3, H, W] float32 array -> per-image detection dicts
@@ -131,3 +164,21 @@ class BatchInference:
 
     def __exit__(self, *args):
         self.close()
+
+
+class PendingDetections:
+    """Results of one BatchInference.submit_u8 call. result() waits for this call only
+    (and for the calls queued before it) and returns (counts, dets, meta) as
+    detect_u8 does."""
+
+    def __init__(self, runner: BatchInference, ticket: int, images, counts, dets, meta):
+        self._runner, self.ticket, self._images = runner, ticket, images
+        self._counts, self._dets, self.meta = counts, dets, meta
+        self._done = False
+
+    def result(self):
+        if not self._done:
+            _check(N.lib().pdefa_batch_wait(self._runner._handle, self.ticket), "batch_wait")
+            self._done = True
+            self._images = None
+        return self._counts, self._dets, self.meta

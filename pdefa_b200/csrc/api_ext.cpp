@@ -72,11 +72,17 @@ struct PdefaBatchRunner {
         void* meta = nullptr;
         int32_t* h_counts = nullptr; // pinned host mirrors
         PdefaDetection* h_dets = nullptr;
+        PdefaPreprocessMeta* h_meta = nullptr;   // pinned staging of the micro-batch's meta records
         size_t dets_cap = 0;
         cudaEvent_t h2d = nullptr, ran = nullptr, done = nullptr;
         cudaStream_t compute = nullptr;  // letterbox + inference of this lane's micro-batches
         bool busy = false;           // results of (c0, nb) pending
         int64_t c0 = 0, nb = 0;
+        // where the pending results go: the arrays of the call (ticket) that queued them
+        int64_t ticket = 0;
+        int32_t* dst_counts = nullptr;
+        PdefaDetection* dst_dets = nullptr;
+        int32_t dst_max_det = 0;
         void* pixels = nullptr;      // device copy of an 8-bit micro-batch (pdefa_batch_run_u8)
         size_t pixels_cap = 0;
     };
@@ -87,25 +93,38 @@ struct PdefaBatchRunner {
         cudaStream_t copy = nullptr;     // image copies onto the GPU
         cudaStream_t post = nullptr;     // decode + result copies (overlap the next inference)
         Lane lanes[2];
+        int64_t next_lane = 0;           // lanes alternate across calls too
     };
     std::shared_ptr<const Graph> graph;
     int precision = PREC_BF16;
     int64_t max_per_device = 1;
     std::vector<Replica> reps;
+    int64_t tickets = 0;                 // calls queued so far (pdefa_batch_submit_u8 returns the number)
 };
 
 namespace {
 
 void free_lane(PdefaBatchRunner::Lane& l) {
     if (l.counts) { cudaFree(l.counts); cudaFree(l.dets); cudaFree(l.work); cudaFree(l.meta); }
-    if (l.h_counts) { cudaFreeHost(l.h_counts); cudaFreeHost(l.h_dets); }
+    if (l.h_counts) { cudaFreeHost(l.h_counts); cudaFreeHost(l.h_dets); cudaFreeHost(l.h_meta); }
     if (l.pixels) cudaFree(l.pixels);
     l.pixels = nullptr;
     l.pixels_cap = 0;
     l.counts = l.dets = l.work = l.meta = nullptr;
     l.h_counts = nullptr;
     l.h_dets = nullptr;
+    l.h_meta = nullptr;
     l.dets_cap = 0;
+}
+
+// A lane's finished micro-batch -> the arrays of the call that queued it.
+void retire_lane(PdefaBatchRunner::Lane& l) {
+    if (!l.busy) return;
+    l.busy = false;
+    PB_CUDA(cudaEventSynchronize(l.done));
+    std::memcpy(l.dst_counts + l.c0, l.h_counts, (size_t)l.nb * 4);
+    if (l.dst_max_det > 0)
+        std::memcpy(l.dst_dets + l.c0 * l.dst_max_det, l.h_dets, (size_t)l.nb * l.dst_max_det * sizeof(PdefaDetection));
 }
 
 }  // namespace
@@ -376,12 +395,20 @@ PdefaPreprocessMeta meta_of(const LetterboxGeom& g) {
     return m;
 }
 
+// drain = true: the call returns with its results in out_counts / out_dets. drain =
+// false (pdefa_batch_submit_u8): the call returns once its work is queued; its last
+// micro-batches finish later and are copied out when their lane is reused, by a later
+// call, or by pdefa_batch_wait. Either way, results of earlier calls still pending in
+// a lane are copied to those calls' arrays before the lane is reused, and every
+// earlier call is complete when this one returns.
 EngineStatus run_batch(PdefaBatchRunner* r, const BatchInput& in, int64_t n_images, const PdefaPreprocessMeta* metas,
                        double conf_thres, double iou_thres, int32_t max_det, int32_t* out_counts,
-                       PdefaDetection* out_dets) {
+                       PdefaDetection* out_dets, bool drain = true, int64_t* out_ticket = nullptr) {
     return guarded([&]() -> EngineStatus {
         clear_error();
         if (max_det < 0) return ENGINE_ERR_INVALID_ARG;
+        const int64_t ticket = ++r->tickets;
+        if (out_ticket) *out_ticket = ticket;
         const int nd = (int)r->reps.size();
         const int64_t per = (n_images + nd - 1) / nd;
         std::vector<std::string> errs(nd);
@@ -389,15 +416,7 @@ EngineStatus run_batch(PdefaBatchRunner* r, const BatchInput& in, int64_t n_imag
         for (int d = 0; d < nd; ++d) {
             th.emplace_back([&, d] {
                 auto& rp = r->reps[d];
-                // results of a lane's finished micro-batch -> the caller's arrays
-                auto retire = [&](PdefaBatchRunner::Lane& l) {
-                    if (!l.busy) return;
-                    l.busy = false;
-                    PB_CUDA(cudaEventSynchronize(l.done));
-                    std::memcpy(out_counts + l.c0, l.h_counts, (size_t)l.nb * 4);
-                    if (max_det > 0)
-                        std::memcpy(out_dets + l.c0 * max_det, l.h_dets, (size_t)l.nb * max_det * sizeof(PdefaDetection));
-                };
+                auto retire = [](PdefaBatchRunner::Lane& l) { retire_lane(l); };
                 try {
                     PB_CUDA(cudaSetDevice(rp.device));
                     const int64_t lo = std::min(n_images, d * per), hi = std::min(n_images, lo + per);
@@ -411,7 +430,7 @@ EngineStatus run_batch(PdefaBatchRunner* r, const BatchInput& in, int64_t n_imag
                     int64_t i = 0;
                     for (int64_t c0 = lo, nb = 0; c0 < hi; c0 += nb, ++i) {
                         nb = std::min(i == 0 ? mfirst : mfull, hi - c0);
-                        auto& l = rp.lanes[i & 1];
+                        auto& l = rp.lanes[rp.next_lane++ & 1];
                         retire(l);    // the lane's buffers are free once its previous micro-batch is done
                         auto it = l.plans.find(nb);
                         if (it == l.plans.end())
@@ -430,6 +449,8 @@ EngineStatus run_batch(PdefaBatchRunner* r, const BatchInput& in, int64_t n_imag
                             PB_CUDA(cudaMalloc(&l.meta, cap_imgs * sizeof(PdefaPreprocessMeta)));
                             PB_CUDA(cudaMallocHost(reinterpret_cast<void**>(&l.h_counts), cap_imgs * 4));
                             PB_CUDA(cudaMallocHost(reinterpret_cast<void**>(&l.h_dets), need));
+                            PB_CUDA(cudaMallocHost(reinterpret_cast<void**>(&l.h_meta),
+                                                   cap_imgs * sizeof(PdefaPreprocessMeta)));
                             l.dets_cap = need;
                         }
                         const size_t ibytes = p.input_bytes(0);
@@ -463,7 +484,10 @@ EngineStatus run_batch(PdefaBatchRunner* r, const BatchInput& in, int64_t n_imag
                         // next micro-batch's convolutions
                         PB_CUDA(cudaEventRecord(l.ran, l.compute));
                         PB_CUDA(cudaStreamWaitEvent(rp.post, l.ran, 0));
-                        decode_on_device(p.output_buffer(0), nb, ch, A, metas ? metas + c0 : nullptr, conf_thres,
+                        // meta records via pinned staging: the copy needs no wait for the
+                        // decode stream (a pageable source would make the host wait for it)
+                        if (metas) std::memcpy(l.h_meta, metas + c0, (size_t)nb * sizeof(PdefaPreprocessMeta));
+                        decode_on_device(p.output_buffer(0), nb, ch, A, metas ? l.h_meta : nullptr, conf_thres,
                                          iou_thres, max_det, static_cast<int32_t*>(l.counts), l.dets, l.work,
                                          static_cast<int32_t*>(l.meta), device_error_word(rp.device), rp.post);
                         PB_CUDA(cudaMemcpyAsync(l.h_counts, l.counts, nb * 4, cudaMemcpyDeviceToHost, rp.post));
@@ -474,10 +498,17 @@ EngineStatus run_batch(PdefaBatchRunner* r, const BatchInput& in, int64_t n_imag
                         l.busy = true;
                         l.c0 = c0;
                         l.nb = nb;
+                        l.ticket = ticket;
+                        l.dst_counts = out_counts;
+                        l.dst_dets = out_dets;
+                        l.dst_max_det = max_det;
                     }
-                    retire(rp.lanes[i & 1]);
-                    retire(rp.lanes[(i + 1) & 1]);
-                    if (read_device_error(rp.device)) fail(ENGINE_ERR_RUNTIME, "device-side wait timed out");
+                    // oldest lane first; a submit leaves its own micro-batches pending
+                    for (int k = 0; k < 2; ++k) {
+                        auto& l = rp.lanes[(rp.next_lane + k) & 1];
+                        if (drain || l.ticket < ticket) retire(l);
+                    }
+                    if (drain && read_device_error(rp.device)) fail(ENGINE_ERR_RUNTIME, "device-side wait timed out");
                 } catch (const std::exception& e) {
                     errs[d] = e.what();
                     // leave no lane pending: its buffers may be reused by the next call
@@ -502,21 +533,12 @@ EngineStatus run_batch(PdefaBatchRunner* r, const BatchInput& in, int64_t n_imag
 
 }  // namespace
 
-extern "C" {
+namespace {
 
-ENGINE_API EngineStatus pdefa_batch_run(PdefaBatchRunner* r, const float* images, int64_t n_images,
-                                        const PdefaPreprocessMeta* metas, double conf_thres, double iou_thres,
-                                        int32_t max_det, int32_t* out_counts, PdefaDetection* out_dets) {
-    if (!r || !images || !out_counts || (!out_dets && max_det > 0)) return ENGINE_ERR_NULL_PTR;
-    BatchInput in;
-    in.f32 = images;
-    return run_batch(r, in, n_images, metas, conf_thres, iou_thres, max_det, out_counts, out_dets);
-}
-
-ENGINE_API EngineStatus pdefa_batch_run_u8(PdefaBatchRunner* r, const uint8_t* images, int64_t n_images, int32_t src_h,
-                                           int32_t src_w, int32_t channels, const PdefaPreprocessConfig* cfg,
-                                           double conf_thres, double iou_thres, int32_t max_det, int32_t* out_counts,
-                                           PdefaDetection* out_dets, PdefaPreprocessMeta* out_meta) {
+EngineStatus batch_u8(PdefaBatchRunner* r, const uint8_t* images, int64_t n_images, int32_t src_h, int32_t src_w,
+                      int32_t channels, const PdefaPreprocessConfig* cfg, double conf_thres, double iou_thres,
+                      int32_t max_det, int32_t* out_counts, PdefaDetection* out_dets, PdefaPreprocessMeta* out_meta,
+                      bool drain, int64_t* out_ticket) {
     if (!r || !images || !cfg || !out_counts || (!out_dets && max_det > 0)) return ENGINE_ERR_NULL_PTR;
     return guarded([&]() -> EngineStatus {
         clear_error();
@@ -533,7 +555,56 @@ ENGINE_API EngineStatus pdefa_batch_run_u8(PdefaBatchRunner* r, const uint8_t* i
         if (out_meta) *out_meta = m;
         // boxes come back in original-image coordinates, as decode_yolo(out, meta) gives them
         std::vector<PdefaPreprocessMeta> metas((size_t)std::max<int64_t>(n_images, 1), m);
-        return run_batch(r, in, n_images, metas.data(), conf_thres, iou_thres, max_det, out_counts, out_dets);
+        return run_batch(r, in, n_images, metas.data(), conf_thres, iou_thres, max_det, out_counts, out_dets, drain,
+                         out_ticket);
+    });
+}
+
+}  // namespace
+
+extern "C" {
+
+ENGINE_API EngineStatus pdefa_batch_run(PdefaBatchRunner* r, const float* images, int64_t n_images,
+                                        const PdefaPreprocessMeta* metas, double conf_thres, double iou_thres,
+                                        int32_t max_det, int32_t* out_counts, PdefaDetection* out_dets) {
+    if (!r || !images || !out_counts || (!out_dets && max_det > 0)) return ENGINE_ERR_NULL_PTR;
+    BatchInput in;
+    in.f32 = images;
+    return run_batch(r, in, n_images, metas, conf_thres, iou_thres, max_det, out_counts, out_dets);
+}
+
+ENGINE_API EngineStatus pdefa_batch_run_u8(PdefaBatchRunner* r, const uint8_t* images, int64_t n_images, int32_t src_h,
+                                           int32_t src_w, int32_t channels, const PdefaPreprocessConfig* cfg,
+                                           double conf_thres, double iou_thres, int32_t max_det, int32_t* out_counts,
+                                           PdefaDetection* out_dets, PdefaPreprocessMeta* out_meta) {
+    return batch_u8(r, images, n_images, src_h, src_w, channels, cfg, conf_thres, iou_thres, max_det, out_counts,
+                    out_dets, out_meta, true, nullptr);
+}
+
+ENGINE_API EngineStatus pdefa_batch_submit_u8(PdefaBatchRunner* r, const uint8_t* images, int64_t n_images,
+                                              int32_t src_h, int32_t src_w, int32_t channels,
+                                              const PdefaPreprocessConfig* cfg, double conf_thres, double iou_thres,
+                                              int32_t max_det, int32_t* out_counts, PdefaDetection* out_dets,
+                                              PdefaPreprocessMeta* out_meta, int64_t* out_ticket) {
+    if (!out_ticket) return ENGINE_ERR_NULL_PTR;
+    return batch_u8(r, images, n_images, src_h, src_w, channels, cfg, conf_thres, iou_thres, max_det, out_counts,
+                    out_dets, out_meta, false, out_ticket);
+}
+
+ENGINE_API EngineStatus pdefa_batch_wait(PdefaBatchRunner* r, int64_t ticket) {
+    if (!r) return ENGINE_ERR_NULL_PTR;
+    return guarded([&]() -> EngineStatus {
+        clear_error();
+        const int64_t upto = ticket > 0 ? ticket : r->tickets;
+        for (auto& rp : r->reps) {
+            PB_CUDA(cudaSetDevice(rp.device));
+            for (int k = 0; k < 2; ++k) {
+                auto& l = rp.lanes[(rp.next_lane + k) & 1];    // oldest first
+                if (l.busy && l.ticket <= upto) retire_lane(l);
+            }
+            if (read_device_error(rp.device)) fail(ENGINE_ERR_RUNTIME, "device-side wait timed out");
+        }
+        return ENGINE_OK;
     });
 }
 

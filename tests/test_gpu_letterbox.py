@@ -185,3 +185,31 @@ def test_prepare_for_engine_jpeg_matches_reference(tmp_path, name):
         ref, m, ratio = _ref_prepare(p, 64, 64, 1 / 255, 114 / 255)
         np.testing.assert_array_equal(y, ref)
         assert [getattr(meta, k) for k in META_FIELDS] == m
+
+
+def test_batch_submit_u8_matches_detect_u8(engine_dir):
+    """Pipelined submits (pdefa_batch_submit_u8 / pdefa_batch_wait): each call's
+    results, collected after later calls were queued (and after a synchronous call on
+    the same runner), equal what detect_u8 returns for the same frames."""
+    g, _ = build_yolov8("n", imgsz=128, seed=0)
+    p = str(engine_dir / "y8n_128_submit.engine")
+    write_engine(p, g)
+    ctx = pb.Context(precision=pb.BF16)
+    m = pb.Model(ctx, p)
+    rng = np.random.default_rng(21)
+    frames = [rng.integers(0, 256, (n, 96, 120, 3), dtype=np.uint8) for n in (7, 3, 9, 1)]
+    kw = dict(target_w=128, target_h=128, conf_thres=0.2, iou_thres=0.5, max_det=40)
+    with pb.BatchInference(ctx, m, batch_size=4, devices=[0]) as bi:
+        want = [bi.detect_u8(f, **kw) for f in frames]
+        pend = [bi.submit_u8(frames[0], **kw), bi.submit_u8(frames[1], **kw)]
+        mid = bi.detect_u8(frames[2], **kw)        # a synchronous call between submits
+        pend += [bi.submit_u8(frames[2], **kw), bi.submit_u8(frames[3], **kw)]
+        got = [q.result() for q in pend]
+        again = bi.submit_u8(frames[0], **kw)
+        bi.wait()
+        got.append(again.result())
+    for (c, d, meta), (cw, dw, mw) in zip(got[:4] + [mid, got[4]], want + [want[2], want[0]]):
+        np.testing.assert_array_equal(c, cw)
+        for b in range(len(c)):
+            np.testing.assert_array_equal(d[b, :c[b]], dw[b, :cw[b]])
+        assert meta == mw
