@@ -16,7 +16,7 @@ Printed JSON line (rank 0):
   read after step k+1 is queued), also as e2e.sync_value through the blocking
   detect_u8 (pdefa_batch_run_u8), and under e2e.f32_input float32 NCHW tensors
   (detect_arrays -> pdefa_batch_run); the runner pipelines micro-batches of
-  --e2e-micro (128) images (copy of one overlapping the inference of the previous);
+  --e2e-micro (256) images (copy of one overlapping the inference of the previous);
 * roofline: the tcgen05 convolution kernels of the step (the dominant kernel
   family): conv FLOPs / their CUDA-event time measured inside the timed region,
   against the measured sustained BF16 peak;
@@ -194,7 +194,7 @@ def main():
     ap.add_argument("--model", default="yolov8n", choices=["yolov8n", "yolov8m", "yolo11n"],
                     help="yolov8n is the headline configuration")
     ap.add_argument("--e2e-steps", type=int, default=0, help="steps for the e2e leg (default: --steps)")
-    ap.add_argument("--e2e-micro", type=int, default=128,
+    ap.add_argument("--e2e-micro", type=int, default=256,
                     help="micro-batch of the e2e leg's pipelined batch runner (images per GPU launch)")
     ap.add_argument("--cpu-images", type=int, default=48, help="images in the bounded CPU baseline sample")
     ap.add_argument("--ref-images", type=int, default=4, help="images per step of the reference arm")
@@ -364,7 +364,10 @@ def main():
         # before step k's detections are collected, so its frames cross PCIe while
         # step k's last micro-batches finish; every step's copies and detections are
         # inside the timed region (the last result() ends it)
-        bi.submit_u8(u8np, **u8kw).result()
+        # warm-up: the runner's two lanes alternate across calls, so each lane meets
+        # every micro-batch size of a step within two calls; their plans are built here
+        for _ in range(3):
+            bi.submit_u8(u8np, **u8kw).result()
         if world > 1:
             dist.barrier()
         t0 = time.perf_counter()
