@@ -272,10 +272,32 @@ constexpr int kRegP = 9;                         // 16-byte pieces per region ro
 constexpr int kRegW = 4 * kRegP;
 constexpr int kRegPlane = kRegH * kRegW;
 
+// q = n / d for n < 2^31 as (n * m) >> p, p = 31 + ceil(log2 d), m = ceil(2^p / d)
+// (Granlund and Montgomery, "Division by invariant integers using multiplication", 1994).
+struct StemDiv {
+    uint64_t m;
+    uint32_t p, d;
+};
+
+StemDiv make_stem_div(uint32_t d) {
+    uint32_t l = 0;
+    while ((1ull << l) < d) ++l;
+    StemDiv f;
+    f.p = 31 + l;
+    f.m = ((1ull << f.p) + d - 1) / d;      // p <= 62: no overflow
+    f.d = d;
+    return f;
+}
+
+__device__ __forceinline__ uint32_t stem_div(uint32_t n, const StemDiv& f) {
+    return (uint32_t)(((uint64_t)n * f.m) >> f.p);   // n < 2^31, m <= 2^32 + 1: fits 64 bits
+}
+
 struct StemTileParams {
     ConvArgs a;
     int Ho, Wo, K;
     int tiles_h, tiles_w;
+    StemDiv div_img, div_tw;   // tile -> (image, tile row, tile column)
     int64_t tiles;
     int RH, RW;           // input region of one tile (rows, columns)
     int ncols;
@@ -294,11 +316,10 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool i
 // pieces of 16 bytes, piece j of a row holding input columns 32*tw - 4 + 4j ... + 3.
 __device__ __forceinline__ void stem_region_load(const StemTileParams& P, int64_t t, float* dst, int H, int W) {
     const ConvArgs& a = P.a;
-    const int64_t per_img = (int64_t)P.tiles_h * P.tiles_w;
-    // tile counts stay below 2^31 (host-checked): 32-bit divisions
-    const uint32_t b = (uint32_t)t / (uint32_t)per_img;
-    const int r = (int)((uint32_t)t - b * (uint32_t)per_img);
-    const int th = r / P.tiles_w, tw = r - th * P.tiles_w;
+    // tile counts stay below 2^31 (host-checked): 32-bit multiply-shift divisions
+    const uint32_t b = stem_div((uint32_t)t, P.div_img);
+    const int r = (int)((uint32_t)t - b * P.div_img.d);
+    const int th = (int)stem_div((uint32_t)r, P.div_tw), tw = r - th * P.tiles_w;
     const int h0 = th * (2 * kTileH) - 1, c0 = tw * (2 * kTileW) - 4;
     const float* const in = static_cast<const float*>(a.in.ptr) + b * a.in.img_stride;
     for (int i = threadIdx.x; i < 3 * kRegH * kRegP; i += blockDim.x) {
@@ -328,6 +349,7 @@ __global__ void __launch_bounds__(128, 8) conv_stem_tile_kernel(const StemTilePa
     uint64_t* const mbar = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(sR1) + rbytes);
     uint32_t* const tmem_slot = reinterpret_cast<uint32_t*>(mbar + 1);
     volatile int* const abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    float* const sBias = reinterpret_cast<float*>(mbar + 2);     // [cout], 16-byte aligned
 
     const int tid = threadIdx.x, warp = tid >> 5;
     if (tid == 0) *abort_flag = *reinterpret_cast<volatile int*>(P.err) != 0;
@@ -344,6 +366,7 @@ __global__ void __launch_bounds__(128, 8) conv_stem_tile_kernel(const StemTilePa
         __nv_bfloat16* row = reinterpret_cast<__nv_bfloat16*>(sB + sw64_off(n, k >> 3));
         row[k & 7] = __float2bfloat16_rn(v);
     }
+    for (int i = tid; i < cout; i += blockDim.x) sBias[i] = a.bias ? a.bias[i] : 0.0f;
     if (tid == 0) {
         asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(mbar)) : "memory");
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -364,7 +387,6 @@ __global__ void __launch_bounds__(128, 8) conv_stem_tile_kernel(const StemTilePa
                           ((uintptr_t)a.out.ptr % 16) == 0 && (a.out.stride[2] % 8) == 0 && (a.out.stride[1] % 8) == 0 &&
                           (a.out.img_stride % 8) == 0;
     const int rbase = 2 * py * kRegW + 2 * px + 3;          // this pixel's first tap (column 2*px - 1 -> piece offset 3)
-    const int64_t per_img = (int64_t)P.tiles_h * P.tiles_w;
     const bool vec_out = a.out.stride[3] == 1 && ((uintptr_t)a.out.ptr % 16) == 0 && (a.out.stride[2] % 8) == 0 &&
                          (a.out.stride[1] % 8) == 0 && (a.out.img_stride % 8) == 0;
     const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16);
@@ -418,7 +440,9 @@ __global__ void __launch_bounds__(128, 8) conv_stem_tile_kernel(const StemTilePa
             asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
                          ::"r"(smem_u32(mbar)) : "memory");
         }
-        bool ok = mbar_wait_bounded(mbar, (uint32_t)(it & 1), 200000000LL);
+        // one warp waits for the MMAs; the others wait at the barrier without issuing
+        bool ok = true;
+        if (warp == 0) ok = mbar_wait_bounded(mbar, (uint32_t)(it & 1), 200000000LL);
         ok = __syncthreads_and(ok);
         if (!ok) {
             if (tid == 0) atomicExch(P.err, 8);
@@ -426,9 +450,9 @@ __global__ void __launch_bounds__(128, 8) conv_stem_tile_kernel(const StemTilePa
             break;
         }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t b = (uint32_t)t / (uint32_t)per_img;
-        const int r = (int)((uint32_t)t - b * (uint32_t)per_img);
-        const int th = r / P.tiles_w, tw = r - th * P.tiles_w;
+        const uint32_t b = stem_div((uint32_t)t, P.div_img);
+        const int r = (int)((uint32_t)t - b * P.div_img.d);
+        const int th = (int)stem_div((uint32_t)r, P.div_tw), tw = r - th * P.tiles_w;
         const int ho = th * kTileH + py, wo = tw * kTileW + px;
         const bool live = ho < P.Ho && wo < P.Wo;
         const int64_t ob = b * a.out.img_stride + (int64_t)ho * a.out.stride[1] + (int64_t)wo * a.out.stride[2];
@@ -442,16 +466,18 @@ __global__ void __launch_bounds__(128, 8) conv_stem_tile_kernel(const StemTilePa
             asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
             if (!live) continue;
             float o[16];
+            float bv[16];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const float4 b4 = reinterpret_cast<const float4*>(sBias + c0)[q];
+                bv[4 * q] = b4.x; bv[4 * q + 1] = b4.y; bv[4 * q + 2] = b4.z; bv[4 * q + 3] = b4.w;
+            }
             if (fast_epi) {
 #pragma unroll
-                for (int i = 0; i < 16; ++i)
-                    o[i] = stem_act(__uint_as_float(rr[i]) + (a.bias ? __ldg(a.bias + i) : 0.0f), ACT_SILU, 0.f);
+                for (int i = 0; i < 16; ++i) o[i] = stem_act(__uint_as_float(rr[i]) + bv[i], ACT_SILU, 0.f);
             } else {
 #pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    float x = __uint_as_float(rr[i]) + (a.bias ? __ldg(a.bias + c0 + i) : 0.0f);
-                    o[i] = stem_act(x, a.act, a.slope);
-                }
+                for (int i = 0; i < 16; ++i) o[i] = stem_act(__uint_as_float(rr[i]) + bv[i], a.act, a.slope);
             }
             if (vec_out && a.out.dt == BF16) {
                 uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(const_cast<void*>(a.out.ptr)) + ob + c0);
@@ -513,12 +539,16 @@ void launch_conv_stem_tc(const ConvArgs& a, int* err, cudaStream_t s) {
         T.tiles_h = (P.Ho + kTileH - 1) / kTileH;
         T.tiles_w = (P.Wo + kTileW - 1) / kTileW;
         T.tiles = (int64_t)T.tiles_h * T.tiles_w * a.batch;
+        T.div_img = make_stem_div((uint32_t)(T.tiles_h * T.tiles_w));
+        T.div_tw = make_stem_div((uint32_t)T.tiles_w);
         T.RH = kRegH;
         T.RW = kRegW;
         T.ncols = P.ncols;
         T.err = err;
         const size_t rbytes = (size_t)3 * kRegPlane * 4;
-        const size_t smem = 512 + kRows * kRowBytes + ((a.cout * kRowBytes + 511) & ~511) + 2 * rbytes + 64;
+        // tail: barrier, TMEM slot, flag (16 B), then the biases (cout floats)
+        const size_t smem = 512 + kRows * kRowBytes + ((a.cout * kRowBytes + 511) & ~511) + 2 * rbytes + 16 +
+                            (((size_t)a.cout * 4 + 15) & ~size_t(15)) + 48;
         if (smem <= 48 * 1024 && T.tiles < (int64_t(1) << 31)) {
             static int sms_t[64] = {};
             int sms = 148;
