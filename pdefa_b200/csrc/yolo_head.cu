@@ -109,10 +109,18 @@ __global__ void __launch_bounds__(kHeadAnchors) yolo_head_tile_kernel(YoloHeadAr
         src[j] = nullptr;
     }
     __syncthreads();
-    for (int idx = j; idx < kHeadAnchors * chunks; idx += kHeadAnchors) {
-        const int r = idx / chunks, q = idx - r * chunks;
-        const char* p = src[r];
-        if (p) rows[r * row_chunks + q] = __ldg(reinterpret_cast<const uint4*>(p) + q);
+    // chunk idx = j + k * kHeadAnchors of the tile is (row r, piece q); (r, q) advance
+    // by (kHeadAnchors / chunks, kHeadAnchors % chunks) per step, no division per load
+    {
+        int r = j / chunks, q = j - r * chunks;
+        const int dr = kHeadAnchors / chunks, dq = kHeadAnchors - dr * chunks;
+        for (int idx = j; idx < kHeadAnchors * chunks; idx += kHeadAnchors) {
+            const char* p = src[r];
+            if (p) rows[r * row_chunks + q] = __ldg(reinterpret_cast<const uint4*>(p) + q);
+            r += dr;
+            q += dq;
+            if (q >= chunks) { q -= chunks; ++r; }
+        }
     }
     __syncthreads();
     if (i >= A) return;
