@@ -173,3 +173,20 @@ def test_malformed_and_unknown_files_are_reported(tmp_path):
     p.write_bytes(b"\xff\xd8")
     assert N.lib().pdefa_image_load(str(p).encode()) is None
     assert b"too small" in N.lib().pdefa_last_error()
+
+
+def test_batch_submit_and_wait_argument_checks():
+    """pdefa_batch_submit_u8 / pdefa_batch_wait report missing pointers with
+    ENGINE_ERR_NULL_PTR (1) before touching a GPU."""
+    L = N.lib()
+    px = (C.c_uint8 * 12)()
+    cfg = N.PreConfig(64, 64, 1.0 / 255.0, 0.0)
+    counts = (N.i32 * 1)()
+    dets = (N.Detection * 4)()
+    ticket = C.c_int64(0)
+    assert L.pdefa_batch_wait(None, 0) == 1
+    assert L.pdefa_batch_submit_u8(None, px, 1, 2, 2, 3, C.byref(cfg), 0.25, 0.45, 4, counts, dets, None,
+                                   C.byref(ticket)) == 1
+    fake = C.create_string_buffer(64)          # never dereferenced: the ticket check comes first
+    assert L.pdefa_batch_submit_u8(C.cast(fake, C.c_void_p), px, 1, 2, 2, 3, C.byref(cfg), 0.25, 0.45, 4,
+                                   counts, dets, None, None) == 1
