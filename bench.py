@@ -173,6 +173,68 @@ def run_reference_arm(args, rank):
     }))
 
 
+def run_layers(args):
+    """--layer CIN,COUT,K,S,HW / --sweep-layers: one conv layer (Conv-BN-SiLU graph of
+    yolo.build_single_conv) at a time through the engine, per-launch CUDA-event time
+    of the conv launch, its TFLOP/s, algorithmic HBM GB/s and the fraction of its
+    roofline max(FLOPs / sustained tensor peak, bytes / HBM bandwidth). One JSON line
+    per layer. The graph input is fp32 NCHW, so for Cin > 8 the plan's first launch
+    stages it into the NHWC operand layout; only the conv launch is reported."""
+    import torch
+
+    import pdefa_b200 as pb
+    from pdefa_b200.engine_file import write_engine
+    from pdefa_b200.yolo import build_single_conv, build_yolov8
+
+    hbm, _, peak_sus, src = load_peaks()
+    prec = {"bf16": pb.BF16, "tf32": pb.TF32, "fp32": pb.FP32}[args.precision]
+    if args.precision == "tf32":
+        peak_sus /= 2
+    if args.sweep_layers:
+        _, info = build_yolov8("n", imgsz=640, seed=0)
+        shapes = []
+        for _, cin, cout, k, s, h, w in info["convs"]:
+            if (cin, cout, k, s, h) not in shapes:
+                shapes.append((cin, cout, k, s, h))
+    else:
+        shapes = [tuple(int(v) for v in args.layer.split(","))]
+    torch.cuda.set_device(0)
+    ts = torch.cuda.Stream()
+    torch.cuda.set_stream(ts)
+    for cin, cout, k, s, hw in shapes:
+        g, _ = build_single_conv(cin=cin, cout=cout, k=k, s=s, hw=hw, act=True)
+        path = os.path.join(tempfile.mkdtemp(), "layer.engine")
+        write_engine(path, g)
+        ctx = pb.Context(precision=prec)
+        model = pb.Model(ctx, path)
+        sess = pb.Session(ctx, model)
+        B = args.batch
+        x = torch.rand((B, cin, hw, hw), device="cuda", generator=torch.Generator(device="cuda").manual_seed(7))
+        for _ in range(args.warmup):
+            sess.run_device(x.data_ptr(), B, None, ts.cuda_stream)
+        torch.cuda.synchronize()
+        summary = model.plan_summary(prec, B)
+        sess.set_step_timing(B, True)
+        for _ in range(args.steps):
+            sess.run_device(x.data_ptr(), B, None, ts.cuda_stream)
+        torch.cuda.synchronize()
+        times = sess.step_times(B)
+        sess.set_step_timing(B, False)
+        i = next(j for j, (kind, _) in enumerate(summary) if kind.startswith("conv"))
+        ms = times[i] / args.steps
+        ho = (hw + 2 * (k // 2) - k) // s + 1
+        in_esz = 4 if summary[i][0] in ("conv_direct", "conv_stem_tc") or prec != pb.BF16 else 2
+        out_esz = 2 if prec == pb.BF16 else 4
+        flops = 2.0 * cin * cout * k * k * ho * ho * B
+        nbytes = float((in_esz * cin * hw * hw + out_esz * cout * ho * ho) * B)
+        t_flop, t_byte = flops / peak_sus / 1e9, nbytes / hbm / 1e6
+        print(json.dumps({"layer": f"conv{k}x{k}s{s} {cin}->{cout} @{hw}x{hw}", "batch": B, "kind": summary[i][0],
+                          "ms": round(ms, 4), "tflops": round(flops / ms / 1e9, 1),
+                          "gbs": round(nbytes / ms / 1e6, 1), "bound": "tensor" if t_flop > t_byte else "hbm",
+                          "bound_ms": round(max(t_flop, t_byte), 4), "roofline_frac": round(max(t_flop, t_byte) / ms, 3),
+                          "peaks": f"{src}: {peak_sus:.1f} TFLOP/s sustained, {hbm:.0f} GB/s"}), flush=True)
+
+
 def config(args, world):
     name = {"yolov8n": "configs[3]: YOLOv8n", "yolov8m": "configs[4]: YOLOv8m", "yolo11n": "YOLO11n"}[args.model]
     return {"workload": f"{name}-{args.imgsz} random-init, {args.precision.upper()} tcgen05 convs + GPU decode/NMS "
@@ -200,7 +262,12 @@ def main():
     ap.add_argument("--ref-images", type=int, default=4, help="images per step of the reference arm")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", action="store_true", help="print per-launch milliseconds to stderr")
+    ap.add_argument("--layer", default="", help="CIN,COUT,K,S,HW: time one conv layer (Conv-BN-SiLU) instead")
+    ap.add_argument("--sweep-layers", action="store_true", help="time every distinct YOLOv8n-640 conv shape")
     args = ap.parse_args()
+    if args.layer or args.sweep_layers:
+        run_layers(args)
+        return
     args.warmup = max(args.warmup, 3)
 
     rank = int(os.environ.get("RANK", "0"))

@@ -115,7 +115,9 @@ ENGINE_API EngineStatus pdefa_decode_yolo_device(const float* d_preds, int64_t b
  * fail with ENGINE_ERR_INVALID_ARG. The first call on a device looks up the array's
  * device address (make it before any stream capture). Calls share the array: calls
  * that overlap on the GPU (other streams, other threads) race and must be ordered
- * by the caller. Allocates nothing, no cudaMalloc or cudaFree. */
+ * by the caller. The array used is the current device's: a non-NULL `stream` must
+ * belong to the current device (ENGINE_ERR_INVALID_ARG otherwise). Allocates
+ * nothing, no cudaMalloc or cudaFree. */
 ENGINE_API EngineStatus pdefa_decode_yolo_noalloc(const float* d_preds, int64_t batch, int64_t channels,
                                                   int64_t anchors, const PdefaPreprocessMeta* d_metas,
                                                   double conf_thres, double iou_thres, int32_t max_det,
@@ -180,7 +182,10 @@ ENGINE_API EngineStatus pdefa_batch_submit_u8(PdefaBatchRunner* runner, const ui
                                               PdefaDetection* out_dets, PdefaPreprocessMeta* out_meta,
                                               int64_t* out_ticket);
 /* Completes every queued call up to and including `ticket` (all of them when
- * ticket <= 0): their results land in the arrays they were given. */
+ * ticket <= 0): their results land in the arrays they were given. If a later call
+ * failed on a device before an earlier call's pending micro-batches finished there,
+ * those results are lost and the wait covering that earlier call returns
+ * ENGINE_ERR_RUNTIME (once) instead of leaving its arrays silently unwritten. */
 ENGINE_API EngineStatus pdefa_batch_wait(PdefaBatchRunner* runner, int64_t ticket);
 
 #ifdef __cplusplus

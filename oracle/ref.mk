@@ -16,9 +16,11 @@
 #  * Flags follow PDEFA1.0/cmake/CompilerFlags.cmake:34 and 43-49 (-O3,
 #    -ffp-contract=fast, -fno-math-errno, -fno-trapping-math) with -mavx2 -mfma.
 #
-# Usage: make -f oracle/ref.mk REF=/path/to/reference [-j8]
+# Usage: make -f oracle/ref.mk REF=/path/to/reference [-j8]   (REF is required)
 
-REF      ?= /root/reference
+ifeq ($(strip $(REF)),)
+$(error REF=<path of the pdefa reference checkout> is required)
+endif
 OUT      := $(dir $(lastword $(MAKEFILE_LIST)))_ref
 OBJ      := $(OUT)/obj
 LIB      := $(OUT)/libpdefa_ref.so

@@ -3,6 +3,8 @@
 // multi-GPU batch runner (one replica per device, contiguous shards, no collective).
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
+#include <set>
 #include <thread>
 
 #include "../../include/pdefa_b200_ext.h"
@@ -100,6 +102,10 @@ struct PdefaBatchRunner {
     int64_t max_per_device = 1;
     std::vector<Replica> reps;
     int64_t tickets = 0;                 // calls queued so far (pdefa_batch_submit_u8 returns the number)
+    // Earlier calls whose pending micro-batches were lost when a later call failed on a
+    // device; pdefa_batch_wait reports them instead of returning unwritten arrays.
+    std::mutex failed_mu;
+    std::set<int64_t> failed_tickets;
 };
 
 namespace {
@@ -511,10 +517,23 @@ EngineStatus run_batch(PdefaBatchRunner* r, const BatchInput& in, int64_t n_imag
                     if (drain && read_device_error(rp.device)) fail(ENGINE_ERR_RUNTIME, "device-side wait timed out");
                 } catch (const std::exception& e) {
                     errs[d] = e.what();
-                    // leave no lane pending: its buffers may be reused by the next call
+                    // Leave no lane pending: its buffers may be reused by the next call.
+                    // A lane still holding an earlier call's micro-batch hands its results
+                    // over if they finished; otherwise that call is marked failed, so its
+                    // pdefa_batch_wait reports the loss.
                     for (auto& l : rp.lanes) {
-                        if (l.busy) cudaEventSynchronize(l.done);
+                        if (!l.busy) continue;
                         l.busy = false;
+                        const bool done = cudaEventSynchronize(l.done) == cudaSuccess;
+                        if (l.ticket < ticket && done) {
+                            std::memcpy(l.dst_counts + l.c0, l.h_counts, (size_t)l.nb * 4);
+                            if (l.dst_max_det > 0)
+                                std::memcpy(l.dst_dets + l.c0 * l.dst_max_det, l.h_dets,
+                                            (size_t)l.nb * l.dst_max_det * sizeof(PdefaDetection));
+                        } else if (l.ticket < ticket) {
+                            std::lock_guard<std::mutex> lk(r->failed_mu);
+                            r->failed_tickets.insert(l.ticket);
+                        }
                     }
                     cudaStreamSynchronize(rp.copy);
                     cudaStreamSynchronize(rp.stream);
@@ -596,6 +615,16 @@ ENGINE_API EngineStatus pdefa_batch_wait(PdefaBatchRunner* r, int64_t ticket) {
     return guarded([&]() -> EngineStatus {
         clear_error();
         const int64_t upto = ticket > 0 ? ticket : r->tickets;
+        {
+            std::lock_guard<std::mutex> lk(r->failed_mu);
+            auto it = r->failed_tickets.begin();
+            if (it != r->failed_tickets.end() && *it <= upto) {
+                const int64_t t = *it;
+                r->failed_tickets.erase(r->failed_tickets.begin(), r->failed_tickets.upper_bound(upto));
+                set_error("call " + std::to_string(t) + " lost its pending results when a later call failed");
+                return ENGINE_ERR_RUNTIME;
+            }
+        }
         for (auto& rp : r->reps) {
             PB_CUDA(cudaSetDevice(rp.device));
             for (int k = 0; k < 2; ++k) {

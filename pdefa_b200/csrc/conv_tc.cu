@@ -2,7 +2,8 @@
 //
 // GEMM view: D[M = batch*Ho*Wo pixels, N = Cout] = A[M, K] * W[N, K]^T with
 // K = kh*kw*Cin ordered (tap, channel), cut into 128 x BN output tiles. The kernel
-// is persistent (one CTA per SM, tiles taken round-robin) and warp-specialized:
+// is persistent (1-4 CTAs per SM as TMEM, registers and shared memory allow; tiles
+// taken round-robin) and warp-specialized:
 //   * warp 0 / lane 0 issues TMA loads into a ring of `stages` shared-memory slots
 //     that runs on across tile boundaries:
 //       A: im2col-mode tensor map (3x3 / strided / padded convs: the TMA unit walks
@@ -12,9 +13,11 @@
 //     Each load covers `CH` channels (CH*elem = 32/64/128 bytes, the swizzle width).
 //     No load uses cluster multicast.
 //   * warp 1 / lane 0 issues tcgen05.mma (kind::f16 for BF16, kind::tf32 for TF32)
-//     into one of two TMEM accumulators (128 lanes x BN fp32 columns each), releases
-//     ring slots with tcgen05.commit and hands a finished accumulator to the epilogue.
-//   * warps 2-5 run the epilogue of tile t while tile t+1 accumulates: tcgen05.ld of
+//     into one of 1, 2 or 4 TMEM accumulators (128 lanes x BN fp32 columns each),
+//     releases ring slots with tcgen05.commit and hands a finished accumulator to the
+//     epilogue.
+//   * 4 or 8 epilogue warps run the epilogue of tile t while tile t+1 accumulates
+//     (with a single accumulator, after it): tcgen05.ld of
 //     their 32 TMEM lanes, bias, activation, optional residual add, and a strided
 //     store (bf16 or fp32) that can land inside a channel slice of a concat buffer.
 // Every mbarrier wait is bounded; on timeout the kernel records an error in the
@@ -140,8 +143,8 @@ __device__ __forceinline__ void tma_load_im2col_4d(uint32_t dst, const CUtensorM
 // One k-block: ksteps (1, 2 or 4) MMAs over consecutive 32-byte K slices of the A and
 // B rows, then a commit of all of them to `bar`, in one branch-free instruction
 // sequence (the extra MMAs are predicated off). A branch between a tcgen05.mma and the
-// next one costs the issuing thread a few hundred cycles, so the k-slices are never
-// issued from a loop. acc = 0 starts a fresh accumulator with the first slice;
+// next one costs the issuing thread tens of cycles, so the k-slices are never issued
+// from a loop. acc = 0 starts a fresh accumulator with the first slice;
 // bar == nullptr issues no commit.
 template <int KIND>
 __device__ __forceinline__ void umma_kblock(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc,
@@ -864,8 +867,9 @@ void launch_conv_tc(const ConvArgs& a, int op_dt, int* err, cudaStream_t s) {
     // in shared memory, loaded once per CTA. The choices follow per-layer sweeps of
     // every combination on B200 (YOLOv8 layer shapes):
     //   * CTAs per SM matter most: as many as TMEM allows (two accumulators of
-    //     bufcols columns each), four at most with 4 epilogue warps, two with 8,
-    //     even when that leaves a ring of two slots;
+    //     bufcols columns each, or one for multi-tap convs with 64 < Cout < 128),
+    //     four at most with 4 epilogue warps, two with 8, even when that leaves a
+    //     ring of two slots;
     //   * windows win where im2col moves narrow rows (channel chunks under 128
     //     bytes: Cin = 16, 32, 80, ...), im2col elsewhere;
     //   * resident weights whenever they fit without costing a CTA, and always for
@@ -877,10 +881,11 @@ void launch_conv_tc(const ConvArgs& a, int op_dt, int* err, cudaStream_t s) {
     const int swb = ch * esz;
     const int chunks = (a.cin + ch - 1) / ch;   // a last, partial chunk reads zeros past Cin
     const int nk = p.taps * chunks;
-    const int tmem_ctas = 512 / p.tmem_cols;                     // two accumulators per CTA
+    const int tmem_ctas = 512 / p.tmem_cols;                     // p.nbuf accumulators per CTA
     // 8 epilogue warps for 1x1 convs from 128 output channels up and for multi-tap
-    // convs above 64 (TMEM then allows two CTAs at most); 1x1 convs always stage
-    // their output for TMA stores.
+    // convs whose accumulators leave TMEM room for two CTAs at most (Cout >= 128 with
+    // two accumulators); the single-accumulator convs (64 < Cout < 128) fit four CTAs
+    // and take 4 epilogue warps. 1x1 convs stage their output for TMA stores.
     const int epi = (one ? bn >= 128 : tmem_ctas <= 2) ? 8 : 4;
     const int max_ctas = std::min(epi == 8 ? 2 : 4, tmem_ctas);  // register file, TMEM
     const int oes = a.out.dt == BF16 ? 2 : 4;

@@ -17,6 +17,7 @@
 //     0 when the overlap is empty) and stops after max_det kept boxes.
 // Limit: at most 16384 anchors per image (keys live in shared memory).
 #include <cfloat>
+#include <atomic>
 #include <climits>
 
 #include <mutex>
@@ -553,20 +554,29 @@ __global__ void __launch_bounds__(kThreads, 1) decode_nms_kernel(DecodeArgs p) {
 
 }  // namespace
 
-size_t decode_work_bytes(int64_t batch, int64_t anchors) { return (size_t)batch * (size_t)anchors * sizeof(Det); }
+size_t decode_work_bytes(int64_t batch, int64_t anchors) {
+    // SIZE_MAX when batch * anchors * sizeof(Det) does not fit in size_t, so a size
+    // check against it can never pass by wrapping around
+    if (batch <= 0 || anchors <= 0) return 0;
+    if ((uint64_t)batch > SIZE_MAX / sizeof(Det) / (uint64_t)anchors) return SIZE_MAX;
+    return (size_t)batch * (size_t)anchors * sizeof(Det);
+}
 
 void launch_decode_nms(const DecodeArgs& a, cudaStream_t s) {
     if (a.anchors > kMaxKeys) fail(ENGINE_ERR_NOT_IMPL, "decode: more than 16384 anchors per image");
     if (a.channels - 4 > kMaxClasses || a.channels < 5) fail(ENGINE_ERR_INVALID_SHAPE, "decode: bad channel count");
     if (a.max_det < 0) fail(ENGINE_ERR_INVALID_ARG, "decode: max_det must be >= 0");
+    if (a.batch < 0 || a.batch > INT_MAX) fail(ENGINE_ERR_INVALID_ARG, "decode: batch must be in [0, 2^31)");
     if (a.batch == 0) return;
     const size_t smem = kNmsSmem;
     int dev = 0;
     PB_CUDA(cudaGetDevice(&dev));
-    static bool set[64] = {};
-    if (!set[dev]) {
+    // the opt-in shared-memory size is a per-device function attribute, set once
+    // per device (runner threads of several devices may get here at the same time)
+    static std::atomic<bool> set[64] = {};
+    if (dev < 0 || dev >= 64 || !set[dev].load(std::memory_order_acquire)) {
         PB_CUDA(cudaFuncSetAttribute(decode_nms_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        set[dev] = true;
+        if (dev >= 0 && dev < 64) set[dev].store(true, std::memory_order_release);
     }
     int64_t cblocks = (a.batch * a.anchors + 255) / 256;
     if (cblocks > 148 * 16) cblocks = 148 * 16;
@@ -629,16 +639,28 @@ extern "C" ENGINE_API EngineStatus pdefa_decode_yolo_noalloc(const float* d_pred
         clear_error();
         if (batch < 0 || channels < 5 || anchors < 0) { set_error("decode_noalloc: bad shape"); return ENGINE_ERR_INVALID_SHAPE; }
         if (max_det < 0) { set_error("decode_noalloc: max_det must be >= 0"); return ENGINE_ERR_INVALID_ARG; }
-        const size_t need = decode_work_bytes(batch, anchors);
-        if (need > kNoAllocScratchBytes) {
-            set_error("decode_noalloc: batch * anchors = " + std::to_string(batch * anchors) +
-                      " candidate slots exceed the built-in scratch of " +
-                      std::to_string(kNoAllocScratchBytes / sizeof(Det)) +
+        // batch * anchors candidate records must fit the built-in scratch; checked by
+        // division so that huge arguments cannot wrap the product around
+        constexpr uint64_t kSlots = kNoAllocScratchBytes / sizeof(Det);
+        if (anchors > 0 && (uint64_t)batch > kSlots / (uint64_t)anchors) {
+            set_error("decode_noalloc: batch * anchors = " + std::to_string(batch) + " * " + std::to_string(anchors) +
+                      " candidate slots exceed the built-in scratch of " + std::to_string(kSlots) +
                       " (8 MiB); decode fewer images per call or use pdefa_decode_yolo_device");
             return ENGINE_ERR_INVALID_ARG;
         }
         int dev = 0;
         PB_CUDA(cudaGetDevice(&dev));
+        // The scratch address is the current device's; a stream of another device
+        // would run the kernels there against this device's array.
+        if (stream) {
+            int sdev = -1;
+            PB_CUDA(cudaStreamGetDevice(static_cast<cudaStream_t>(stream), &sdev));
+            if (sdev != dev) {
+                set_error("decode_noalloc: stream belongs to device " + std::to_string(sdev) +
+                          " but the current device is " + std::to_string(dev));
+                return ENGINE_ERR_INVALID_ARG;
+            }
+        }
         DecodeArgs a;
         a.preds = d_preds;
         a.batch = batch; a.channels = channels; a.anchors = anchors;

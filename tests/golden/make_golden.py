@@ -27,7 +27,7 @@ import numpy as np
 ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 sys.path.insert(0, ROOT)
 OUT = os.path.dirname(os.path.abspath(__file__))
-REF = os.environ.get("PDEFA_REFERENCE", "/root/reference")
+REF = os.environ.get("PDEFA_REFERENCE") or sys.exit("set PDEFA_REFERENCE to the pdefa reference checkout")
 
 from oracle import ref_engine as R  # noqa: E402
 from pdefa_b200.engine_file import EngineGraph, TensorInfo, write_engine  # noqa: E402

@@ -190,3 +190,23 @@ def test_batch_submit_and_wait_argument_checks():
     fake = C.create_string_buffer(64)          # never dereferenced: the ticket check comes first
     assert L.pdefa_batch_submit_u8(C.cast(fake, C.c_void_p), px, 1, 2, 2, 3, C.byref(cfg), 0.25, 0.45, 4,
                                    counts, dets, None, None) == 1
+
+
+def test_decode_scratch_size_checks_do_not_wrap():
+    """Sizes whose candidate-slot product overflows 64 bits are refused before any
+    device work: the allocation-free decode answers ENGINE_ERR_INVALID_ARG (7), and
+    the work-size query saturates instead of wrapping to a small number."""
+    L = N.lib()
+    f = L.pdefa_decode_yolo_noalloc
+    f.argtypes = [C.c_void_p, C.c_int64, C.c_int64, C.c_int64, C.c_void_p, C.c_double, C.c_double, C.c_int32,
+                  C.c_void_p, C.c_void_p, C.c_void_p]
+    f.restype = C.c_int
+    fake = C.create_string_buffer(64)          # never dereferenced: the size check comes first
+    ptr = C.cast(fake, C.c_void_p)
+    for batch, anchors in ((1 << 46, 16384), (1 << 40, 1 << 23), (21, 8400)):
+        assert f(ptr, batch, 84, anchors, None, 0.25, 0.45, 300, ptr, ptr, None) == 7
+        assert b"scratch" in L.pdefa_last_error()
+    L.pdefa_decode_work_bytes.restype = C.c_size_t
+    L.pdefa_decode_work_bytes.argtypes = [C.c_int64, C.c_int64]
+    assert L.pdefa_decode_work_bytes(1 << 46, 16384) == 2 ** 64 - 1
+    assert L.pdefa_decode_work_bytes(2, 8400) == 2 * 8400 * 48

@@ -24,7 +24,8 @@ from pdefa_b200 import _native as N
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 REF_LIB = os.path.join(ROOT, "oracle", "_ref", "libpdefa_ref.so")
 GOLDEN = os.path.join(ROOT, "tests", "golden", "jpeg_ref.npz")
-REF_FIXTURE = "/root/reference/pdefa/tests/data/cat.jpg"
+# the reference checkout (PDEFA_REFERENCE) holds its own JPEG fixture
+REF_FIXTURE = os.path.join(os.environ.get("PDEFA_REFERENCE", ""), "pdefa", "tests", "data", "cat.jpg")
 
 PIL = pytest.importorskip("PIL.Image")
 cv2 = pytest.importorskip("cv2")
