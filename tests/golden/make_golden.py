@@ -27,7 +27,7 @@ import numpy as np
 ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 sys.path.insert(0, ROOT)
 OUT = os.path.dirname(os.path.abspath(__file__))
-REF = os.environ.get("PDEFA_REFERENCE") or sys.exit("set PDEFA_REFERENCE to the pdefa reference checkout")
+REF = os.environ.get("PDEFA_REFERENCE", "")   # the pdefa reference checkout (needed to make the decode goldens)
 
 from oracle import ref_engine as R  # noqa: E402
 from pdefa_b200.engine_file import EngineGraph, TensorInfo, write_engine  # noqa: E402
@@ -57,6 +57,8 @@ def reference_python_decode():
     """Import the reference decode_yolo from a temporary copy of its package."""
     tmp = tempfile.mkdtemp(prefix="pdefa_refpy_")
     pkg = os.path.join(tmp, "pdefa")
+    if not REF:
+        sys.exit("set PDEFA_REFERENCE to the pdefa reference checkout")
     src = os.path.join(REF, "pdefa", "python", "src", "pdefa")
     os.makedirs(os.path.join(pkg, "lib"))
     for f in ("__init__.py", "batch.py"):
