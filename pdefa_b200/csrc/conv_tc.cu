@@ -237,12 +237,23 @@ __device__ __forceinline__ void epilogue_math(const TcParams& p, float (&v)[16],
     if (p.bias) {
         const float4* b4 = reinterpret_cast<const float4*>(p.bias + ncol);
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
+        for (int q = 0; q < 4; ++q) {      // packed fp32x2 adds: one instruction per pair
             const float4 b = __ldg(b4 + q);
-            v[4 * q] += b.x; v[4 * q + 1] += b.y; v[4 * q + 2] += b.z; v[4 * q + 3] += b.w;
+            const float2 lo = __fadd2_rn(make_float2(v[4 * q], v[4 * q + 1]), make_float2(b.x, b.y));
+            const float2 hi = __fadd2_rn(make_float2(v[4 * q + 2], v[4 * q + 3]), make_float2(b.z, b.w));
+            v[4 * q] = lo.x; v[4 * q + 1] = lo.y; v[4 * q + 2] = hi.x; v[4 * q + 3] = hi.y;
         }
     }
-    if (ACT == ACT_SILU_WINO) {
+    if (ACT == ACT_SILU) {
+        // x/2 + x/2 tanh(x/2) with packed multiplies and fused multiply-adds
+#pragma unroll
+        for (int i = 0; i < 16; i += 2) {
+            const float2 h = __fmul2_rn(make_float2(v[i], v[i + 1]), make_float2(0.5f, 0.5f));
+            const float2 y = __ffma2_rn(h, make_float2(tanh_approx(h.x), tanh_approx(h.y)), h);
+            v[i] = y.x;
+            v[i + 1] = y.y;
+        }
+    } else if (ACT == ACT_SILU_WINO) {
 #pragma unroll
         for (int i = 0; i < 16; i += 2) {
             const float2 y = silu_wino_fast2(make_float2(v[i], v[i + 1]));

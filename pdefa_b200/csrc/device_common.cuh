@@ -83,15 +83,35 @@ __device__ __forceinline__ float silu_wino_fast(float x) {
     return y;
 }
 
-// silu_wino_fast on two values with the packed fp32x2 pipe of sm_100 (each lane of a
-// packed multiply/add/fma rounds like the scalar instruction, so the results equal
-// silu_wino_fast's bit for bit; rint, clamp, the exponent bits and the divide stay
-// per lane).
+// The same flavour on two values with the packed fp32x2 pipe of sm_100, in about 20
+// instructions per pair (the epilogue of the 3x3 convs spends most of its issue slots
+// here):
+//   * t = -x*log2(e) is clamped to [-127, 127] first, so no range selects are needed:
+//     t = -127 gives n = -127, whose exponent field (n + 127) << 23 is 0, so 2^n reads
+//     as 0 and y = x (the flavour returns x above 88.37626); t = 127 gives
+//     den = 1 + 2^127 and y = x * rcp(den), which the flush-to-zero reciprocal makes
+//     0 (the flavour returns 0 below -88.37626);
+//   * n = rint(t) by the 1.5 * 2^23 magic-number addition (round to nearest even,
+//     exact for |t| < 2^22); the sum's bit pattern is 0x4B400000 + n, and
+//     (0x4B400000 << 23) vanishes mod 2^32, so the exponent field of 2^n is
+//     (bits + 127) << 23 with no float-to-int conversion;
+//   * the divide is an approximate reciprocal (rcp.approx.ftz) and a packed multiply.
+// Inside |x| <= 88 the steps match silu_wino_fast (same polynomial, same fused
+// multiply-adds, ~2 ulp divide).
+__device__ __forceinline__ float rcp_approx_ftz(float x) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
 __device__ __forceinline__ float2 silu_wino_fast2(float2 x) {
-    const float2 fx = __fmul2_rn(x, make_float2(-1.44269504088896341f, -1.44269504088896341f));
-    const float n0 = fminf(fmaxf(rintf(fx.x), -126.0f), 127.0f);
-    const float n1 = fminf(fmaxf(rintf(fx.y), -126.0f), 127.0f);
-    const float2 f = __fadd2_rn(fx, make_float2(-n0, -n1));
+    const float kMagic = 12582912.0f;   // 1.5 * 2^23
+    float2 t = __fmul2_rn(x, make_float2(-1.44269504088896341f, -1.44269504088896341f));
+    t.x = fminf(fmaxf(t.x, -127.0f), 127.0f);
+    t.y = fminf(fmaxf(t.y, -127.0f), 127.0f);
+    const float2 tm = __fadd2_rn(t, make_float2(kMagic, kMagic));
+    // -n = M - tm (exact: both are within 2^7 of M), then f = t - n
+    const float2 neg_n = __ffma2_rn(tm, make_float2(-1.0f, -1.0f), make_float2(kMagic, kMagic));
+    const float2 f = __fadd2_rn(t, neg_n);
     float2 p = make_float2(1.9875691500e-4f, 1.9875691500e-4f);
     p = __ffma2_rn(p, f, make_float2(1.3981999507e-3f, 1.3981999507e-3f));
     p = __ffma2_rn(p, f, make_float2(8.3334519073e-3f, 8.3334519073e-3f));
@@ -99,14 +119,10 @@ __device__ __forceinline__ float2 silu_wino_fast2(float2 x) {
     p = __ffma2_rn(p, f, make_float2(1.6666665459e-1f, 1.6666665459e-1f));
     p = __ffma2_rn(p, f, make_float2(5.0000001201e-1f, 5.0000001201e-1f));
     p = __ffma2_rn(p, f, make_float2(1.0f, 1.0f));
-    const float2 scale = make_float2(__int_as_float(((int)n0 + 127) << 23), __int_as_float(((int)n1 + 127) << 23));
+    const float2 scale = make_float2(__uint_as_float((__float_as_uint(tm.x) + 127u) << 23),
+                                     __uint_as_float((__float_as_uint(tm.y) + 127u) << 23));
     const float2 den = __ffma2_rn(p, scale, make_float2(1.0f, 1.0f));
-    float y0 = __fdividef(x.x, den.x), y1 = __fdividef(x.y, den.y);
-    y0 = x.x > 88.37626f ? x.x : y0;
-    y0 = x.x < -88.37626f ? 0.0f : y0;
-    y1 = x.y > 88.37626f ? x.y : y1;
-    y1 = x.y < -88.37626f ? 0.0f : y1;
-    return make_float2(y0, y1);
+    return __fmul2_rn(x, make_float2(rcp_approx_ftz(den.x), rcp_approx_ftz(den.y)));
 }
 
 __device__ __forceinline__ float apply_act(float v, int act, float p0, float p1) {
