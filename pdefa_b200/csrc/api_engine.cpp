@@ -9,6 +9,9 @@
 // and every compute call runs on a CUDA device; without one it fails with
 // ENGINE_ERR_RUNTIME instead of computing on the CPU.
 #include <algorithm>
+#if defined(__x86_64__) || defined(__i386__)
+#include <cpuid.h>
+#endif
 #include <cmath>
 #include <cstdlib>
 #include <random>
@@ -305,14 +308,35 @@ ENGINE_API const char* engine_status_string(EngineStatus s) {
     }
 }
 ENGINE_API size_t engine_dtype_size(EngineDType dt) { return pb::engine_dtype_bytes(dt); }
-ENGINE_API const char* engine_simd_level(void) { return "sm_100a"; }
+// Host introspection keeps the reference's meaning (PDEFA1.0/src/api/engine_api.cpp:
+// simd level, CPU brand and the AVX flags describe the host CPU), so callers that
+// branch on them see the same answers; the compute device is reported by
+// engine_device_count / engine_context_get_device (pdefa_b200_ext.h).
+ENGINE_API const char* engine_simd_level(void) {
+#if defined(__x86_64__) || defined(__i386__)
+    __builtin_cpu_init();
+    if (__builtin_cpu_supports("avx512f")) return "AVX-512";
+    if (__builtin_cpu_supports("avx2") && __builtin_cpu_supports("fma")) return "AVX2";
+    if (__builtin_cpu_supports("sse2")) return "SSE";
+#endif
+    return "SCALAR";
+}
 ENGINE_API const char* engine_cpu_brand(void) {
     static std::string name;
     static std::once_flag once;
     std::call_once(once, [] {
-        cudaDeviceProp prop;
-        if (pb::device_count() > 0 && cudaGetDeviceProperties(&prop, 0) == cudaSuccess) name = prop.name;
-        else { cudaGetLastError(); name = "no CUDA device"; }
+#if defined(__x86_64__) || defined(__i386__)
+        unsigned int r[12] = {};
+        if (__get_cpuid_max(0x80000000u, nullptr) >= 0x80000004u) {
+            for (unsigned int i = 0; i < 3; ++i)
+                __get_cpuid(0x80000002u + i, &r[4 * i], &r[4 * i + 1], &r[4 * i + 2], &r[4 * i + 3]);
+            name.assign(reinterpret_cast<const char*>(r), sizeof(r));
+            name = name.c_str();                                   // up to the first NUL
+            const size_t a = name.find_first_not_of(' '), b = name.find_last_not_of(' ');
+            name = a == std::string::npos ? std::string() : name.substr(a, b - a + 1);
+        }
+#endif
+        if (name.empty()) name = "unknown";
     });
     return name.c_str();
 }
@@ -355,8 +379,22 @@ ENGINE_API int32_t engine_context_get_num_threads(const EngineContext* ctx) {
 ENGINE_API int32_t engine_context_num_physical_cores(void) {
     return (int32_t)std::max(1u, std::thread::hardware_concurrency());
 }
-ENGINE_API int32_t engine_context_has_avx2(void) { return 0; }
-ENGINE_API int32_t engine_context_has_avx512(void) { return 0; }
+ENGINE_API int32_t engine_context_has_avx2(void) {
+#if defined(__x86_64__) || defined(__i386__)
+    __builtin_cpu_init();
+    return __builtin_cpu_supports("avx2") ? 1 : 0;
+#else
+    return 0;
+#endif
+}
+ENGINE_API int32_t engine_context_has_avx512(void) {
+#if defined(__x86_64__) || defined(__i386__)
+    __builtin_cpu_init();
+    return __builtin_cpu_supports("avx512f") ? 1 : 0;
+#else
+    return 0;
+#endif
+}
 
 // ---------------------------------------------------------------------------
 // TENSOR
