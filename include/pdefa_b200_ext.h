@@ -57,6 +57,20 @@ ENGINE_API EngineStatus engine_session_output_shape(const EngineSession* sess, i
  * buf_len, NUL-terminated) and the launch count into *out_launches. */
 ENGINE_API EngineStatus engine_model_plan_summary(const EngineModel* model, int32_t precision, int64_t batch,
                                                   char* buf, size_t buf_len, int64_t* out_launches);
+/* Keeps intermediate tensor `idx` (an index of the .engine graph's tensors) readable
+ * after each run, for engine_session_debug_intermediate. The reference keeps only the
+ * intermediates no node consumes (PDEFA1.0/src/core/session.cpp:322-337); the memory
+ * planner of this library reuses the storage of the others, so a caller that wants one
+ * of them names it here first. The session's plans are lowered again at the next run
+ * (the value's storage then stays reserved). No counterpart in the reference. */
+ENGINE_API EngineStatus engine_session_keep_intermediate(EngineSession* sess, int32_t idx);
+/* Device memory plan of `model` for `batch` images at `precision`, computed without a
+ * GPU: *out_packed_bytes = the activation arena a session allocates (values whose live
+ * ranges do not overlap share bytes, as PDEFA1.0/src/memory/memory_plan.cpp:105-137
+ * plans the reference's buffers); *out_unpacked_bytes = one buffer per value.
+ * Weights, the input and the output buffers are extra. Either pointer may be NULL. */
+ENGINE_API EngineStatus engine_model_memory_plan(const EngineModel* model, int32_t precision, int64_t batch,
+                                                 size_t* out_packed_bytes, size_t* out_unpacked_bytes);
 /* Per-launch CUDA-event timing of the plan for `batch` (enable != 0 turns it on).
  * engine_session_step_times waits for the recorded events and writes, per launch in
  * engine_model_plan_summary order, the total milliseconds accumulated since timing

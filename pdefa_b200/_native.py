@@ -86,6 +86,8 @@ _SIGS = {
     "pdefa_decode_work_bytes": ([i64, i64], sz),
     "pdefa_decode_yolo_device": ([vp, i64, i64, i64, vp, f64, f64, i32, vp, vp, vp, sz, vp], C.c_int),
     "engine_model_plan_summary": ([vp, i32, i64, C.c_char_p, sz, P(i64)], C.c_int),
+    "engine_model_memory_plan": ([vp, i32, i64, P(sz), P(sz)], C.c_int),
+    "engine_session_keep_intermediate": ([vp, i32], C.c_int),
     # ops
     "engine_ops_add": ([vp, vp, P(vp)], C.c_int), "engine_ops_sub": ([vp, vp, P(vp)], C.c_int),
     "engine_ops_mul": ([vp, vp, P(vp)], C.c_int), "engine_ops_div": ([vp, vp, P(vp)], C.c_int),

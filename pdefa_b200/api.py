@@ -470,6 +470,14 @@ class Model:
         lines = [l for l in buf.value.decode().splitlines() if l]
         return [tuple(l.split(" ", 1)) for l in lines]
 
+    def memory_plan(self, precision: int = FP32, batch: int = 1) -> Tuple[int, int]:
+        """(arena bytes with live-range reuse, bytes with one buffer per value) of the
+        activations, from a device-free lowering."""
+        packed, unpacked = N.sz(), N.sz()
+        _check(N.lib().engine_model_memory_plan(self._handle, int(precision), int(batch), C.byref(packed),
+                                                C.byref(unpacked)), "memory_plan")
+        return int(packed.value), int(unpacked.value)
+
     def output_info(self, idx: int) -> TensorInfo:
         return _info(self._handle, idx, N.lib().engine_model_output_info)
 
@@ -514,6 +522,10 @@ class Session:
         s = N.SessionStats()
         _check(N.lib().engine_session_get_stats(self._handle, C.byref(s)), "get_stats")
         return {"last_run_ms": s.last_run_ms, "runs": int(s.runs)}
+
+    def keep_intermediate(self, idx: int) -> None:
+        """Keep tensor `idx` of the graph readable after runs (debug_intermediate)."""
+        _check(N.lib().engine_session_keep_intermediate(self._handle, int(idx)), "keep_intermediate")
 
     def debug_intermediate(self, idx: int) -> Tensor:
         h = C.c_void_p()

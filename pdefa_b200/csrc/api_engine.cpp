@@ -89,7 +89,7 @@ pb::Plan& EngineSession::plan_for(int64_t batch) {
     if (it != plans.end()) return *it->second;
     // keep at most two plans alive (device memory is sized per batch)
     if (plans.size() >= 2) plans.erase(plans.begin());
-    auto p = std::make_unique<pb::Plan>(graph, batch, precision, device);
+    auto p = std::make_unique<pb::Plan>(graph, batch, precision, device, keep);
     pb::Plan& ref = *p;
     plans[batch] = std::move(p);
     return ref;
@@ -605,16 +605,61 @@ ENGINE_API void engine_session_destroy(EngineSession* sess) {
         if (o) o->dev = nullptr;
     }
     sess->plans.clear();
+    if (sess->debug_buf) cudaFree(sess->debug_buf);
     if (sess->stream) cudaStreamDestroy(sess->stream);
     delete sess;
 }
-ENGINE_API EngineStatus engine_session_debug_intermediate(const EngineSession* sess, int32_t idx, const EngineTensor** out_t) {
-    (void)idx;
+// Reference: PDEFA1.0/src/api/engine_api.cpp:876-892 -> Session::debug_intermediate. After
+// a run the reference still holds the intermediates no node consumed (the others are
+// freed by their last consumer); this session keeps those too, plus the indices named
+// by engine_session_keep_intermediate. The tensor is borrowed (valid until the next
+// call for the same index or the session's destruction), fp32, in the engine's
+// internal (NHWC for rank 4) layout with the batch in dimension 0.
+ENGINE_API EngineStatus engine_session_debug_intermediate(const EngineSession* csess, int32_t idx,
+                                                          const EngineTensor** out_t) {
     if (!out_t) return ENGINE_ERR_NULL_PTR;
     *out_t = nullptr;
-    if (!sess || sess->magic != kMagicSession) return ENGINE_ERR_INVALID_HANDLE;
-    set_error("intermediate not available");
-    return ENGINE_ERR_INVALID_ARG;
+    if (!csess || csess->magic != kMagicSession) return ENGINE_ERR_INVALID_HANDLE;
+    auto* sess = const_cast<EngineSession*>(csess);
+    return guarded([&]() -> EngineStatus {
+        clear_error();
+        std::lock_guard<std::mutex> lk(sess->mu);
+        const pb::TView* v = sess->last ? sess->last->debug_view(idx) : nullptr;
+        if (!v) { set_error("intermediate not available"); return ENGINE_ERR_INVALID_ARG; }
+        PB_CUDA(cudaSetDevice(sess->device));
+        const int64_t B = sess->last->batch();
+        std::vector<int64_t> shape(v->shape, v->shape + v->rank);
+        int64_t per = 1;
+        for (int64_t d : shape) per *= d;
+        if (!shape.empty()) shape[0] *= B;
+        const size_t bytes = (size_t)std::max<int64_t>(per * B, 1) * 4;
+        if (sess->debug_cap < bytes) {
+            if (sess->debug_buf) cudaFree(sess->debug_buf);
+            sess->debug_buf = nullptr;
+            sess->debug_cap = 0;
+            PB_CUDA(cudaMalloc(&sess->debug_buf, bytes));
+            sess->debug_cap = bytes;
+        }
+        pb::TView dst = *v;
+        dst.ptr = sess->debug_buf;
+        dst.dt = pb::F32;
+        int64_t st = 1;
+        for (int d = dst.rank - 1; d >= 0; --d) { dst.stride[d] = st; st *= dst.shape[d]; }
+        dst.img_stride = per;
+        pb::launch_strided_copy(*v, dst, B, sess->stream);
+        auto& slot = sess->debug_out[idx];
+        if (!slot.store || slot.store->shape != shape) slot.store = std::make_shared<TensorStore>(shape, ENGINE_F32);
+        PB_CUDA(cudaMemcpyAsync(slot.store->host, sess->debug_buf, slot.store->nbytes, cudaMemcpyDeviceToHost,
+                                sess->stream));
+        PB_CUDA(cudaStreamSynchronize(sess->stream));
+        slot.store->host_valid = true;
+        slot.store->dev = nullptr;
+        slot.handle.magic = pb::kMagicTensor;
+        slot.handle.owned.reset();
+        slot.handle.borrowed = slot.store.get();
+        *out_t = &slot.handle;
+        return ENGINE_OK;
+    });
 }
 ENGINE_API EngineStatus engine_session_get_stats(const EngineSession* sess, EngineSessionStats* out_stats) {
     if (!sess || sess->magic != kMagicSession) return ENGINE_ERR_INVALID_HANDLE;

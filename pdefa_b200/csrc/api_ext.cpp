@@ -1,6 +1,7 @@
 // Additive entry points (include/pdefa_b200_ext.h): precision/device selection,
 // device-pointer execution, tensor-core GEMM, batched GPU decode/NMS and the
 // multi-GPU batch runner (one replica per device, contiguous shards, no collective).
+#include <algorithm>
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
@@ -213,6 +214,38 @@ ENGINE_API EngineStatus engine_model_plan_summary(const EngineModel* model, int3
             buf[n] = 0;
         }
         if (out_launches) *out_launches = plan->launch_count();
+        return ENGINE_OK;
+    });
+}
+
+ENGINE_API EngineStatus engine_session_keep_intermediate(EngineSession* sess, int32_t idx) {
+    if (!sess || sess->magic != kMagicSession) return ENGINE_ERR_INVALID_HANDLE;
+    return guarded([&]() -> EngineStatus {
+        clear_error();
+        if (idx < 0) { set_error("keep_intermediate: negative tensor index"); return ENGINE_ERR_INVALID_ARG; }
+        std::lock_guard<std::mutex> lk(sess->mu);
+        if (std::find(sess->keep.begin(), sess->keep.end(), idx) == sess->keep.end()) {
+            sess->keep.push_back(idx);
+            // plans are lowered again, with the value's storage reserved, at the next run
+            PB_CUDA(cudaSetDevice(sess->device));
+            if (sess->stream) PB_CUDA(cudaStreamSynchronize(sess->stream));
+            sess->last = nullptr;
+            sess->plans.clear();
+        }
+        return ENGINE_OK;
+    });
+}
+
+ENGINE_API EngineStatus engine_model_memory_plan(const EngineModel* model, int32_t precision, int64_t batch,
+                                                 size_t* out_packed_bytes, size_t* out_unpacked_bytes) {
+    if (!model || model->magic != kMagicModel) return ENGINE_ERR_INVALID_HANDLE;
+    return guarded([&]() -> EngineStatus {
+        clear_error();
+        auto plan = Plan::dry_run(model->graph, batch, precision);
+        size_t packed = 0;
+        pack_arena(plan->root_bytes(), plan->root_first(), plan->root_last(), &packed);
+        if (out_packed_bytes) *out_packed_bytes = packed;
+        if (out_unpacked_bytes) *out_unpacked_bytes = plan->activation_bytes();
         return ENGINE_OK;
     });
 }

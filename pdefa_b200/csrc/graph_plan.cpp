@@ -10,6 +10,8 @@
 //  6. allocation and emission of one closure per launch.
 #include "graph_plan.h"
 
+#include <climits>
+
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
@@ -874,7 +876,33 @@ struct PlanBuilder {
 
     // -------------------------------------------------------------------
     // 6. allocation
+    // Activations that own their storage ("roots": not a view, not placed inside a
+    // concat, not a weight or graph input) live in one arena. A dry lowering records
+    // each root's byte size and the range of nodes that touch it (any view of the
+    // root, its slices or its concat members); pack_arena() then gives roots whose
+    // node ranges do not intersect the same bytes, and the real lowering places each
+    // root at its offset (PDEFA1.0/src/memory/memory_plan.cpp:105-137 plans the
+    // reference's CPU buffers the same way, by live ranges).
     std::vector<void*> bufs;
+    int cur_node = -1;                       // node being emitted; nodes.size() for the outputs
+    const std::vector<size_t>* arena_off = nullptr;   // real lowering: byte offset per value id
+    char* arena = nullptr;
+
+    int root_of(int v) const {
+        while (V[v].alias_of >= 0 || V[v].place_in >= 0) v = V[v].alias_of >= 0 ? V[v].alias_of : V[v].place_in;
+        return v;
+    }
+    void touch(int v) {
+        const int r = root_of(v);
+        if ((size_t)r >= P.root_first_.size()) {
+            P.root_first_.resize(V.size(), INT_MAX);
+            P.root_last_.resize(V.size(), -1);
+            P.root_bytes_.resize(V.size(), 0);
+        }
+        const int n = std::max(cur_node, 0);
+        P.root_first_[r] = std::min(P.root_first_[r], n);
+        P.root_last_[r] = std::max(P.root_last_[r], n);
+    }
     void finalize(int v) {
         Value& x = V[v];
         if (x.buf >= 0 || !x.known) return;
@@ -900,7 +928,16 @@ struct PlanBuilder {
         x.img_stride = numel_of(x.shape);
         const size_t bytes = (size_t)x.img_stride * B * (x.dt == BF16 ? 2 : 4);
         x.buf = (int)bufs.size();
-        bufs.push_back(P.alloc(bytes > 0 ? bytes : 16));
+        if ((size_t)v >= P.root_bytes_.size()) {
+            P.root_first_.resize(V.size(), INT_MAX);
+            P.root_last_.resize(V.size(), -1);
+            P.root_bytes_.resize(V.size(), 0);
+        }
+        P.root_bytes_[v] = std::max<size_t>(bytes, 16);
+        if (arena_off && (size_t)v < arena_off->size() && (*arena_off)[v] != SIZE_MAX)
+            bufs.push_back(arena + (*arena_off)[v]);
+        else
+            bufs.push_back(P.alloc(bytes > 0 ? bytes : 16));
     }
 
     void* weight_f32(int w) {
@@ -917,6 +954,7 @@ struct PlanBuilder {
 
     TView view(int v) {
         finalize(v);
+        touch(v);
         const Value& x = V[v];
         TView t;
         t.ptr = static_cast<char*>(bufs[x.buf]) + x.off * (x.dt == BF16 ? 2 : 4);
@@ -929,6 +967,7 @@ struct PlanBuilder {
 
     bool dense(int v) {
         finalize(v);
+        touch(v);
         const Value& x = V[v];
         return x.stride == dense_strides(x.shape) && (x.img_stride == numel_of(x.shape) || x.img_stride == 0);
     }
@@ -994,10 +1033,12 @@ struct PlanBuilder {
             }
         }
         for (size_t i = 0; i < nodes.size(); ++i) {
+            cur_node = (int)i;
             if (skip[i] == 3) { emit_head(); continue; }
             if (skip[i]) continue;
             emit_node((int)i);
         }
+        cur_node = (int)nodes.size();
         // outputs: dense fp32, rank-4 converted to NCHW (session.cpp:347-361)
         for (size_t k = 0; k < g.outputs.size(); ++k) {
             const int v = vid[g.outputs[k]];
@@ -1031,6 +1072,24 @@ struct PlanBuilder {
             P.outputs_.push_back(obuf);
             P.out_bytes_.push_back(bytes);
             P.out_shapes_.push_back(bshape);
+        }
+        // Intermediates readable after a run: values produced by an emitted node that
+        // no node consumes, and the requested ones; their storage stays reserved past
+        // the last node, so no later launch reuses it.
+        cur_node = (int)nodes.size() + 1;
+        std::vector<int32_t> want;
+        for (size_t i = 0; i < nodes.size(); ++i) {
+            if (skip[i]) continue;     // fused away or inside the fused head: never written
+            for (int32_t o : nodes[i].outputs) {
+                if (o < 0) continue;
+                const bool asked = std::find(P.keep_.begin(), P.keep_.end(), o) != P.keep_.end();
+                if (asked || consumers[o] == 0) want.push_back(o);
+            }
+        }
+        for (int32_t idx : want) {
+            auto it = vid.find(idx);
+            if (it == vid.end() || !V[it->second].known || V[it->second].weight >= 0) continue;
+            P.debug_[idx] = view(it->second);
         }
     }
 
@@ -1580,8 +1639,8 @@ struct PlanBuilder {
     }
 };
 
-Plan::Plan(std::shared_ptr<const Graph> g, int64_t batch, int precision, int device)
-    : g_(std::move(g)), batch_(batch), prec_(precision), device_(device) {
+Plan::Plan(std::shared_ptr<const Graph> g, int64_t batch, int precision, int device, std::vector<int32_t> keep)
+    : g_(std::move(g)), batch_(batch), prec_(precision), device_(device), keep_(std::move(keep)) {
     require_device(device);
     if (batch < 1) fail(ENGINE_ERR_INVALID_ARG, "batch must be >= 1");
     PB_CUDA(cudaSetDevice(device));
@@ -1594,8 +1653,8 @@ Plan::Plan(std::shared_ptr<const Graph> g, int64_t batch, int precision, int dev
     }
 }
 
-Plan::Plan(DryTag, std::shared_ptr<const Graph> g, int64_t batch, int precision)
-    : g_(std::move(g)), dry_(true), batch_(batch), prec_(precision), device_(0) {
+Plan::Plan(DryTag, std::shared_ptr<const Graph> g, int64_t batch, int precision, std::vector<int32_t> keep)
+    : g_(std::move(g)), dry_(true), batch_(batch), prec_(precision), device_(0), keep_(std::move(keep)) {
     if (batch < 1) fail(ENGINE_ERR_INVALID_ARG, "batch must be >= 1");
     build();
 }
@@ -1638,9 +1697,68 @@ void* Plan::alloc(size_t bytes) {
     return p;
 }
 
+// Offsets of the arena roots: largest first, each at the lowest 256-byte aligned
+// offset that overlaps no already placed root whose node range intersects its own.
+// first/last: node range per value id; bytes: 0 for values that are not roots.
+std::vector<size_t> pack_arena(const std::vector<size_t>& bytes, const std::vector<int>& first,
+                               const std::vector<int>& last, size_t* total) {
+    std::vector<size_t> off(bytes.size(), SIZE_MAX);
+    std::vector<int> ids;
+    for (size_t v = 0; v < bytes.size(); ++v)
+        if (bytes[v] > 0 && v < first.size() && first[v] <= last[v]) ids.push_back((int)v);
+    std::stable_sort(ids.begin(), ids.end(), [&](int a, int b) {
+        return bytes[a] != bytes[b] ? bytes[a] > bytes[b] : first[a] < first[b];
+    });
+    struct Placed { size_t lo, hi; int first, last; };
+    std::vector<Placed> placed;
+    size_t top = 0;
+    for (int v : ids) {
+        const size_t need = (bytes[v] + 255) & ~size_t(255);
+        std::vector<std::pair<size_t, size_t>> busy;
+        for (const Placed& p : placed)
+            if (p.first <= last[v] && first[v] <= p.last) busy.push_back({p.lo, p.hi});
+        std::sort(busy.begin(), busy.end());
+        size_t at = 0;
+        for (const auto& b : busy) {
+            if (at + need <= b.first) break;
+            at = std::max(at, b.second);
+        }
+        off[v] = at;
+        placed.push_back({at, at + need, first[v], last[v]});
+        top = std::max(top, at + need);
+    }
+    // self-check: roots live at the same time never share a byte
+    for (size_t i = 0; i < placed.size(); ++i)
+        for (size_t j = i + 1; j < placed.size(); ++j) {
+            const Placed& a = placed[i];
+            const Placed& b = placed[j];
+            if (a.first <= b.last && b.first <= a.last && a.lo < b.hi && b.lo < a.hi)
+                fail(ENGINE_ERR_RUNTIME, "memory plan: overlapping live buffers");
+        }
+    *total = top;
+    return off;
+}
+
 void Plan::build() {
+    if (dry_ || std::getenv("PDEFA_NO_ARENA") != nullptr) {
+        PlanBuilder b(*this, *g_);
+        b.build();
+        if (!dry_) activation_bytes_ = 0;
+        for (size_t v = 0; v < root_bytes_.size(); ++v) activation_bytes_ += root_bytes_[v];
+        return;
+    }
+    // A dry lowering of the same graph records every root's size and node range; the
+    // real lowering then places the roots in one arena at packed offsets.
+    Plan probe(DryTag{}, g_, batch_, prec_, keep_);
+    size_t total = 0;
+    const std::vector<size_t> off = pack_arena(probe.root_bytes_, probe.root_first_, probe.root_last_, &total);
+    char* base = static_cast<char*>(alloc(std::max<size_t>(total, 256)));
     PlanBuilder b(*this, *g_);
+    b.arena_off = &off;
+    b.arena = base;
     b.build();
+    activation_bytes_ = total;
+    unpacked_bytes_ = probe.activation_bytes_;
 }
 
 void Plan::run_steps(cudaStream_t s) {

@@ -8,6 +8,7 @@
 #pragma once
 
 #include <functional>
+#include <map>
 #include <memory>
 #include <string>
 #include <vector>
@@ -48,7 +49,10 @@ struct PlanStep {
 
 class Plan {
 public:
-    Plan(std::shared_ptr<const Graph> g, int64_t batch, int precision, int device);
+    // keep: engine tensor indices whose values stay readable after a run (see
+    // debug_view); values no node consumes are always kept, as in the reference.
+    Plan(std::shared_ptr<const Graph> g, int64_t batch, int precision, int device,
+         std::vector<int32_t> keep = {});
     // Device-free lowering: every pass runs and every launch is recorded, but nothing
     // is allocated or copied (addresses are placeholders). Used to validate a model
     // and to inspect its launch list without a GPU.
@@ -78,6 +82,20 @@ public:
     void set_step_timing(bool on) { timing_ = on; }
     std::vector<double> collect_step_ms();
     int64_t batch() const { return batch_; }
+    // Device bytes of the activations: packed in the arena, and what one buffer per
+    // value would take.
+    size_t activation_bytes() const { return activation_bytes_; }
+    size_t unpacked_activation_bytes() const { return unpacked_bytes_; }
+    const std::vector<size_t>& root_bytes() const { return root_bytes_; }
+    const std::vector<int>& root_first() const { return root_first_; }
+    const std::vector<int>& root_last() const { return root_last_; }
+    // Device view of intermediate tensor `idx` after a run: values no node consumes
+    // (PDEFA1.0/src/core/session.cpp:322-337 frees every other intermediate once its
+    // last consumer ran) and the indices passed as `keep`. nullptr if not kept.
+    const TView* debug_view(int32_t idx) const {
+        auto it = debug_.find(idx);
+        return it == debug_.end() ? nullptr : &it->second;
+    }
     int precision() const { return prec_; }
     int device() const { return device_; }
 
@@ -86,7 +104,9 @@ private:
     void* alloc(size_t bytes);
 
     struct DryTag {};
-    Plan(DryTag, std::shared_ptr<const Graph> g, int64_t batch, int precision);
+    Plan(DryTag, std::shared_ptr<const Graph> g, int64_t batch, int precision, std::vector<int32_t> keep = {});
+    std::vector<int32_t> keep_;
+    std::map<int32_t, TView> debug_;
     std::shared_ptr<const Graph> g_;
     bool dry_ = false;
     uintptr_t dry_next_ = 0x10000000;
@@ -115,8 +135,19 @@ private:
     cudaEvent_t take_event();
     const float* cur_in_ = nullptr;   // overrides valid during run()
     float* cur_out_ = nullptr;
+    // memory plan: per value id, bytes of an arena root (0: not a root) and the range
+    // of node indices that touch it (filled by every lowering)
+    std::vector<size_t> root_bytes_;
+    std::vector<int> root_first_, root_last_;
+    size_t activation_bytes_ = 0, unpacked_bytes_ = 0;
     friend struct PlanBuilder;
 };
+
+// Arena offsets (bytes) of the activation roots: largest first, each at the lowest
+// aligned offset free of every placed root whose node range intersects its own;
+// SIZE_MAX for values that are not roots. *total: arena size.
+std::vector<size_t> pack_arena(const std::vector<size_t>& bytes, const std::vector<int>& first,
+                               const std::vector<int>& last, size_t* total);
 
 // Kernel the reference dispatcher picks for a batch-1 NHWC conv
 // (PDEFA1.0/src/ops/conv2d.cpp:602-642): 0 direct (Cin <= 16, not pure 1x1),

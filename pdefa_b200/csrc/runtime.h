@@ -80,6 +80,16 @@ struct EngineSession {
     EngineProfileFn profile_fn = nullptr;
     void* profile_user = nullptr;
     std::mutex mu;
+    // intermediates: indices kept readable after a run (besides the unconsumed
+    // ones), and the host tensors engine_session_debug_intermediate hands out
+    std::vector<int32_t> keep;
+    struct Debug {
+        std::shared_ptr<pb::TensorStore> store;
+        EngineTensor handle;
+    };
+    std::map<int32_t, Debug> debug_out;
+    void* debug_buf = nullptr;       // dense fp32 staging on the device
+    size_t debug_cap = 0;
 
     pb::Plan& plan_for(int64_t batch);
     void run();

@@ -87,3 +87,15 @@ def test_yolo11n_plan_lowers_attention(tmp_path):
     kinds = Counter(k for k, _ in m.plan_summary(pb.BF16, batch=8))
     assert kinds["conv_stem_tc"] == 1 and kinds["conv_tc_bf16"] == 79 and kinds["conv_simt"] == 0
     assert kinds["conv_direct"] == 0
+
+
+def test_memory_plan_reuses_activation_storage(y8n):
+    """Live-range packing (engine_model_memory_plan): YOLOv8n-640 at 256 images keeps
+    its BF16 activations in a fraction of the one-buffer-per-value footprint; the
+    planner's own self-check rejects any overlap of live buffers."""
+    m, _ = y8n
+    packed, unpacked = m.memory_plan(pb.BF16, batch=256)
+    assert unpacked > 8e9
+    assert packed < 0.2 * unpacked and packed < 2e9
+    p1, u1 = m.memory_plan(pb.FP32, batch=1)
+    assert 0 < p1 < u1
