@@ -84,14 +84,15 @@ using namespace pb;
 // ---------------------------------------------------------------------------
 // Session internals
 // ---------------------------------------------------------------------------
-pb::Plan& EngineSession::plan_for(int64_t batch) {
-    auto it = plans.find(batch);
+pb::Plan& EngineSession::plan_for(int64_t batch, const std::vector<int64_t>& in_shape) {
+    const auto key = std::make_pair(batch, in_shape);
+    auto it = plans.find(key);
     if (it != plans.end()) return *it->second;
     // keep at most two plans alive (device memory is sized per batch)
     if (plans.size() >= 2) plans.erase(plans.begin());
-    auto p = std::make_unique<pb::Plan>(graph, batch, precision, device, keep);
+    auto p = std::make_unique<pb::Plan>(graph, batch, precision, device, keep, in_shape);
     pb::Plan& ref = *p;
-    plans[batch] = std::move(p);
+    plans[key] = std::move(p);
     return ref;
 }
 
@@ -103,14 +104,18 @@ void EngineSession::run() {
     if (x.dtype != ENGINE_F32) fail(ENGINE_ERR_INVALID_ARG, "input must be F32");
     const auto& info = graph->input_infos.empty() ? std::vector<int64_t>{} : graph->input_infos[0].shape;
     if (x.shape.empty()) fail(ENGINE_ERR_INVALID_SHAPE, "input has rank 0");
+    // Like the reference interpreter, which runs the graph on whatever input it is
+    // given (session.cpp:181-215), an input whose image size differs from the
+    // declared one gets a plan lowered for its own shape; the rank must match.
+    std::vector<int64_t> own;
     if (!info.empty()) {
         if (x.shape.size() != info.size()) fail(ENGINE_ERR_INVALID_SHAPE, "input rank differs from the model input");
         for (size_t d = 1; d < info.size(); ++d)
-            if (info[d] > 0 && x.shape[d] != info[d])
-                fail(ENGINE_ERR_INVALID_SHAPE, "input shape differs from the model input");
+            if (info[d] > 0 && x.shape[d] != info[d]) own.assign(x.shape.begin(), x.shape.end());
+        if (!own.empty()) own[0] = 1;
     }
     const int64_t batch = x.shape[0];
-    pb::Plan& p = plan_for(batch);
+    pb::Plan& p = plan_for(batch, own);
     for (size_t i = 0; i < inputs.size() && i < graph->inputs.size(); ++i) {
         if (!inputs[i]) fail(ENGINE_ERR_INVALID_ARG, "input " + std::to_string(i) + " is not set");
         TensorStore& t = *inputs[i]->ptr();

@@ -242,6 +242,7 @@ struct PlanBuilder {
             x.known = true;
             x.dt = F32;
             std::vector<int64_t> s = i < g.input_infos.size() ? g.input_infos[i].shape : std::vector<int64_t>{};
+            if (i == 0 && !P.in_shape_.empty()) s = P.in_shape_;
             if (s.empty()) fail(ENGINE_ERR_INVALID_FORMAT, "model has no input shape information (v1 file)");
             for (auto& d : s) if (d <= 0) d = 1;
             s[0] = 1;
@@ -1639,8 +1640,10 @@ struct PlanBuilder {
     }
 };
 
-Plan::Plan(std::shared_ptr<const Graph> g, int64_t batch, int precision, int device, std::vector<int32_t> keep)
-    : g_(std::move(g)), batch_(batch), prec_(precision), device_(device), keep_(std::move(keep)) {
+Plan::Plan(std::shared_ptr<const Graph> g, int64_t batch, int precision, int device, std::vector<int32_t> keep,
+           std::vector<int64_t> in_shape)
+    : g_(std::move(g)), batch_(batch), prec_(precision), device_(device), keep_(std::move(keep)),
+      in_shape_(std::move(in_shape)) {
     require_device(device);
     if (batch < 1) fail(ENGINE_ERR_INVALID_ARG, "batch must be >= 1");
     PB_CUDA(cudaSetDevice(device));
@@ -1653,8 +1656,10 @@ Plan::Plan(std::shared_ptr<const Graph> g, int64_t batch, int precision, int dev
     }
 }
 
-Plan::Plan(DryTag, std::shared_ptr<const Graph> g, int64_t batch, int precision, std::vector<int32_t> keep)
-    : g_(std::move(g)), dry_(true), batch_(batch), prec_(precision), device_(0), keep_(std::move(keep)) {
+Plan::Plan(DryTag, std::shared_ptr<const Graph> g, int64_t batch, int precision, std::vector<int32_t> keep,
+           std::vector<int64_t> in_shape)
+    : g_(std::move(g)), dry_(true), batch_(batch), prec_(precision), device_(0), keep_(std::move(keep)),
+      in_shape_(std::move(in_shape)) {
     if (batch < 1) fail(ENGINE_ERR_INVALID_ARG, "batch must be >= 1");
     build();
 }
@@ -1749,7 +1754,7 @@ void Plan::build() {
     }
     // A dry lowering of the same graph records every root's size and node range; the
     // real lowering then places the roots in one arena at packed offsets.
-    Plan probe(DryTag{}, g_, batch_, prec_, keep_);
+    Plan probe(DryTag{}, g_, batch_, prec_, keep_, in_shape_);
     size_t total = 0;
     const std::vector<size_t> off = pack_arena(probe.root_bytes_, probe.root_first_, probe.root_last_, &total);
     char* base = static_cast<char*>(alloc(std::max<size_t>(total, 256)));

@@ -51,8 +51,10 @@ class Plan {
 public:
     // keep: engine tensor indices whose values stay readable after a run (see
     // debug_view); values no node consumes are always kept, as in the reference.
+    // in_shape: shape of one image of input 0 when it differs from the declared one
+    // (empty: the declared shape).
     Plan(std::shared_ptr<const Graph> g, int64_t batch, int precision, int device,
-         std::vector<int32_t> keep = {});
+         std::vector<int32_t> keep = {}, std::vector<int64_t> in_shape = {});
     // Device-free lowering: every pass runs and every launch is recorded, but nothing
     // is allocated or copied (addresses are placeholders). Used to validate a model
     // and to inspect its launch list without a GPU.
@@ -104,8 +106,10 @@ private:
     void* alloc(size_t bytes);
 
     struct DryTag {};
-    Plan(DryTag, std::shared_ptr<const Graph> g, int64_t batch, int precision, std::vector<int32_t> keep = {});
+    Plan(DryTag, std::shared_ptr<const Graph> g, int64_t batch, int precision, std::vector<int32_t> keep = {},
+         std::vector<int64_t> in_shape = {});
     std::vector<int32_t> keep_;
+    std::vector<int64_t> in_shape_;
     std::map<int32_t, TView> debug_;
     std::shared_ptr<const Graph> g_;
     bool dry_ = false;

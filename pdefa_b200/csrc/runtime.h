@@ -71,7 +71,8 @@ struct EngineSession {
     int precision = pb::PREC_FP32;
     cudaStream_t stream = nullptr;
     std::vector<const EngineTensor*> inputs;
-    std::map<int64_t, std::unique_ptr<pb::Plan>> plans;   // by batch size
+    // by (batch, input 0 shape of one image; empty = the model's declared shape)
+    std::map<std::pair<int64_t, std::vector<int64_t>>, std::unique_ptr<pb::Plan>> plans;
     pb::Plan* last = nullptr;
     std::vector<std::shared_ptr<pb::TensorStore>> outputs;
     std::vector<EngineTensor> out_handles;
@@ -91,7 +92,7 @@ struct EngineSession {
     void* debug_buf = nullptr;       // dense fp32 staging on the device
     size_t debug_cap = 0;
 
-    pb::Plan& plan_for(int64_t batch);
+    pb::Plan& plan_for(int64_t batch, const std::vector<int64_t>& in_shape = {});
     void run();
 };
 

@@ -246,6 +246,24 @@ def test_tiny_classifier_graph(golden, engine_dir):
     assert normwise(y, d["y"]) <= 1e-5
 
 
+def test_input_size_other_than_declared(engine_dir):
+    """The reference interpreter runs a graph on whatever image size it is given (its
+    BatchInference feeds 640x640 images to a model declared at 64x64); a session here
+    lowers a plan for the input's own size and matches the reference engine on it."""
+    import tests.golden.make_golden as mg
+    from oracle import ref_engine as R
+    if not R.available():
+        pytest.skip("compiled reference engine (oracle/_ref) not built")
+    p = str(engine_dir / "tiny_any.engine")
+    write_engine(p, mg.build_tiny())
+    for h, w in ((96, 80), (64, 64), (130, 47)):
+        x = np.random.default_rng(h * w).random((1, 3, h, w), dtype=np.float32)
+        y = run_engine(p, x, pb.FP32)
+        ref = R.RefSession(p, threads=4).run(x)
+        assert y.shape == (1, 4)
+        assert normwise(y, ref) <= 1e-5, (h, w)
+
+
 # ---------------------------------------------------------------- decode / NMS
 def _cases():
     with open(os.path.join(GOLDEN, "decode_expected.json")) as f:
