@@ -14,6 +14,7 @@
 #endif
 #include <cmath>
 #include <cstdlib>
+#include <map>
 #include <random>
 #include <thread>
 
@@ -177,28 +178,69 @@ EngineTensor* new_tensor(std::vector<int64_t> shape, EngineDType dt) {
 }
 
 // Device scratch on the default device for the stateless ops.
+// Per-thread, per-device resources of the direct ops (engine_ops_*): one non-blocking
+// stream and a workspace that grows to the largest op seen and is reused, so a call
+// makes no cudaMalloc/cudaFree and creates no stream once warm (the reference's ops run
+// in the caller's thread too, ops/matmul.cpp:107-135). Freed when the thread exits.
+struct OpCache {
+    int device = -1;
+    cudaStream_t stream = nullptr;
+    std::vector<std::pair<void*, size_t>> chunks;   // device workspace pieces, kept across calls
+    ~OpCache() {
+        if (device < 0) return;
+        if (cudaSetDevice(device) != cudaSuccess) return;
+        if (stream) cudaStreamSynchronize(stream);
+        for (auto& c : chunks) cudaFree(c.first);
+        if (stream) cudaStreamDestroy(stream);
+    }
+};
+
+OpCache& op_cache(int dev) {
+    static thread_local std::map<int, OpCache> caches;
+    OpCache& c = caches[dev];
+    if (c.device < 0) {
+        PB_CUDA(cudaSetDevice(dev));
+        PB_CUDA(cudaStreamCreateWithFlags(&c.stream, cudaStreamNonBlocking));
+        c.device = dev;
+    }
+    return c;
+}
+
+// One direct op: bump allocations from the thread's workspace on its stream; the
+// destructor waits for the stream, so workspace and host copies are settled when the
+// op returns.
 struct OpDevice {
     int device = -1;
     cudaStream_t stream = nullptr;
-    std::vector<void*> bufs;
+    OpCache* cache = nullptr;
+    size_t chunk = 0, used = 0;
     explicit OpDevice(int dev) : device(dev) {
         require_device(dev);
         PB_CUDA(cudaSetDevice(dev));
-        PB_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+        cache = &op_cache(dev);
+        stream = cache->stream;
     }
     ~OpDevice() {
         cudaSetDevice(device);
         if (stream) cudaStreamSynchronize(stream);
-        for (void* p : bufs) cudaFree(p);
-        if (stream) cudaStreamDestroy(stream);
     }
     void* alloc(size_t n) {
-        void* p = nullptr;
-        if (cudaMalloc(&p, std::max<size_t>(n, 16)) != cudaSuccess) {
-            cudaGetLastError();
-            fail(ENGINE_ERR_OUT_OF_MEMORY, "device allocation failed");
+        n = (std::max<size_t>(n, 16) + 255) & ~size_t(255);
+        auto& cs = cache->chunks;
+        while (chunk < cs.size() && used + n > cs[chunk].second) { ++chunk; used = 0; }
+        if (chunk == cs.size()) {
+            // a new piece; earlier pieces may still be in use by this op's queued work
+            const size_t sz = std::max<size_t>(n, cs.empty() ? (size_t)4 << 20 : cs.back().second * 2);
+            void* p = nullptr;
+            if (cudaMalloc(&p, sz) != cudaSuccess) {
+                cudaGetLastError();
+                fail(ENGINE_ERR_OUT_OF_MEMORY, "device allocation failed");
+            }
+            cs.push_back({p, sz});
+            used = 0;
         }
-        bufs.push_back(p);
+        void* p = static_cast<char*>(cs[chunk].first) + used;
+        used += n;
         return p;
     }
     void* upload(TensorStore& t) {
@@ -740,8 +782,8 @@ ENGINE_API EngineStatus engine_ops_matmul_ex(const EngineTensor* a, const Engine
         const float* da = static_cast<const float*>(od.upload(A));
         const float* db = static_cast<const float*>(od.upload(Bt));
         float* dc = static_cast<float*>(od.alloc(C.nbytes));
-        const EngineStatus st = engine_gemm_f32_device(da, db, dc, M, N, K, precision, od.stream);
-        if (st != ENGINE_OK) return st;
+        const size_t sb = gemm_device_scratch_bytes(M, N, K, precision);
+        gemm_device(da, db, dc, M, N, K, precision, sb ? od.alloc(sb) : nullptr, od.stream);
         od.download(C, dc);
         return ENGINE_OK;
     });

@@ -16,27 +16,6 @@ using namespace pb;
 
 namespace {
 
-// Per-device scratch kept across calls (GEMM operand staging).
-struct Scratch {
-    void* p = nullptr;
-    size_t n = 0;
-};
-std::mutex g_scratch_mu;
-Scratch g_scratch[64];
-
-void* scratch(int dev, size_t n) {
-    std::lock_guard<std::mutex> lk(g_scratch_mu);
-    Scratch& s = g_scratch[dev];
-    if (s.n < n) {
-        if (s.p) cudaFree(s.p);
-        s.p = nullptr;
-        s.n = 0;
-        if (cudaMalloc(&s.p, n) != cudaSuccess) { cudaGetLastError(); fail(ENGINE_ERR_OUT_OF_MEMORY, "scratch allocation failed"); }
-        s.n = n;
-    }
-    return s.p;
-}
-
 struct DeviceBuffer {
     void* p = nullptr;
     explicit DeviceBuffer(size_t n) {
@@ -310,24 +289,52 @@ ENGINE_API int64_t engine_session_launch_count(const EngineSession* sess, int64_
     }
 }
 
+}  // extern "C"
+
+namespace pb {
+size_t gemm_device_scratch_bytes(int64_t m, int64_t n, int64_t k, int precision) {
+    if (precision == PREC_FP32) return 0;
+    const int esz = precision == PREC_BF16 ? 2 : 4;
+    return ((size_t)m * k + (size_t)n * k) * esz + 512;
+}
+
+// C[m,n] = A[m,k] B[k,n] on `s`; tensor-core precisions stage their operands in
+// `scratch` (gemm_device_scratch_bytes), which must stay untouched until the GEMM ran.
+void gemm_device(const float* d_a, const float* d_b, float* d_c, int64_t m, int64_t n, int64_t k, int precision,
+                 void* scratch, cudaStream_t s) {
+    int dev = 0;
+    PB_CUDA(cudaGetDevice(&dev));
+    if (precision != PREC_FP32) {
+        const int op_dt = precision == PREC_BF16 ? BF16 : F32;
+        const bool ok = n % 16 == 0 && k % (op_dt == BF16 ? 16 : 8) == 0 && ((uintptr_t)d_c % 16) == 0;
+        if (ok) {
+            launch_gemm_tc(d_a, d_b, d_c, m, n, k, op_dt, scratch, device_error_word(dev), s);
+            return;
+        }
+    }
+    launch_gemm_f32(d_a, d_b, d_c, nullptr, m, n, k, k, n, n, 1, 0, 0, 0, s);
+}
+}  // namespace pb
+
+extern "C" {
+
 ENGINE_API EngineStatus engine_gemm_f32_device(const float* d_a, const float* d_b, float* d_c, int64_t m, int64_t n,
                                                int64_t k, int32_t precision, void* stream) {
     if (!d_a || !d_b || !d_c) return ENGINE_ERR_NULL_PTR;
     return guarded([&]() -> EngineStatus {
         cudaStream_t s = static_cast<cudaStream_t>(stream);
-        int dev = 0;
-        PB_CUDA(cudaGetDevice(&dev));
-        if (precision != PREC_FP32) {
-            const int op_dt = precision == PREC_BF16 ? BF16 : F32;
-            const int esz = op_dt == BF16 ? 2 : 4;
-            const bool ok = n % 16 == 0 && k % (op_dt == BF16 ? 16 : 8) == 0 && ((uintptr_t)d_c % 16) == 0;
-            if (ok) {
-                void* sc = scratch(dev, ((size_t)m * k + (size_t)n * k) * esz + 256);
-                launch_gemm_tc(d_a, d_b, d_c, m, n, k, op_dt, sc, device_error_word(dev), s);
-                return ENGINE_OK;
-            }
+        // Operand staging comes from the stream-ordered pool: calls on different
+        // streams never share it, and a warm pool makes no cudaMalloc.
+        void* sc = nullptr;
+        const size_t sb = gemm_device_scratch_bytes(m, n, k, precision);
+        if (sb) PB_CUDA(cudaMallocAsync(&sc, sb, s));
+        try {
+            gemm_device(d_a, d_b, d_c, m, n, k, precision, sc, s);
+        } catch (...) {
+            if (sc) cudaFreeAsync(sc, s);
+            throw;
         }
-        launch_gemm_f32(d_a, d_b, d_c, nullptr, m, n, k, k, n, n, 1, 0, 0, 0, s);
+        if (sc) PB_CUDA(cudaFreeAsync(sc, s));
         return ENGINE_OK;
     });
 }

@@ -167,4 +167,10 @@ LetterboxGeom letterbox_geometry(int src_w, int src_h, int W, int H, float scale
 void launch_letterbox_u8(const uint8_t* d_src, int64_t n, int channels, const LetterboxGeom& g, float* d_out,
                          cudaStream_t s);
 
+// GEMM on device pointers (engine_gemm_f32_device, engine_ops_matmul): strict FP32
+// SIMT, or tcgen05 with operands staged in `scratch` (gemm_device_scratch_bytes).
+size_t gemm_device_scratch_bytes(int64_t m, int64_t n, int64_t k, int precision);
+void gemm_device(const float* d_a, const float* d_b, float* d_c, int64_t m, int64_t n, int64_t k, int precision,
+                 void* scratch, cudaStream_t s);
+
 }  // namespace pb
