@@ -41,18 +41,33 @@ sys.path.insert(0, ROOT)
 METRIC = "YOLOv8n-640 images/sec at 1/2/4/8 B200; conv TFLOP/s vs tensor-core peak"
 
 
-def conv_tc_traffic_per_launch(batch: int):
-    """DRAM bytes (read + write) per conv_tc launch at `batch`, from the committed ncu
-    capture in profiles/ (bytes per image of one step's 62 launches, scaled by batch)."""
-    p = os.path.join(ROOT, "profiles", "conv_tc_dram_traffic_yolov8n640.md")
-    try:
-        with open(p) as f:
-            for line in f:
-                if line.startswith("traffic_bytes_per_image:"):
-                    return float(line.split(":")[1]) * batch / 62
-    except OSError:
-        pass
-    return None
+# DRAM bytes (read + write) per image over the 62 conv_tc launches of one YOLOv8n-640
+# BF16 step: one ncu capture (dram__bytes_read.sum + dram__bytes_write.sum) of a whole
+# step at batch 32, divided by 32 (profiles/conv_tc_dram_traffic_yolov8n640.md). Every
+# launch streams its images once, so the figure is scaled to the bench batch by images;
+# at batch 32 more producer->consumer pairs stay in L2 than at 256, so it is a lower
+# bound there.
+CONV_TC_DRAM_BYTES_PER_IMAGE_B32 = 48.1e6
+
+
+def per_layer_roofline(summary, step_ms, steps, info, B, peak_tflops, hbm_gbs, abytes):
+    """(bound ms, measured ms) summed over the conv launches: each layer's bound is
+    max(FLOPs / tensor peak, bytes / HBM bandwidth), bytes = activations in (fp32 for
+    the stem's graph input) and out once."""
+    layer_of = {name: (cin, cout, k, s, h, w) for name, cin, cout, k, s, h, w in info["convs"]}
+    ideal = meas = 0.0
+    for i, (kd, name) in enumerate(summary):
+        key = name.strip("/").replace("/conv/Conv", "")
+        if not kd.startswith("conv") or key not in layer_of:
+            continue
+        cin, cout, k, s, h, w = layer_of[key]
+        ho, wo = (h + 2 * (k // 2) - k) // s + 1, (w + 2 * (k // 2) - k) // s + 1
+        fl = 2.0 * cin * cout * k * k * ho * wo * B
+        by = ((4 if kd.startswith("conv_stem") or kd == "conv_direct" else abytes) * cin * h * w
+              + abytes * cout * ho * wo) * B
+        ideal += max(fl / (peak_tflops * 1e12), by / (hbm_gbs * 1e9)) * 1e3
+        meas += step_ms[i] / steps
+    return ideal, meas
 
 
 def load_peaks():
@@ -148,6 +163,18 @@ def cpu_reference(images: int, threads: int, model: str = "yolov8n"):
     return step
 
 
+def cpu_model():
+    """Host CPU model name (the line /proc/cpuinfo gives), for the CPU baseline records."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
 def run_reference_arm(args, rank):
     if rank != 0:
         return
@@ -163,13 +190,46 @@ def run_reference_arm(args, rank):
     value = args.ref_images * args.steps / tot
     sample = (f"{args.ref_images} images per step, batch-1 Session.run of the reference engine "
               f"(oracle/_ref, AVX2) + reference decode/NMS restated in Python (oracle/decode_ref.py)")
+    # the reference's CPU path on configs[0], [1] and [4] (same shapes as our records)
+    configs = None
+    if not args.no_configs:
+        import numpy as np
+        from oracle import ref_engine as R
+        from pdefa_b200.engine_file import write_engine
+        from pdefa_b200.yolo import build_single_conv, build_yolov8
+        rng = np.random.default_rng(42)
+        A = rng.standard_normal((512, 512), dtype=np.float32)
+        Bm = rng.standard_normal((512, 512), dtype=np.float32)
+        R.time_matmul(A, Bm, 3, threads)
+        mm_ms = R.time_matmul(A, Bm, 30, threads) * 1e3
+        g, _ = build_single_conv(cin=3, cout=16, k=3, s=2, hw=640, act=True, seed=1)
+        sp = os.path.join(tempfile.mkdtemp(), "stem.engine")
+        write_engine(sp, g)
+        x = np.random.default_rng(0).random((1, 3, 640, 640), dtype=np.float32)
+        rs = R.RefSession(sp, threads=threads)
+        rs.time_run(x, 3)
+        stem_ms = rs.time_run(x, 20) * 1e3
+        g, _ = build_yolov8("m", imgsz=640, seed=0)
+        mp = os.path.join(tempfile.mkdtemp(), "y8m.engine")
+        write_engine(mp, g)
+        rm = R.RefSession(mp, threads=threads)
+        rm.time_run(x, 1)
+        m_s = rm.time_run(x, 3)
+        configs = {"configs[0]_ops_matmul_512": {"fp32_call_ms": round(mm_ms, 4),
+                                                "gflops": round(2 * 512 ** 3 / mm_ms / 1e6, 1),
+                                                "api": "engine_ops_matmul (AVX2 sgemm, matmul_avx2.cpp:538-681)"},
+                   "configs[1]_stem_conv": {"fp32_b1_ms": round(stem_ms, 4), "path": "Session.run, direct NHWC conv"},
+                   "configs[4]_yolov8m_tf32_b64": {"images_per_s": round(1.0 / m_s, 3),
+                                                   "sample": "3 images, batch-1 Session.run, FP32"}}
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": value, "unit": "images/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": tot / args.steps * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": config(args, 1),
-        "cpu_baseline": {"value": value, "unit": "images/s", "cores": threads, "kind": "reference", "sample": sample},
+        "cpu_baseline": {"value": value, "unit": "images/s", "cores": threads, "kind": "reference", "sample": sample,
+                         "cpu": cpu_model()},
         "e2e": {"value": value, "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "configs": configs,
     }))
 
 
@@ -235,6 +295,134 @@ def run_layers(args):
                           "peaks": f"{src}: {peak_sus:.1f} TFLOP/s sustained, {hbm:.0f} GB/s"}), flush=True)
 
 
+def measure_configs(args, local):
+    """BASELINE.json configs[0], [1] and [4] on this GPU (rank 0, one GPU): per-config
+    records of the same JSON line.
+    * ops_matmul A[512,512] @ B[512,512] (seed 42, N(0,1)) through the C ABI
+      with host tensors (engine_ops_matmul_ex: copies in, GEMM, copy out: the call a
+      ctypes user makes), median over calls, per precision; plus the device GEMM alone
+      (engine_gemm_f32_device on resident operands, CUDA events, mean of 200).
+    * the stem Conv-BN-SiLU [1,3,640,640] -> [1,16,320,320] (3x3 s2) through
+      a Session at batch 1 (FP32 strict and BF16), the conv launch's CUDA-event time and
+      its HBM GB/s (fp32 input read in place, output once), also at batch 256.
+    * YOLOv8m-640 random-init, TF32 tcgen05 convs, 64 images per GPU:
+      images/s (inference, device-timed), conv TFLOP/s and the per-layer roofline
+      fraction against the TF32 peak (half the measured BF16 sustained figure)."""
+    import numpy as np
+    import torch
+
+    import pdefa_b200 as pb
+    from pdefa_b200 import _native as N
+    from pdefa_b200.engine_file import write_engine
+    from pdefa_b200.yolo import build_single_conv, build_yolov8, conv_flops
+
+    hbm, _, peak_sus, src = load_peaks()
+    L = N.lib()
+    res = {}
+    # ---- configs[0]
+    rng = np.random.default_rng(42)
+    A = rng.standard_normal((512, 512), dtype=np.float32)
+    Bm = rng.standard_normal((512, 512), dtype=np.float32)
+    ta, tb = pb.Tensor.from_numpy(A), pb.Tensor.from_numpy(Bm)
+    ref = A.astype(np.float64) @ Bm.astype(np.float64)
+    flop = 2.0 * 512 ** 3
+    da = torch.from_numpy(A).cuda()
+    db = torch.from_numpy(Bm).cuda()
+    dc = torch.empty((512, 512), device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    mm = {}
+    for name, prec in (("fp32", pb.FP32), ("tf32", pb.TF32), ("bf16", pb.BF16)):
+        tc = pb.tensor_empty([512, 512])
+        for _ in range(5):
+            pb.ops_matmul(ta, tb, tc, precision=prec)
+        ts = []
+        for _ in range(30):
+            t0 = time.perf_counter()
+            pb.ops_matmul(ta, tb, tc, precision=prec)
+            ts.append(time.perf_counter() - t0)
+        ts.sort()
+        call_ms = ts[len(ts) // 2] * 1e3
+        err = float(np.abs(tc.to_numpy() - ref).max() / np.abs(ref).max())
+        for _ in range(10):
+            L.engine_gemm_f32_device(da.data_ptr(), db.data_ptr(), dc.data_ptr(), 512, 512, 512, prec, stream)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(200):
+            L.engine_gemm_f32_device(da.data_ptr(), db.data_ptr(), dc.data_ptr(), 512, 512, 512, prec, stream)
+        e1.record()
+        torch.cuda.synchronize()
+        dev_ms = e0.elapsed_time(e1) / 200
+        mm[name] = {"call_ms": round(call_ms, 4), "call_gflops": round(flop / call_ms / 1e6, 1),
+                    "device_ms": round(dev_ms, 5), "device_tflops": round(flop / dev_ms / 1e9, 2),
+                    "normwise_err_vs_f64": err}
+    res["configs[0]_ops_matmul_512"] = {
+        "api": "engine_ops_matmul_ex, host tensors (H2D of A and B, GEMM, D2H of C inside each call)", **mm}
+    # ---- configs[1]
+    g, _ = build_single_conv(cin=3, cout=16, k=3, s=2, hw=640, act=True, seed=1)
+    path = os.path.join(tempfile.mkdtemp(), "stem.engine")
+    write_engine(path, g)
+    stem = {}
+    for name, prec, batch in (("fp32_b1", pb.FP32, 1), ("bf16_b1", pb.BF16, 1), ("bf16_b256", pb.BF16, 256)):
+        ctx = pb.Context(precision=prec, device=local)
+        model = pb.Model(ctx, path)
+        sess = pb.Session(ctx, model)
+        x = torch.rand((batch, 3, 640, 640), device="cuda", generator=torch.Generator(device="cuda").manual_seed(0))
+        for _ in range(3):
+            sess.run_device(x.data_ptr(), batch, None, stream)
+        torch.cuda.synchronize()
+        summary = model.plan_summary(prec, batch)
+        reps = 50 if batch == 1 else 5
+        sess.set_step_timing(batch, True)
+        for _ in range(reps):
+            sess.run_device(x.data_ptr(), batch, None, stream)
+        torch.cuda.synchronize()
+        t = sess.step_times(batch)
+        sess.set_step_timing(batch, False)
+        i = next(j for j, (kd, _) in enumerate(summary) if kd.startswith("conv"))
+        ms = t[i] / reps
+        nbytes = (4 * 3 * 640 * 640 + (4 if prec == pb.FP32 else 2) * 16 * 320 * 320) * batch
+        stem[name] = {"kernel": summary[i][0], "ms": round(ms, 5), "gbs": round(nbytes / ms / 1e6, 1),
+                      "hbm_frac": round(nbytes / ms / 1e6 / hbm, 3)}
+    res["configs[1]_stem_conv"] = {"bytes": "fp32 input read once + output written once", **stem}
+    # ---- configs[4]
+    B = 64
+    g, info = build_yolov8("m", imgsz=640, seed=0)
+    path = os.path.join(tempfile.mkdtemp(), "y8m.engine")
+    write_engine(path, g)
+    ctx = pb.Context(precision=pb.TF32, device=local)
+    model = pb.Model(ctx, path)
+    sess = pb.Session(ctx, model)
+    x = torch.rand((B, 3, 640, 640), device="cuda", generator=torch.Generator(device="cuda").manual_seed(4))
+    for _ in range(3):
+        sess.run_device(x.data_ptr(), B, None, stream)
+    torch.cuda.synchronize()
+    summary = model.plan_summary(pb.TF32, B)
+    steps = 5
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        sess.run_device(x.data_ptr(), B, None, stream)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    sess.set_step_timing(B, True)
+    for _ in range(steps):
+        sess.run_device(x.data_ptr(), B, None, stream)
+    torch.cuda.synchronize()
+    step_ms = sess.step_times(B)
+    sess.set_step_timing(B, False)
+    peak_tf32 = peak_sus / 2
+    bound, meas = per_layer_roofline(summary, step_ms, steps, info, B, peak_tf32, hbm, 4)
+    conv_ms = sum(step_ms[i] for i, (kd, _) in enumerate(summary) if kd.startswith("conv")) / steps
+    flops = conv_flops(info) * B
+    res["configs[4]_yolov8m_tf32_b64"] = {
+        "images_per_s": round(B / ms * 1e3, 1), "ms_per_step": round(ms, 3), "conv_ms": round(conv_ms, 3),
+        "conv_tflops": round(flops / conv_ms / 1e9, 1), "conv_frac_of_tf32_peak": round(flops / conv_ms / 1e9 / peak_tf32, 3),
+        "conv_per_layer_roofline_frac": round(bound / meas, 3) if meas else None,
+        "peak": f"{src} bf16 sustained / 2 = {peak_tf32:.1f} TFLOP/s", "step": "inference only (no decode)"}
+    return res
+
+
 def config(args, world):
     name = {"yolov8n": "configs[3]: YOLOv8n", "yolov8m": "configs[4]: YOLOv8m", "yolo11n": "YOLO11n"}[args.model]
     return {"workload": f"{name}-{args.imgsz} random-init, {args.precision.upper()} tcgen05 convs + GPU decode/NMS "
@@ -261,6 +449,7 @@ def main():
     ap.add_argument("--cpu-images", type=int, default=48, help="images in the bounded CPU baseline sample")
     ap.add_argument("--ref-images", type=int, default=4, help="images per step of the reference arm")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-configs", action="store_true", help="skip the configs[0]/[1]/[4] records")
     ap.add_argument("--layers", action="store_true", help="print per-launch milliseconds to stderr")
     ap.add_argument("--layer", default="", help="CIN,COUT,K,S,HW: time one conv layer (Conv-BN-SiLU) instead")
     ap.add_argument("--sweep-layers", action="store_true", help="time every distinct YOLOv8n-640 conv shape")
@@ -375,23 +564,13 @@ def main():
     # HBM bandwidth), bytes = activations in (fp32 for the stem's graph input, bf16
     # otherwise) + out (bf16) once; the fraction is the sum of the bounds over the
     # sum of the measured conv times
-    layer_of = {name: (cin, cout, k, s, h, w) for name, cin, cout, k, s, h, w in info["convs"]}
-    ideal_ms = meas_ms = 0.0
-    for i, (kd, name) in enumerate(summary):
-        key = name.strip("/").replace("/conv/Conv", "")
-        if not kd.startswith("conv") or key not in layer_of:
-            continue
-        cin, cout, k, s, h, w = layer_of[key]
-        ho, wo = (h + 2 * (k // 2) - k) // s + 1, (w + 2 * (k // 2) - k) // s + 1
-        fl = 2.0 * cin * cout * k * k * ho * wo * B
-        by = ((4 if kd.startswith("conv_stem") or kd == "conv_direct" else abytes) * cin * h * w
-              + abytes * cout * ho * wo) * B
-        ideal_ms += max(fl / (peak_sus * 1e12), by / (hbm * 1e9)) * 1e3
-        meas_ms += step_ms[i] / args.steps
+    ideal_ms, meas_ms = per_layer_roofline(summary, step_ms, args.steps, info, B, peak_sus, hbm, abytes)
+    yolov8n640 = args.imgsz == 640 and args.model == "yolov8n" and args.precision == "bf16"
     roofline = {"bound": "tensor", "achieved": achieved, "peak": peak_sus, "unit": "TFLOP/s",
                 "frac": (achieved / peak_sus) if achieved else None,
-                "traffic": conv_tc_traffic_per_launch(B) if args.imgsz == 640 and args.model == "yolov8n" else None,
-                "traffic_unit": "DRAM bytes per conv_tc launch (ncu, averaged over the 62 launches of a step)",
+                "traffic": CONV_TC_DRAM_BYTES_PER_IMAGE_B32 * B / 62 if yolov8n640 else None,
+                "traffic_unit": "DRAM bytes per conv_tc launch, averaged over the 62 launches of a step: "
+                                "ncu capture of a batch-32 step scaled to this batch by images (a lower bound)",
                 "kernel": f"conv_tc_{args.precision} ({sum(1 for k, _ in summary if k.startswith('conv_tc'))} launches/step)",
                 "peak_source": f"{peak_src} bf16 sustained" + (" / 2 (tf32)" if args.precision == "tf32" else ""),
                 "conv_tflops_all_convs": flops_img * B / (conv_ms_all / 1e3) / 1e12 if conv_ms_all else None,
@@ -456,6 +635,31 @@ def main():
     e2e_f32_value = timed(lambda: bi.detect_arrays(xnp, conf_thres=0.25, iou_thres=0.45, max_det=max_det))
     bi.close()
 
+    # Host->device ceiling: every rank copies its pinned 8-bit frames to its GPU at the
+    # same time (CUDA events around 5 copies), against the H2D rate the e2e leg needed
+    dst = torch.empty(u8.shape, dtype=torch.uint8, device="cuda")
+    dst.copy_(u8, non_blocking=True)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    h0, h1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    h0.record()
+    for _ in range(5):
+        dst.copy_(u8, non_blocking=True)
+    h1.record()
+    torch.cuda.synchronize()
+    h2d_ms = h0.elapsed_time(h1) / 5
+    h2d_ms_max, h2d_bytes = reduce_job(h2d_ms, u8.numel(), device=torch.device("cuda", local))
+    del dst
+    h2d = {"ceiling_gbs_per_gpu": u8.numel() / h2d_ms / 1e6,
+           "ceiling_gbs_total": h2d_bytes / h2d_ms_max / 1e6,
+           "e2e_gbs_total": e2e_value * (u8.numel() / B) / 1e9,
+           "how": "pinned 8-bit frames of one step copied to the GPU on all ranks at once, CUDA events"}
+
+    configs = None
+    if rank == 0 and world == 1 and not args.no_configs:
+        configs = measure_configs(args, local)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
@@ -463,8 +667,11 @@ def main():
         if stepf is not None:
             secs = stepf(args.cpu_images)
             cpu = {"value": args.cpu_images / secs, "unit": "images/s", "cores": threads, "kind": "reference",
+                   "cpu": cpu_model(),
                    "sample": f"{args.cpu_images} images: reference engine (oracle/_ref) batch-1 Session.run "
-                             f"+ restated reference decode/NMS (oracle/decode_ref.py)"}
+                             f"+ restated reference decode/NMS (oracle/decode_ref.py, numpy argmax: a little "
+                             f"faster than the reference's pure-Python decode, so the baseline is if anything "
+                             f"overstated)"}
 
     if world > 1:
         dist.destroy_process_group()
@@ -483,9 +690,11 @@ def main():
                     "sync_value": e2e_sync_value,
                     "sync_api": "BatchInference.detect_u8 (pdefa_batch_run_u8), one blocking call per step",
                     "f32_input": {"value": e2e_f32_value, "h2d_bytes_per_step": xh.numel() * 4,
-                                  "api": "BatchInference.detect_arrays (pdefa_batch_run), pinned float32 NCHW"}},
+                                  "api": "BatchInference.detect_arrays (pdefa_batch_run), pinned float32 NCHW"},
+                    "h2d": h2d},
             "roofline": roofline, "cpu_baseline": cpu,
             "conv_gflop_per_image": flops_img / 1e9,
+            "configs": configs,
         }))
 
 
