@@ -34,8 +34,15 @@ ENGINE_API EngineStatus engine_context_set_device(EngineContext* ctx, int32_t de
 ENGINE_API int32_t      engine_context_get_device(const EngineContext* ctx);
 /* Number of visible CUDA devices (0 without a GPU). */
 ENGINE_API int32_t      engine_device_count(void);
-/* Sticky device-side error word set by bounded waits that timed out (0 = none). */
+/* Device-wide error word of the kernels that run outside a session's plan (GPU
+ * decode, engine_gemm_f32_device): set by bounded waits that timed out (0 = none),
+ * cleared when read. Plans have their own word (engine_session_device_error). */
 ENGINE_API int32_t      engine_device_error(int32_t device);
+/* Error code the kernels of `sess`'s plan for `batch` recorded in their last
+ * engine_session_run_device call (0: none; a bounded wait that ran out), read once the
+ * caller has synchronized that call's stream; the code is cleared when read. Each plan
+ * has its own word, so one session's timeout never affects another's kernels. */
+ENGINE_API int32_t      engine_session_device_error(EngineSession* sess, int64_t batch);
 
 /* Run a session on device buffers already resident on the session's GPU.
  * d_input: [batch, C, H, W] fp32 NCHW; d_output: graph output 0 for `batch` images

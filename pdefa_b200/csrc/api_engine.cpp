@@ -141,11 +141,12 @@ void EngineSession::run() {
         }
         cudaEventDestroy(a);
         cudaEventDestroy(b);
+        p.enqueue_error_copy(stream);
     } else {
         p.run(stream);
     }
     PB_CUDA(cudaStreamSynchronize(stream));
-    const int derr = read_device_error(device);
+    const int derr = p.take_error();
     if (derr) fail(ENGINE_ERR_RUNTIME, "device-side wait timed out (code " + std::to_string(derr) + ")");
     last = &p;
     outputs.resize(p.num_outputs());

@@ -67,6 +67,7 @@ struct PdefaBatchRunner {
         int32_t dst_max_det = 0;
         void* pixels = nullptr;      // device copy of an 8-bit micro-batch (pdefa_batch_run_u8)
         size_t pixels_cap = 0;
+        Plan* plan = nullptr;        // plan of the pending micro-batch (its error word)
     };
     struct Replica {
         int device = 0;
@@ -108,6 +109,10 @@ void retire_lane(PdefaBatchRunner::Lane& l) {
     if (!l.busy) return;
     l.busy = false;
     PB_CUDA(cudaEventSynchronize(l.done));
+    if (l.plan) {
+        const int e = l.plan->take_error();
+        if (e) fail(ENGINE_ERR_RUNTIME, "device-side wait timed out (code " + std::to_string(e) + ")");
+    }
     std::memcpy(l.dst_counts + l.c0, l.h_counts, (size_t)l.nb * 4);
     if (l.dst_max_det > 0)
         std::memcpy(l.dst_dets + l.c0 * l.dst_max_det, l.h_dets, (size_t)l.nb * l.dst_max_det * sizeof(PdefaDetection));
@@ -138,6 +143,15 @@ ENGINE_API int32_t engine_context_get_device(const EngineContext* ctx) {
 ENGINE_API int32_t engine_device_count(void) { return pb::device_count(); }
 ENGINE_API int32_t engine_device_error(int32_t device) {
     try { return read_device_error(device); } catch (...) { return -1; }
+}
+ENGINE_API int32_t engine_session_device_error(EngineSession* sess, int64_t batch) {
+    if (!sess || sess->magic != kMagicSession) return -1;
+    try {
+        std::lock_guard<std::mutex> lk(sess->mu);
+        return sess->plan_for(batch).take_error();
+    } catch (...) {
+        return -1;
+    }
 }
 
 ENGINE_API EngineStatus engine_session_run_device(EngineSession* sess, const float* d_input, int64_t batch,
@@ -542,6 +556,7 @@ EngineStatus run_batch(PdefaBatchRunner* r, const BatchInput& in, int64_t n_imag
                                                     cudaMemcpyDeviceToHost, rp.post));
                         PB_CUDA(cudaEventRecord(l.done, rp.post));
                         l.busy = true;
+                        l.plan = &p;
                         l.c0 = c0;
                         l.nb = nb;
                         l.ticket = ticket;

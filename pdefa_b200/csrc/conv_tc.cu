@@ -92,6 +92,7 @@ struct TcParams {
     int tma_store;                        // 1: stage output chunks in shared memory, TMA-store them
     uint32_t staging_bytes;               // bn * 128 * out element size (0 without tma_store)
     int* err;
+    long long wait_limit;                 // SM cycles a bounded wait on a pipeline barrier may take
 };
 
 __device__ __forceinline__ uint64_t make_smem_desc(uint32_t addr, int swb) {
@@ -403,7 +404,7 @@ __device__ void epilogue_loop(const TcParams& p, const CUtensorMap* tmOut, uint8
         }
         uint4 rn[4] = {};
         if (p.res && live && grp < nchunks) load_res_chunk(p, rb + 16 * grp, rn);
-        bool ok = mbar_wait_bounded(&tfull[buf], use & 1u);
+        bool ok = mbar_wait_bounded(&tfull[buf], use & 1u, p.wait_limit);
         ok = __all_sync(0xffffffffu, ok);
         if (p.tma_store) {
             // One decision for the whole group (its warps meet at named barriers, so
@@ -480,13 +481,13 @@ __device__ __forceinline__ void mma_issuer(const TcParams& p, const MmaSmem& m, 
     const uint64_t bdesc0 = make_smem_desc(m.bres, p.swb);
     const uint32_t bstep = (p.btile_bytes >> 4);          // descriptor units per resident k-block
     int64_t it = 0, hit = 0, i = 0;
-    if (BRES && blockIdx.x < total && !mbar_wait_bounded(m.bres_full, 0)) {
+    if (BRES && blockIdx.x < total && !mbar_wait_bounded(m.bres_full, 0, p.wait_limit)) {
         atomicExch(p.err, 2);
         *abort_flag = 1;
     }
     for (int64_t t = blockIdx.x; t < total && !*abort_flag; t += gridDim.x, ++i) {
         const int buf = (int)(i % p.nbuf);
-        if (i >= p.nbuf && !mbar_wait_bounded(&m.tempty[buf], (uint32_t)(((i / p.nbuf) & 1) ^ 1))) {
+        if (i >= p.nbuf && !mbar_wait_bounded(&m.tempty[buf], (uint32_t)(((i / p.nbuf) & 1) ^ 1), p.wait_limit)) {
             atomicExch(p.err, 5);
             *abort_flag = 1;
             break;
@@ -501,7 +502,7 @@ __device__ __forceinline__ void mma_issuer(const TcParams& p, const MmaSmem& m, 
             const uint32_t off0 = P0 - fdiv(P0, p.div_wp) * p.div_wp.d;
             for (int cc = 0; cc < chunks && ok; ++cc) {
                 const int hs = (int)(hit % m.HS);
-                if (!mbar_wait_bounded(&m.hfull[hs], (uint32_t)((hit / m.HS) & 1))) { ok = false; break; }
+                if (!mbar_wait_bounded(&m.hfull[hs], (uint32_t)((hit / m.HS) & 1), p.wait_limit)) { ok = false; break; }
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 const uint64_t adesc0 = make_smem_desc(m.halo + (uint32_t)hs * p.halo_bytes + off0 * (uint32_t)p.swb, p.swb);
                 for (int r = 0, tap = 0; r < p.taps / kw; ++r) {
@@ -513,7 +514,7 @@ __device__ __forceinline__ void mma_issuer(const TcParams& p, const MmaSmem& m, 
                             db = bdesc0 + (uint64_t)(cc * taps + tap) * bstep;
                         } else {
                             const int st = (int)(it % m.S);
-                            if (!mbar_wait_bounded(&m.full[st], (uint32_t)((it / m.S) & 1))) { ok = false; break; }
+                            if (!mbar_wait_bounded(&m.full[st], (uint32_t)((it / m.S) & 1), p.wait_limit)) { ok = false; break; }
                             ++it;
                             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                             db = make_smem_desc(m.ring + (uint32_t)m.S * m.a_bytes + (uint32_t)st * m.b_bytes, p.swb);
@@ -531,7 +532,7 @@ __device__ __forceinline__ void mma_issuer(const TcParams& p, const MmaSmem& m, 
             for (int tap = 0; tap < taps && ok; ++tap) {
                 for (int cc = 0; cc < chunks; ++cc) {
                     const int st = (int)(it % m.S);
-                    if (!mbar_wait_bounded(&m.full[st], (uint32_t)((it / m.S) & 1))) { ok = false; break; }
+                    if (!mbar_wait_bounded(&m.full[st], (uint32_t)((it / m.S) & 1), p.wait_limit)) { ok = false; break; }
                     ++it;
                     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                     const uint64_t da = make_smem_desc(m.ring + (uint32_t)st * m.a_bytes, p.swb);
@@ -652,7 +653,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                         cc = kb / p.taps; tap = kb - cc * p.taps;
                         if (tap == 0) {
                             const int hs = (int)(hit % HS);
-                            if (hit >= HS && !mbar_wait_bounded(&hempty[hs], (uint32_t)(((hit / HS) & 1) ^ 1))) {
+                            if (hit >= HS && !mbar_wait_bounded(&hempty[hs], (uint32_t)(((hit / HS) & 1) ^ 1), p.wait_limit)) {
                                 atomicExch(p.err, 7);
                                 *abort_flag = 1;
                                 stop = true;
@@ -668,7 +669,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     }
                     if (!ring_used) continue;
                     const int st = (int)(it % S);
-                    if (it >= S && !mbar_wait_bounded(&empty[st], (uint32_t)(((it / S) & 1) ^ 1))) {
+                    if (it >= S && !mbar_wait_bounded(&empty[st], (uint32_t)(((it / S) & 1) ^ 1), p.wait_limit)) {
                         atomicExch(p.err, 1);
                         *abort_flag = 1;
                         break;
@@ -976,6 +977,9 @@ void launch_conv_tc(const ConvArgs& a, int op_dt, int* err, cudaStream_t s) {
     p.res_img = a.res.img_stride; p.res_sh = a.res.stride[1]; p.res_sw = a.res.stride[2];
     p.bias = a.bias; p.act = a.act; p.slope = a.slope; p.cout = a.cout;
     p.err = err;
+    // Pipeline waits give up after wait_limit cycles (~0.5 s by default); the drains
+    // before exit always use the default, so no copy or MMA is left in flight.
+    p.wait_limit = a.wait_limit > 0 ? a.wait_limit : 1000000000LL;
 
     CUtensorMap tmA, tmB, tmOut;
     std::memset(&tmOut, 0, sizeof(tmOut));

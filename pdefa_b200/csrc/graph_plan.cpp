@@ -1497,7 +1497,8 @@ struct PlanBuilder {
                 if (!P.dry_) PB_CUDA(cudaMemcpy(d, h.data(), h.size() * 4, cudaMemcpyHostToDevice));
             }
             a.weight = d;
-            int* err = P.dry_ ? nullptr : device_error_word(P.device_);
+            int* err = P.err_;
+            a.wait_limit = P.wait_limit_;
             kind(op_dt == BF16 ? "conv_tc_bf16" : "conv_tc_tf32");
             add_step(n.name, [a, op_dt, err](cudaStream_t s) { launch_conv_tc(a, op_dt, err, s); });
         } else {
@@ -1513,7 +1514,7 @@ struct PlanBuilder {
             if (!P.dry_) PB_CUDA(cudaMemcpy(d, h.data(), h.size() * 4, cudaMemcpyHostToDevice));
             a.weight = d;
             if (prec == PREC_BF16 && conv_stem_tc_supported(a)) {
-                int* err = P.dry_ ? nullptr : device_error_word(P.device_);
+                int* err = P.err_;
                 kind("conv_stem_tc");
                 add_step(n.name, [a, ext, pp, err](cudaStream_t s) mutable {
                     if (ext && pp->cur_in_) a.in.ptr = pp->cur_in_;
@@ -1683,7 +1684,19 @@ Plan::~Plan() {
     for (auto e : ev_pool_) cudaEventDestroy(e);
     if (gexec_) cudaGraphExecDestroy(gexec_);
     for (void* p : allocs_) cudaFree(p);
+    if (err_host_) cudaFreeHost(err_host_);
     cudaSetDevice(prev);
+}
+
+int Plan::take_error() {
+    if (dry_ || !err_host_) return 0;
+    const int v = *reinterpret_cast<volatile int*>(err_host_);
+    if (v) {
+        PB_CUDA(cudaSetDevice(device_));
+        PB_CUDA(cudaMemset(err_, 0, sizeof(int)));
+        *err_host_ = 0;
+    }
+    return v;
 }
 
 void* Plan::alloc(size_t bytes) {
@@ -1745,6 +1758,13 @@ std::vector<size_t> pack_arena(const std::vector<size_t>& bytes, const std::vect
 }
 
 void Plan::build() {
+    if (!dry_) {
+        if (const char* w = std::getenv("PDEFA_WAIT_LIMIT_CYCLES")) wait_limit_ = std::atoll(w);
+        err_ = static_cast<int*>(alloc(sizeof(int)));
+        PB_CUDA(cudaMemset(err_, 0, sizeof(int)));
+        PB_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&err_host_), sizeof(int), cudaHostAllocDefault));
+        *err_host_ = 0;
+    }
     if (dry_ || std::getenv("PDEFA_NO_ARENA") != nullptr) {
         PlanBuilder b(*this, *g_);
         b.build();
@@ -1782,6 +1802,16 @@ void Plan::run_steps(cudaStream_t s) {
 
 void Plan::run(cudaStream_t s, const float* in_override, float* out_override) {
     (void)out_override;
+    run_launches(s, in_override);
+    enqueue_error_copy(s);
+}
+
+void Plan::enqueue_error_copy(cudaStream_t s) {
+    // the plan's error word reaches the host with the stream's other results
+    if (err_host_) PB_CUDA(cudaMemcpyAsync(err_host_, err_, sizeof(int), cudaMemcpyDeviceToHost, s));
+}
+
+void Plan::run_launches(cudaStream_t s, const float* in_override) {
     cur_in_ = in_override;
     struct Reset { const float*& p; ~Reset() { p = nullptr; } } reset{cur_in_};
     // Eager: timed runs, the legacy default stream (cannot be captured), the first run.

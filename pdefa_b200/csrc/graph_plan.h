@@ -84,6 +84,12 @@ public:
     void set_step_timing(bool on) { timing_ = on; }
     std::vector<double> collect_step_ms();
     int64_t batch() const { return batch_; }
+    // After the stream of the last run() was synchronized: the error code its kernels
+    // recorded (0: none); the word is cleared, so the next run starts clean.
+    int take_error();
+    // Enqueues the copy of the error word to the host (Plan::run does it after its
+    // launches; callers that launch the steps themselves call it).
+    void enqueue_error_copy(cudaStream_t s);
     // Device bytes of the activations: packed in the arena, and what one buffer per
     // value would take.
     size_t activation_bytes() const { return activation_bytes_; }
@@ -133,6 +139,7 @@ private:
     cudaGraphExec_t gexec_ = nullptr;
     const float* g_in_ = nullptr;
     void run_steps(cudaStream_t s);
+    void run_launches(cudaStream_t s, const float* in_override);
     std::vector<cudaEvent_t> ev_pool_;
     std::vector<std::pair<int, std::pair<cudaEvent_t, cudaEvent_t>>> pending_;
     std::vector<double> step_ms_;
@@ -144,6 +151,12 @@ private:
     std::vector<size_t> root_bytes_;
     std::vector<int> root_first_, root_last_;
     size_t activation_bytes_ = 0, unpacked_bytes_ = 0;
+    // Error word of this plan's kernels (a bounded wait that ran out records a code and
+    // the plan's later CTAs skip their work), copied to pinned host memory at the end
+    // of every run, so one plan's timeout never blanks another plan's work.
+    int* err_ = nullptr;
+    int* err_host_ = nullptr;
+    long long wait_limit_ = 0;   // PDEFA_WAIT_LIMIT_CYCLES at lowering (0: kernel default)
     friend struct PlanBuilder;
 };
 

@@ -77,6 +77,7 @@ struct ConvArgs {
     int act = ACT_NONE;
     float slope = 0.01f;
     int64_t batch = 1;
+    long long wait_limit = 0;   // tcgen05 kernels: bounded-wait limit in SM cycles (0: default)
 };
 // Strict fp32 SIMT implicit GEMM. weight: fp32 [kh][kw][cin][cout].
 void launch_conv_simt(const ConvArgs& a, cudaStream_t s);

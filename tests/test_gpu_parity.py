@@ -177,6 +177,27 @@ def test_single_conv_staged_input(engine_dir, prec, cin, cout, k, s, hw):
         assert normwise(y, ref) <= TOL[prec]
 
 
+def check_head(y, ref, prec, ref64=None):
+    """[B, 4+nc, A] head outputs, channel groups checked apart: the box channels
+    (pixels, up to the image size) normwise over the boxes, the class scores (in [0, 1])
+    absolutely, so loose boxes cannot hide behind the scores or the other way round.
+    BF16/TF32: both against the compiled reference at 1e-2. FP32: boxes against it at
+    1e-5; the scores at 1e-5 against ref64, the float64 restatement of the same graph
+    semantics (oracle/onnx_numpy.py), and at 1e-2 against the compiled reference, whose
+    Winograd SiLU flavour is discontinuous at the points where its rounded exponent
+    changes: its own float rounding puts single activations on the other side of such a
+    jump (on YOLOv8n-640 seed 1: one 3x3 block of anchors, 1.7e-3 on one score, while
+    the boxes agree to 2e-7)."""
+    tol = TOL[prec]
+    bx, rb = y[..., :4, :], ref[..., :4, :]
+    assert normwise(bx, rb) <= tol, ("boxes", normwise(bx, rb))
+    err = float(np.abs(y[..., 4:, :] - ref[..., 4:, :]).max())
+    assert err <= max(tol, 1e-2), ("class scores", err)
+    if ref64 is not None:
+        err64 = float(np.abs(y[..., 4:, :] - ref64[..., 4:, :]).max())
+        assert err64 <= tol, ("class scores vs float64", err64)
+
+
 # ---------------------------------------------------------------- YOLOv8n (cfg3/cfg4 numerics)
 @pytest.mark.parametrize("prec", PRECS)
 def test_yolov8n_128_golden(golden, y8n_128, prec):
@@ -218,6 +239,12 @@ def test_yolov8n_640_against_reference_engine(y8n_640, prec):
     ref = R.RefSession(y8n_640).run(x)
     y = run_engine(y8n_640, x, prec)
     assert normwise(y, ref) <= TOL[prec]
+    ref64 = None
+    if prec == pb.FP32:
+        from oracle import onnx_numpy
+        g, _ = build_yolov8("n", imgsz=640, seed=0)
+        ref64 = np.asarray(onnx_numpy.run(g, [x.astype(np.float64)])[0], dtype=np.float64)
+    check_head(y, ref, prec, ref64)
 
 
 @pytest.mark.parametrize("prec", [pb.TF32, pb.BF16])
@@ -233,7 +260,9 @@ def test_yolov8m_640_against_reference_engine(engine_dir, prec):
     y = run_engine(p, x, prec)
     sess = R.RefSession(p)
     for i in range(2):
-        assert normwise(y[i], sess.run(x[i:i + 1])[0]) <= TOL[prec]
+        ref = sess.run(x[i:i + 1])[0]
+        assert normwise(y[i], ref) <= TOL[prec]
+        check_head(y[i], ref, prec)
 
 
 def test_tiny_classifier_graph(golden, engine_dir):
