@@ -116,6 +116,22 @@ class RefSession:
         finally:
             L.engine_tensor_destroy(t)
 
+    def run_all(self, x: np.ndarray, n_outputs: int):
+        """Outputs 0..n_outputs-1 of one batch-1 run (float32 outputs only)."""
+        L = lib()
+        t = _tensor_from(x)
+        try:
+            _check(L.engine_session_set_input(self.sess, 0, t), "set_input")
+            _check(L.engine_session_run(self.sess), "session_run")
+            res = []
+            for i in range(n_outputs):
+                out = vp()
+                _check(L.engine_session_get_output(self.sess, i, ctypes.byref(out)), "get_output")
+                res.append(_to_numpy(out))
+            return res
+        finally:
+            L.engine_tensor_destroy(t)
+
     def run_batch(self, xs: np.ndarray) -> np.ndarray:
         """Image-by-image, as the reference's BatchInference does (batch.py:45-60)."""
         return np.stack([self.run(xs[i:i + 1])[0] for i in range(xs.shape[0])])

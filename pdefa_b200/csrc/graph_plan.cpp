@@ -405,6 +405,40 @@ struct PlanBuilder {
             set_out(n, 0, s, F32, ni);
             return;
         }
+        case Op::TopK: {
+            // session_ops_math.inc:321-391: the axis indexes the tensor as stored (no
+            // NHWC remap), k comes from the second input, k <= 0 or > the axis: all
+            need(2);
+            const auto s = V[input_vid(n, 0)].shape;
+            int64_t ax = n.params.axis < 0 ? n.params.axis + (int64_t)s.size() : n.params.axis;
+            if (ax < 0 || ax >= (int64_t)s.size()) fail(ENGINE_ERR_INVALID_SHAPE, "TopK '" + n.name + "': axis");
+            std::vector<double> kv;
+            if (!weight_values(n.inputs[1], kv) || kv.empty())
+                fail(ENGINE_ERR_NOT_IMPL, "TopK '" + n.name + "': k computed at run time is not supported");
+            int64_t k = (int64_t)kv[0];
+            if (k <= 0 || k > s[ax]) k = s[ax];
+            auto os = s;
+            os[ax] = k;
+            nt.mode = (int)ax;
+            nt.a = {k};
+            set_out(n, 0, os, F32, ni);
+            if (n.outputs.size() > 1 && n.outputs[1] >= 0) set_out(n, 1, os, F32, ni);   // positions as exact floats
+            return;
+        }
+        case Op::GatherElements: {
+            // session_ops_math.inc:393-433: output shaped like the indices
+            need(2);
+            const auto ds = V[input_vid(n, 0)].shape, is = V[input_vid(n, 1)].shape;
+            int64_t ax = n.params.axis < 0 ? n.params.axis + (int64_t)ds.size() : n.params.axis;
+            if (ax < 0 || ax >= (int64_t)ds.size() || is.size() != ds.size())
+                fail(ENGINE_ERR_INVALID_SHAPE, "GatherElements '" + n.name + "': axis or rank");
+            for (size_t d = 0; d < ds.size(); ++d)
+                if ((int64_t)d != ax && is[d] != ds[d])
+                    fail(ENGINE_ERR_NOT_IMPL, "GatherElements '" + n.name + "': indices must match the data off the axis");
+            nt.mode = (int)ax;
+            set_out(n, 0, is, F32, ni);
+            return;
+        }
         default:
             fail(ENGINE_ERR_NOT_IMPL, std::string("op ") + op_name(n.op) + " (id " + std::to_string((int)n.op) +
                                           ") in node '" + n.name + "' is not supported by this build");
@@ -1250,6 +1284,44 @@ struct PlanBuilder {
             float* op = static_cast<float*>(const_cast<void*>(out.ptr));
             kind("softmax");
             add_step(n.name, [=](cudaStream_t st) { launch_softmax(ip, op, outer, axl, inner, per, b, st); });
+            return;
+        }
+        case Op::TopK: {
+            const int x = input_vid(n, 0);
+            TView in = dense_f32(x, n.name);
+            const auto s = V[x].shape;
+            const int ax = nt.mode;
+            const int64_t k = nt.a[0];
+            int64_t outer = B, inner = 1;        // images are consecutive slices of dense values
+            for (int d = 0; d < ax; ++d) outer *= s[d];
+            for (size_t d = ax + 1; d < s.size(); ++d) inner *= s[d];
+            const int64_t L = s[ax];
+            TView vo = view(vid[n.outputs[0]]);
+            float* ip_out = nullptr;
+            if (n.outputs.size() > 1 && n.outputs[1] >= 0 && vid.count(n.outputs[1]))
+                ip_out = static_cast<float*>(const_cast<void*>(view(vid[n.outputs[1]]).ptr));
+            const float* ip = static_cast<const float*>(in.ptr);
+            float* vp = static_cast<float*>(const_cast<void*>(vo.ptr));
+            kind("topk");
+            add_step(n.name, [=](cudaStream_t st) { launch_topk(ip, vp, ip_out, outer, L, inner, k, st); });
+            return;
+        }
+        case Op::GatherElements: {
+            const int x = input_vid(n, 0), ix = input_vid(n, 1);
+            TView data = dense_f32(x, n.name + "/data");
+            TView idx = dense_f32(ix, n.name + "/indices");
+            const auto ds = V[x].shape, is = V[ix].shape;
+            const int ax = nt.mode;
+            int64_t outer = B, inner = 1;
+            for (int d = 0; d < ax; ++d) outer *= ds[d];
+            for (size_t d = ax + 1; d < ds.size(); ++d) inner *= ds[d];
+            const int64_t L = ds[ax], K = is[ax];
+            TView out = view(vid[n.outputs[0]]);
+            const float* dp = static_cast<const float*>(data.ptr);
+            const float* xp = static_cast<const float*>(idx.ptr);
+            float* op = static_cast<float*>(const_cast<void*>(out.ptr));
+            kind("gather_elements");
+            add_step(n.name, [=](cudaStream_t st) { launch_gather_elements(dp, xp, op, outer, K, L, inner, st); });
             return;
         }
         default:

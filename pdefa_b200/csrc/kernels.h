@@ -168,6 +168,16 @@ LetterboxGeom letterbox_geometry(int src_w, int src_h, int W, int H, float scale
 void launch_letterbox_u8(const uint8_t* d_src, int64_t n, int channels, const LetterboxGeom& g, float* d_out,
                          cudaStream_t s);
 
+// TopK along the middle axis of [outer, L, inner] (dense fp32): the k largest values,
+// descending, equal values lowest position first; positions written as exact floats
+// (indices may be null). GatherElements: out[o, a, i] = data[o, idx[o, a, i], i]
+// for idx [outer, K, inner], data [outer, L, inner] (negative counted from the end,
+// out of range -> 0).
+void launch_topk(const float* in, float* values, float* indices, int64_t outer, int64_t L, int64_t inner, int64_t k,
+                 cudaStream_t s);
+void launch_gather_elements(const float* data, const float* idx, float* out, int64_t outer, int64_t K, int64_t L,
+                            int64_t inner, cudaStream_t s);
+
 // GEMM on device pointers (engine_gemm_f32_device, engine_ops_matmul): strict FP32
 // SIMT, or tcgen05 with operands staged in `scratch` (gemm_device_scratch_bytes).
 size_t gemm_device_scratch_bytes(int64_t m, int64_t n, int64_t k, int precision);
