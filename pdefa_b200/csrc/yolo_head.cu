@@ -85,6 +85,23 @@ __device__ __forceinline__ void unpack8(uint4 q, float* f) {
     }
 }
 
+// BF16 plans (bf16 logits, results held to 1e-2) evaluate the exponentials with the
+// hardware ex2 (__expf, ~2 ulp), the softmax normalisation with an approximate
+// reciprocal, and the class sigmoid as 0.5 + 0.5 tanh(z / 2) with the hardware tanh:
+// 148 special-function operations per anchor instead of 144 accurate expf and 84
+// correctly rounded reciprocals, which made the kernel issue bound. FP32/TF32 plans
+// (fp32 logits) keep the accurate sequence above.
+__device__ __forceinline__ float head_tanh(float x) {
+    float y;
+    asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+__device__ __forceinline__ float head_rcp(float x) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 template <bool BF>
 __global__ void __launch_bounds__(kHeadAnchors) yolo_head_tile_kernel(YoloHeadArgs a, int tiles, int chunks,
                                                                       int row_chunks) {
@@ -136,8 +153,9 @@ __global__ void __launch_bounds__(kHeadAnchors) yolo_head_tile_kernel(YoloHeadAr
         for (int k = 0; k < kReg; ++k) mx = fmaxf(mx, x[k]);
         float sum = 0.0f;
 #pragma unroll
-        for (int k = 0; k < kReg; ++k) { x[k] = expf(x[k] - mx); sum += x[k]; }
-        const float inv = sum > 0.0f ? __frcp_rn(sum) : 0.0f;   // = 1.0f / sum (both correctly rounded)
+        for (int k = 0; k < kReg; ++k) { x[k] = BF ? __expf(x[k] - mx) : expf(x[k] - mx); sum += x[k]; }
+        // = 1.0f / sum (correctly rounded on the fp32 path)
+        const float inv = sum > 0.0f ? (BF ? head_rcp(sum) : __frcp_rn(sum)) : 0.0f;
         float d = 0.0f;
 #pragma unroll
         for (int k = 0; k < kReg; ++k) d = fmaf(x[k] * inv, a.dfl_w[k], d);
@@ -158,7 +176,9 @@ __global__ void __launch_bounds__(kHeadAnchors) yolo_head_tile_kernel(YoloHeadAr
         float z[kPer];
         unpack8<BF>(row[4 * kReg / kPer + c], z);
 #pragma unroll
-        for (int e = 0; e < kPer; ++e) o[(4 + c * kPer + e) * A] = __frcp_rn(1.0f + expf(-z[e]));
+        for (int e = 0; e < kPer; ++e)
+            o[(4 + c * kPer + e) * A] = BF ? fmaf(0.5f, head_tanh(0.5f * z[e]), 0.5f)
+                                           : __frcp_rn(1.0f + expf(-z[e]));   // = 1 / (1 + e), correctly rounded
     }
 }
 
