@@ -473,8 +473,19 @@ __global__ void __launch_bounds__(128, 8) conv_stem_tile_kernel(const StemTilePa
                 bv[4 * q] = b4.x; bv[4 * q + 1] = b4.y; bv[4 * q + 2] = b4.z; bv[4 * q + 3] = b4.w;
             }
             if (fast_epi) {
+                // bias + SiLU (x/2 + x/2 tanh(x/2)) on the packed fp32x2 pipe
 #pragma unroll
-                for (int i = 0; i < 16; ++i) o[i] = stem_act(__uint_as_float(rr[i]) + bv[i], ACT_SILU, 0.f);
+                for (int i = 0; i < 16; i += 2) {
+                    const float2 x = __fadd2_rn(make_float2(__uint_as_float(rr[i]), __uint_as_float(rr[i + 1])),
+                                                make_float2(bv[i], bv[i + 1]));
+                    const float2 h = __fmul2_rn(x, make_float2(0.5f, 0.5f));
+                    float t0, t1;
+                    asm("tanh.approx.f32 %0, %1;" : "=f"(t0) : "f"(h.x));
+                    asm("tanh.approx.f32 %0, %1;" : "=f"(t1) : "f"(h.y));
+                    const float2 y = __ffma2_rn(h, make_float2(t0, t1), h);
+                    o[i] = y.x;
+                    o[i + 1] = y.y;
+                }
             } else {
 #pragma unroll
                 for (int i = 0; i < 16; ++i) o[i] = stem_act(__uint_as_float(rr[i]) + bv[i], a.act, a.slope);
