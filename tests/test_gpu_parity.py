@@ -138,11 +138,13 @@ def test_stem_rows_kernel_batched(engine_dir, prec, cout, hw, s):
 @pytest.mark.parametrize("cin,cout,k,s,hw", [(64, 64, 3, 1, 20), (16, 48, 3, 2, 33), (80, 80, 1, 1, 12),
                                              (80, 80, 3, 1, 20), (48, 32, 1, 1, 24), (80, 64, 3, 2, 21),
                                              (112, 32, 3, 1, 9), (16, 16, 3, 1, 40), (32, 32, 3, 1, 37),
-                                             (16, 32, 3, 1, 61)])
+                                             (16, 32, 3, 1, 61), (144, 48, 3, 1, 13), (144, 32, 1, 1, 19)])
 def test_single_conv_staged_input(engine_dir, prec, cin, cout, k, s, hw):
     """A conv fed directly by the fp32 NCHW graph input: the plan stages the input into
-    the operand layout and runs the tensor-core kernel (no SIMT fallback). Cin = 48,
-    80 and 112 run in BF16 as zero-padded 64-channel chunks; the 16- and 32-channel
+    the operand layout and runs the tensor-core kernel (no SIMT fallback). In BF16,
+    multi-tap convs with Cin = 80 and 144 run as full 64-channel chunks plus a 16-channel
+    tail chunk (own 32-byte-swizzle maps); 1x1 convs with those Cin and Cin = 48 and 112
+    run as zero-padded 64-channel chunks; the 16- and 32-channel
     3x3 cases run in window mode (zero-padded row windows, taps as shifted windows)
     at sizes whose last tile is partial.
 
