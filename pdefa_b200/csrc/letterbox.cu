@@ -93,6 +93,48 @@ __global__ void __launch_bounds__(128) letterbox_kernel(const uint8_t* __restric
     }
 }
 
+// Identity geometry (the image already has the target size: ratio 1, no border). The
+// blend above then reduces exactly to one product per sample: inside the image fx = fy
+// = 0, so top = fma(p00, 1, p10 * 0) = p00 and value = fma(p00, scale, bot * 0) =
+// round(p00 * scale); on the last column (row) the clamped index gives fx (fy) = 1, so
+// the weights select p10 (the bottom row) exactly and the same single rounding follows.
+// One thread converts four pixels (one 12-byte RGB read) into three float4 stores.
+template <int CH>
+__global__ void __launch_bounds__(128) letterbox_identity_kernel(const uint8_t* __restrict__ src,
+                                                                 float* __restrict__ out, LetterboxGeom g) {
+    const int y = blockIdx.y;
+    const int64_t b = blockIdx.z;
+    const int x0p = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
+    if (x0p >= g.W) return;
+    const size_t plane = (size_t)g.W * g.H;
+    const uint8_t* const row = src + ((size_t)b * g.H + y) * g.W * CH + (size_t)x0p * CH;
+    uint8_t px[4 * CH];
+    if (CH == 3) {
+        const uint32_t* w = reinterpret_cast<const uint32_t*>(row);     // 4-byte aligned: W % 4 == 0
+        const uint32_t a = __ldcs(w), bb = __ldcs(w + 1), c = __ldcs(w + 2);
+        const uint32_t u[3] = {a, bb, c};
+#pragma unroll
+        for (int i = 0; i < 12; ++i) px[i] = (uint8_t)(u[i >> 2] >> (8 * (i & 3)));
+    } else if (CH == 4) {
+        const uint4 q = __ldcs(reinterpret_cast<const uint4*>(row));     // 16-byte aligned: W % 4 == 0
+        const uint32_t u[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int i = 0; i < 16; ++i) px[i] = (uint8_t)(u[i >> 2] >> (8 * (i & 3)));
+    } else {
+        const uint32_t a = __ldcs(reinterpret_cast<const uint32_t*>(row));
+#pragma unroll
+        for (int i = 0; i < 4; ++i) px[i] = (uint8_t)(a >> (8 * i));
+    }
+    float* const o = out + b * 3 * plane + (size_t)y * g.W + x0p;
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+        const int cc = CH == 1 ? 0 : c;
+        __stcs(reinterpret_cast<float4*>(o + c * plane),
+               make_float4(__fmul_rn((float)px[0 * CH + cc], g.scale), __fmul_rn((float)px[1 * CH + cc], g.scale),
+                           __fmul_rn((float)px[2 * CH + cc], g.scale), __fmul_rn((float)px[3 * CH + cc], g.scale)));
+    }
+}
+
 }  // namespace
 
 LetterboxGeom letterbox_geometry(int src_w, int src_h, int W, int H, float scale, float pad) {
@@ -116,6 +158,18 @@ void launch_letterbox_u8(const uint8_t* d_src, int64_t n, int channels, const Le
     const dim3 block(128);
     const dim3 grid((unsigned)((g.W + 4 * 128 - 1) / (4 * 128)), (unsigned)g.H, (unsigned)n);
     const bool vec = g.W % 4 == 0 && ((uintptr_t)d_out % 16) == 0;
+    const bool identity = g.ratio == 1.0f && g.inv == 1.0f && g.src_w == g.W && g.src_h == g.H && g.sw == g.W &&
+                          g.sh == g.H && g.px == 0 && g.py == 0;
+    if (identity && vec && ((uintptr_t)d_src % 16) == 0) {
+        switch (channels) {
+            case 1: letterbox_identity_kernel<1><<<grid, block, 0, s>>>(d_src, d_out, g); break;
+            case 3: letterbox_identity_kernel<3><<<grid, block, 0, s>>>(d_src, d_out, g); break;
+            case 4: letterbox_identity_kernel<4><<<grid, block, 0, s>>>(d_src, d_out, g); break;
+            default: fail(ENGINE_ERR_INVALID_ARG, "letterbox: channels must be 1, 3 or 4");
+        }
+        PB_CUDA(cudaGetLastError());
+        return;
+    }
     switch (channels * 2 + (vec ? 1 : 0)) {
         case 2: letterbox_kernel<1, false><<<grid, block, 0, s>>>(d_src, d_out, g); break;
         case 3: letterbox_kernel<1, true><<<grid, block, 0, s>>>(d_src, d_out, g); break;

@@ -32,7 +32,10 @@ def test_letterbox_matches_reference_golden():
 
 @pytest.mark.parametrize("n,h,w,ch,tw,th", [(3, 480, 640, 3, 640, 640), (2, 1080, 1920, 3, 640, 640),
                                             (4, 300, 200, 1, 320, 320), (2, 333, 517, 4, 416, 416),
-                                            (1, 17, 1, 3, 63, 61), (5, 64, 64, 3, 64, 64)])
+                                            (1, 17, 1, 3, 63, 61), (5, 64, 64, 3, 64, 64),
+                                            # identity geometry (the identity kernel): RGB, gray, RGBA
+                                            (3, 640, 640, 3, 640, 640), (2, 96, 128, 1, 128, 96),
+                                            (2, 40, 72, 4, 72, 40)])
 def test_letterbox_matches_oracle(n, h, w, ch, tw, th):
     rng = np.random.default_rng(n * 1000 + h)
     imgs = rng.integers(0, 256, (n, h, w, ch), dtype=np.uint8)
