@@ -11,7 +11,9 @@ Printed JSON line (rank 0):
   device, 1.26 GB per GPU > L2, so no L2 flush is needed), device-timed with CUDA
   events, max over ranks;
 * e2e: the same through the public batch API from pinned host images to host
-  detections: 8-bit RGB frames letterboxed on the GPU, one step per call of the
+  detections: 8-bit RGB frames at the model size, whose scale-only letterbox the stem
+  conv applies as it reads them (frames of another size are letterboxed by a GPU
+  kernel first), one step per call of the
   pipelined BatchInference.submit_u8 (pdefa_batch_submit_u8; step k's detections are
   read after step k+1 is queued), also as e2e.sync_value through the blocking
   detect_u8 (pdefa_batch_run_u8), and under e2e.f32_input float32 NCHW tensors
@@ -685,8 +687,10 @@ def main():
             "e2e": {"value": e2e_value, "unit": "images/s", "h2d_bytes_per_step": u8.numel(),
                     "d2h_bytes_per_step": B * 4 + B * max_det * 48, "micro_batch": e2e_micro,
                     "api": "BatchInference.submit_u8 + result() (pdefa_batch_submit_u8 / pdefa_batch_wait): "
-                           f"pinned 8-bit RGB frames [{B}, {args.imgsz}, {args.imgsz}, 3], GPU letterbox + "
-                           "inference + decode, step k+1 queued before step k's detections are read",
+                           f"pinned 8-bit RGB frames [{B}, {args.imgsz}, {args.imgsz}, 3] (already at the model "
+                           "size: the scale-only letterbox is fused into the stem conv, which reads the 8-bit "
+                           "pixels) + inference + decode, step k+1 queued before step k's detections are read",
+                    "steps": e2e_steps, "warmup": 3,
                     "sync_value": e2e_sync_value,
                     "sync_api": "BatchInference.detect_u8 (pdefa_batch_run_u8), one blocking call per step",
                     "f32_input": {"value": e2e_f32_value, "h2d_bytes_per_step": xh.numel() * 4,

@@ -181,7 +181,11 @@ ENGINE_API EngineStatus pdefa_letterbox(const uint8_t* images, int64_t n, int32_
  * inference and decode, and returns detections in original-image coordinates (the
  * decode unmaps boxes with the letterbox meta, as decode_yolo(out, meta) does).
  * The model input must be [B, 3, cfg->target_h, cfg->target_w]. out_meta (may be
- * NULL) receives the shared meta record. */
+ * NULL) receives the shared meta record. RGB images already at the target size
+ * (width a multiple of 4) on a BF16 runner skip the letterbox kernel: the stem conv
+ * reads the 8-bit pixels and applies pixel * cfg->scale itself (the letterbox's
+ * value for that geometry, bit for bit), when the stem is a 3x3 stride-2 conv and
+ * the input's only consumer; otherwise the letterbox runs as above. */
 ENGINE_API EngineStatus pdefa_batch_run_u8(PdefaBatchRunner* runner, const uint8_t* images, int64_t n_images,
                                            int32_t src_h, int32_t src_w, int32_t channels,
                                            const PdefaPreprocessConfig* cfg, double conf_thres, double iou_thres,

@@ -2,6 +2,7 @@
 // device-pointer execution, tensor-core GEMM, batched GPU decode/NMS and the
 // multi-GPU batch runner (one replica per device, contiguous shards, no collective).
 #include <algorithm>
+#include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
@@ -48,6 +49,8 @@ struct PdefaBatchRunner {
     // that the copy of micro-batch i+1 onto the GPU overlaps the inference of i.
     struct Lane {
         std::map<int64_t, std::unique_ptr<Plan>> plans;
+        // plans whose stem reads the 8-bit frames itself (identity letterbox fused)
+        std::map<int64_t, std::unique_ptr<Plan>> plans_u8;
         void* counts = nullptr;      // device [max_per_device]
         void* dets = nullptr;        // device [max_per_device * max_det]
         void* work = nullptr;
@@ -77,6 +80,7 @@ struct PdefaBatchRunner {
         cudaStream_t post = nullptr;     // decode + result copies (overlap the next inference)
         Lane lanes[2];
         int64_t next_lane = 0;           // lanes alternate across calls too
+        bool u8_unfused = false;         // the graph cannot take 8-bit frames at its stem
     };
     std::shared_ptr<const Graph> graph;
     int precision = PREC_BF16;
@@ -492,10 +496,49 @@ EngineStatus run_batch(PdefaBatchRunner* r, const BatchInput& in, int64_t n_imag
                         nb = std::min(i == 0 ? mfirst : mfull, hi - c0);
                         auto& l = rp.lanes[rp.next_lane++ & 1];
                         retire(l);    // the lane's buffers are free once its previous micro-batch is done
-                        auto it = l.plans.find(nb);
-                        if (it == l.plans.end())
-                            it = l.plans.emplace(nb, std::make_unique<Plan>(r->graph, nb, r->precision, rp.device)).first;
-                        Plan& p = *it->second;
+                        // Frames already at the model size with scale-only preprocessing go
+                        // straight to a plan whose stem conv reads the 8-bit pixels (pixel *
+                        // scale, bit for bit the letterbox's value); other geometries, and
+                        // graphs whose stem cannot take them, letterbox into a float32 input.
+                        const LetterboxGeom& gm = in.geo;
+                        const bool fuse = !in.f32 && !rp.u8_unfused && in.channels == 3 && gm.ratio == 1.0f &&
+                                          gm.inv == 1.0f && gm.src_w == gm.W && gm.src_h == gm.H && gm.sw == gm.W &&
+                                          gm.sh == gm.H && gm.px == 0 && gm.py == 0 && gm.W % 4 == 0 &&
+                                          gm.scale > 0.0f && r->precision == PREC_BF16;
+                        Plan* pp = nullptr;
+                        if (fuse) {
+                            auto fit = l.plans_u8.find(nb);
+                            if (fit != l.plans_u8.end() && fit->second->u8_scale() != gm.scale) {
+                                l.plans_u8.erase(fit);
+                                fit = l.plans_u8.end();
+                            }
+                            if (fit == l.plans_u8.end()) {
+                                try {
+                                    fit = l.plans_u8.emplace(nb, std::make_unique<Plan>(r->graph, nb, r->precision,
+                                                                                        rp.device, std::vector<int32_t>{},
+                                                                                        std::vector<int64_t>{}, gm.scale))
+                                              .first;
+                                    if (verbose())
+                                        std::fprintf(stderr, "[pdefa-b200] batch runner: 8-bit frames read by the stem "
+                                                     "(batch %lld)\n", (long long)nb);
+                                } catch (const Error& e) {
+                                    if (e.status != ENGINE_ERR_NOT_IMPL) throw;
+                                    if (verbose())
+                                        std::fprintf(stderr, "[pdefa-b200] batch runner: letterbox kept (%s)\n", e.what());
+                                    rp.u8_unfused = true;
+                                }
+                            }
+                            if (fit != l.plans_u8.end()) pp = fit->second.get();
+                        }
+                        if (!pp) {
+                            auto it = l.plans.find(nb);
+                            if (it == l.plans.end())
+                                it = l.plans.emplace(nb, std::make_unique<Plan>(r->graph, nb, r->precision, rp.device))
+                                         .first;
+                            pp = it->second.get();
+                        }
+                        Plan& p = *pp;
+                        const bool fused = p.u8_scale() > 0.0f;
                         const auto& os = p.output_shape(0);
                         if (os.size() != 3) fail(ENGINE_ERR_INVALID_SHAPE, "batch runner expects a [B, 4+nc, A] output");
                         const int64_t ch = os[1], A = os[2];
@@ -522,9 +565,15 @@ EngineStatus run_batch(PdefaBatchRunner* r, const BatchInput& in, int64_t n_imag
                         } else {
                             // 8-bit pixels cross PCIe (a quarter of the float32 bytes for RGB) and
                             // are letterboxed into the plan's input on the GPU
-                            if (ibytes != (size_t)nb * 3 * in.geo.H * in.geo.W * sizeof(float))
+                            if (ibytes != (size_t)nb * 3 * in.geo.H * in.geo.W * (fused ? 1 : sizeof(float)))
                                 fail(ENGINE_ERR_INVALID_SHAPE, "batch_run_u8: the model input is not [B, 3, target_h, target_w]");
                             const size_t pb_img = (size_t)in.geo.src_h * in.geo.src_w * in.channels;
+                            if (fused) {
+                                PB_CUDA(cudaMemcpyAsync(p.input_buffer(0), in.u8 + c0 * pb_img, pb_img * nb,
+                                                        cudaMemcpyHostToDevice, rp.copy));
+                                PB_CUDA(cudaEventRecord(l.h2d, rp.copy));
+                                PB_CUDA(cudaStreamWaitEvent(l.compute, l.h2d, 0));
+                            } else {
                             if (l.pixels_cap < pb_img * r->max_per_device) {
                                 if (l.pixels) cudaFree(l.pixels);
                                 l.pixels = nullptr;
@@ -538,6 +587,7 @@ EngineStatus run_batch(PdefaBatchRunner* r, const BatchInput& in, int64_t n_imag
                             PB_CUDA(cudaStreamWaitEvent(l.compute, l.h2d, 0));
                             launch_letterbox_u8(static_cast<const uint8_t*>(l.pixels), nb, in.channels, in.geo,
                                                 p.input_buffer(0), l.compute);
+                            }
                         }
                         p.run(l.compute);
                         // decode on its own stream: one CTA per image leaves most SMs to the
@@ -763,6 +813,7 @@ ENGINE_API void pdefa_batch_destroy(PdefaBatchRunner* r) {
         if (rp.post) cudaStreamSynchronize(rp.post);
         for (auto& l : rp.lanes) {
             l.plans.clear();
+            l.plans_u8.clear();
             free_lane(l);
             if (l.h2d) cudaEventDestroy(l.h2d);
             if (l.ran) cudaEventDestroy(l.ran);

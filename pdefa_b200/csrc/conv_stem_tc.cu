@@ -295,6 +295,8 @@ __device__ __forceinline__ uint32_t stem_div(uint32_t n, const StemDiv& f) {
 
 struct StemTileParams {
     ConvArgs a;
+    const uint8_t* u8;    // 8-bit RGB frames instead of the fp32 input (U8 variant)
+    float u8_scale;
     int Ho, Wo, K;
     int tiles_h, tiles_w;
     StemDiv div_img, div_tw;   // tile -> (image, tile row, tile column)
@@ -333,6 +335,33 @@ __device__ __forceinline__ void stem_region_load(const StemTileParams& P, int64_
     asm volatile("cp.async.commit_group;" ::: "memory");
 }
 
+// The same region from 8-bit RGB frames [N, H, W, 3] (U8 variant): 17 rows of 36 pixels
+// = 108 bytes, as 27 pieces of 4 bytes; W % 4 == 0 and the region starts at a multiple
+// of 4 pixels, so each group of three pieces (four pixels) is all in or all out.
+constexpr int kRegU8Row = kRegW * 3;                       // 108 bytes
+constexpr int kRegU8Bytes = (kRegH * kRegU8Row + 15) & ~15;
+
+__device__ __forceinline__ void cp_async4_u8(uint32_t dst, const void* src, bool in) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(in ? 4 : 0) : "memory");
+}
+
+__device__ __forceinline__ void stem_region_load_u8(const StemTileParams& P, int64_t t, uint8_t* dst, int H, int W) {
+    const uint32_t b = stem_div((uint32_t)t, P.div_img);
+    const int r = (int)((uint32_t)t - b * P.div_img.d);
+    const int th = (int)stem_div((uint32_t)r, P.div_tw), tw = r - th * P.tiles_w;
+    const int h0 = th * (2 * kTileH) - 1, c0 = tw * (2 * kTileW) - 4;
+    const uint8_t* const img = P.u8 + (int64_t)b * H * W * 3;
+    for (int i = threadIdx.x; i < kRegH * (kRegU8Row / 4); i += blockDim.x) {
+        const int row = i / (kRegU8Row / 4), j = i - row * (kRegU8Row / 4);
+        const int hi = h0 + row, px = c0 + 4 * (j / 3);
+        const bool ok = hi >= 0 && hi < H && px >= 0 && px < W;
+        const uint8_t* src = ok ? img + ((int64_t)hi * W + c0) * 3 + 4 * j : P.u8;
+        cp_async4_u8(smem_u32(dst + row * kRegU8Row + 4 * j), src, ok);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+template <bool U8>
 __global__ void __launch_bounds__(128, 8) conv_stem_tile_kernel(const StemTileParams P) {
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
@@ -343,7 +372,7 @@ __global__ void __launch_bounds__(128, 8) conv_stem_tile_kernel(const StemTilePa
     // [A: 128 rows x 64 B | B: cout rows x 64 B | region x 2 | barrier, TMEM slot, flag]
     uint8_t* const sA = smem;
     uint8_t* const sB = smem + kRows * kRowBytes;
-    constexpr int rbytes = 3 * kRegPlane * 4;
+    constexpr int rbytes = U8 ? kRegU8Bytes : 3 * kRegPlane * 4;
     float* const sR0 = reinterpret_cast<float*>(sB + ((cout * kRowBytes + 511) & ~511));
     float* const sR1 = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(sR0) + rbytes);
     uint64_t* const mbar = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(sR1) + rbytes);
@@ -357,7 +386,10 @@ __global__ void __launch_bounds__(128, 8) conv_stem_tile_kernel(const StemTilePa
     if (*abort_flag) return;
 
     const int H = (int)a.in.shape[1], W = (int)a.in.shape[2];
-    if ((int64_t)blockIdx.x < P.tiles) stem_region_load(P, blockIdx.x, sR0, H, W);
+    if ((int64_t)blockIdx.x < P.tiles) {
+        if (U8) stem_region_load_u8(P, blockIdx.x, reinterpret_cast<uint8_t*>(sR0), H, W);
+        else stem_region_load(P, blockIdx.x, sR0, H, W);
+    }
 
     const float* w = reinterpret_cast<const float*>(a.weight);
     for (int i = tid; i < cout * 32; i += blockDim.x) {
@@ -398,7 +430,8 @@ __global__ void __launch_bounds__(128, 8) conv_stem_tile_kernel(const StemTilePa
         float* const cur = (it & 1) ? sR1 : sR0;
         float* const nxt = (it & 1) ? sR0 : sR1;
         if (tn < P.tiles) {
-            stem_region_load(P, tn, nxt, H, W);
+            if (U8) stem_region_load_u8(P, tn, reinterpret_cast<uint8_t*>(nxt), H, W);
+            else stem_region_load(P, tn, nxt, H, W);
             asm volatile("cp.async.wait_group 1;" ::: "memory");
         } else {
             asm volatile("cp.async.wait_group 0;" ::: "memory");
@@ -406,13 +439,25 @@ __global__ void __launch_bounds__(128, 8) conv_stem_tile_kernel(const StemTilePa
         __syncthreads();          // region visible; previous tile's TMEM reads finished
         {
             float v[32];
-#pragma unroll
-            for (int c = 0; c < 3; ++c)
+            if (U8) {
+                // pixel * scale: the identity letterbox's value, bit for bit
+                const uint8_t* cu = reinterpret_cast<const uint8_t*>(cur) + 2 * py * kRegU8Row + (2 * px + 3) * 3;
 #pragma unroll
                 for (int kr = 0; kr < 3; ++kr)
 #pragma unroll
                     for (int ks = 0; ks < 3; ++ks)
-                        v[(kr * 3 + ks) * 3 + c] = cur[rbase + c * kRegPlane + kr * kRegW + ks];
+#pragma unroll
+                        for (int c = 0; c < 3; ++c)
+                            v[(kr * 3 + ks) * 3 + c] = __fmul_rn((float)cu[kr * kRegU8Row + ks * 3 + c], P.u8_scale);
+            } else {
+#pragma unroll
+                for (int c = 0; c < 3; ++c)
+#pragma unroll
+                    for (int kr = 0; kr < 3; ++kr)
+#pragma unroll
+                        for (int ks = 0; ks < 3; ++ks)
+                            v[(kr * 3 + ks) * 3 + c] = cur[rbase + c * kRegPlane + kr * kRegW + ks];
+            }
 #pragma unroll
             for (int k = 27; k < 32; ++k) v[k] = 0.0f;
 #pragma unroll
@@ -540,12 +585,18 @@ void launch_conv_stem_tc(const ConvArgs& a, int* err, cudaStream_t s) {
     int dev0 = 0;
     PB_CUDA(cudaGetDevice(&dev0));
     const int esz_in = 4;
-    if (a.kh == 3 && a.kw == 3 && a.cin == 3 && a.in.dt == F32 && a.sh == 2 && a.sw == 2 && a.ph == 1 && a.pw == 1 &&
-        a.dh == 1 && a.dw == 1 && a.in.stride[2] == 1 && a.in.shape[2] % 4 == 0 && ((uintptr_t)a.in.ptr % 16) == 0 &&
-        (a.in.stride[1] * esz_in) % 16 == 0 && (a.in.stride[3] * esz_in) % 16 == 0 &&
-        (a.in.img_stride * esz_in) % 16 == 0) {
+    const bool u8 = a.in_u8 != nullptr;
+    const bool geom = a.kh == 3 && a.kw == 3 && a.cin == 3 && a.sh == 2 && a.sw == 2 && a.ph == 1 && a.pw == 1 &&
+                      a.dh == 1 && a.dw == 1 && a.in.shape[2] % 4 == 0;
+    if (u8 && !(geom && ((uintptr_t)a.in_u8 % 4) == 0))
+        fail(ENGINE_ERR_NOT_IMPL, "conv_stem_tc: 8-bit input needs a 3x3 stride-2 RGB stem with W % 4 == 0");
+    if (geom && (u8 || (a.in.dt == F32 && a.in.stride[2] == 1 && ((uintptr_t)a.in.ptr % 16) == 0 &&
+                        (a.in.stride[1] * esz_in) % 16 == 0 && (a.in.stride[3] * esz_in) % 16 == 0 &&
+                        (a.in.img_stride * esz_in) % 16 == 0))) {
         StemTileParams T;
         T.a = a;
+        T.u8 = a.in_u8;
+        T.u8_scale = a.in_u8_scale;
         T.Ho = P.Ho; T.Wo = P.Wo; T.K = P.K;
         T.tiles_h = (P.Ho + kTileH - 1) / kTileH;
         T.tiles_w = (P.Wo + kTileW - 1) / kTileW;
@@ -556,7 +607,7 @@ void launch_conv_stem_tc(const ConvArgs& a, int* err, cudaStream_t s) {
         T.RW = kRegW;
         T.ncols = P.ncols;
         T.err = err;
-        const size_t rbytes = (size_t)3 * kRegPlane * 4;
+        const size_t rbytes = u8 ? (size_t)kRegU8Bytes : (size_t)3 * kRegPlane * 4;
         // tail: barrier, TMEM slot, flag (16 B), then the biases (cout floats)
         const size_t smem = 512 + kRows * kRowBytes + ((a.cout * kRowBytes + 511) & ~511) + 2 * rbytes + 16 +
                             (((size_t)a.cout * 4 + 15) & ~size_t(15)) + 48;
@@ -572,11 +623,13 @@ void launch_conv_stem_tc(const ConvArgs& a, int* err, cudaStream_t s) {
             const int by_smem = (int)((228u * 1024u) / (smem + 1024));
             const int per_sm = std::max(1, std::min({8, by_smem, 512 / T.ncols}));
             const int64_t grid = std::min<int64_t>(T.tiles, (int64_t)sms * per_sm);
-            conv_stem_tile_kernel<<<(unsigned)grid, 128, smem, s>>>(T);
+            if (u8) conv_stem_tile_kernel<true><<<(unsigned)grid, 128, smem, s>>>(T);
+            else conv_stem_tile_kernel<false><<<(unsigned)grid, 128, smem, s>>>(T);
             PB_CUDA(cudaGetLastError());
             return;
         }
     }
+    if (u8) fail(ENGINE_ERR_NOT_IMPL, "conv_stem_tc: 8-bit input needs the tiled stem kernel");
     P.tiles = (P.M + kRows - 1) / kRows;
     P.ncols = 32;
     while (P.ncols < a.cout) P.ncols <<= 1;

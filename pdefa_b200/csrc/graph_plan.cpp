@@ -32,13 +32,13 @@ int reference_conv_path(int64_t cin, int64_t kh, int64_t kw, const OpParams& p) 
     return 2;
 }
 
-namespace {
-
 bool verbose() {
     static int v = -1;
     if (v < 0) { const char* e = std::getenv("PDEFA_VERBOSE"); v = (e && *e && *e != '0') ? 1 : 0; }
     return v == 1;
 }
+
+namespace {
 
 int64_t numel_of(const std::vector<int64_t>& s) {
     int64_t n = 1;
@@ -920,6 +920,7 @@ struct PlanBuilder {
     // reference's CPU buffers the same way, by live ranges).
     std::vector<void*> bufs;
     int cur_node = -1;                       // node being emitted; nodes.size() for the outputs
+    bool u8_stem = false;                    // the stem reads 8-bit input frames (Plan::u8_scale_)
     const std::vector<size_t>* arena_off = nullptr;   // real lowering: byte offset per value id
     char* arena = nullptr;
 
@@ -1053,9 +1054,11 @@ struct PlanBuilder {
             Value& x = V[v];
             const auto& s = x.shape;   // motor [1,H,W,C] for rank 4
             const int64_t per = numel_of(s);
-            float* d = static_cast<float*>(P.alloc(std::max<size_t>((size_t)per * B * 4, 16)));
+            // 8-bit frames: one byte per element, read only by the stem (checked below)
+            const size_t ibytes = (size_t)per * B * (i == 0 && P.u8_scale_ > 0.0f ? 1 : 4);
+            float* d = static_cast<float*>(P.alloc(std::max<size_t>(ibytes, 16)));
             P.inputs_.push_back(d);
-            P.input_bytes_.push_back((size_t)per * B * 4);
+            P.input_bytes_.push_back(ibytes);
             x.buf = (int)bufs.size();
             bufs.push_back(d);
             x.off = 0;
@@ -1074,6 +1077,8 @@ struct PlanBuilder {
             emit_node((int)i);
         }
         cur_node = (int)nodes.size();
+        if (P.u8_scale_ > 0.0f && (!u8_stem || consumers[g.inputs[0]] != 1))
+            fail(ENGINE_ERR_NOT_IMPL, "8-bit input: the stem conv must be the graph input's only consumer");
         // outputs: dense fp32, rank-4 converted to NCHW (session.cpp:347-361)
         for (size_t k = 0; k < g.outputs.size(); ++k) {
             const int v = vid[g.outputs[k]];
@@ -1587,9 +1592,21 @@ struct PlanBuilder {
             a.weight = d;
             if (prec == PREC_BF16 && conv_stem_tc_supported(a)) {
                 int* err = P.err_;
+                const bool u8 = ext && P.u8_scale_ > 0.0f;
+                if (u8 && !(a.kh == 3 && a.kw == 3 && a.cin == 3 && a.sh == 2 && a.sw == 2 && a.ph == 1 && a.pw == 1 &&
+                            a.dh == 1 && a.dw == 1 && a.in.shape[2] % 4 == 0))
+                    fail(ENGINE_ERR_NOT_IMPL, "8-bit input needs a 3x3 stride-2 RGB stem with width % 4 == 0");
+                if (u8) {
+                    a.in_u8 = reinterpret_cast<const uint8_t*>(P.inputs_[0]);
+                    a.in_u8_scale = P.u8_scale_;
+                    u8_stem = true;
+                }
                 kind("conv_stem_tc");
-                add_step(n.name, [a, ext, pp, err](cudaStream_t s) mutable {
-                    if (ext && pp->cur_in_) a.in.ptr = pp->cur_in_;
+                add_step(n.name, [a, ext, u8, pp, err](cudaStream_t s) mutable {
+                    if (ext && pp->cur_in_) {
+                        if (u8) a.in_u8 = reinterpret_cast<const uint8_t*>(pp->cur_in_);
+                        else a.in.ptr = pp->cur_in_;
+                    }
                     launch_conv_stem_tc(a, err, s);
                 });
             } else if (conv_direct_supported(a)) {
@@ -1714,9 +1731,9 @@ struct PlanBuilder {
 };
 
 Plan::Plan(std::shared_ptr<const Graph> g, int64_t batch, int precision, int device, std::vector<int32_t> keep,
-           std::vector<int64_t> in_shape)
+           std::vector<int64_t> in_shape, float in_u8_scale)
     : g_(std::move(g)), batch_(batch), prec_(precision), device_(device), keep_(std::move(keep)),
-      in_shape_(std::move(in_shape)) {
+      in_shape_(std::move(in_shape)), u8_scale_(in_u8_scale) {
     require_device(device);
     if (batch < 1) fail(ENGINE_ERR_INVALID_ARG, "batch must be >= 1");
     PB_CUDA(cudaSetDevice(device));
@@ -1730,9 +1747,9 @@ Plan::Plan(std::shared_ptr<const Graph> g, int64_t batch, int precision, int dev
 }
 
 Plan::Plan(DryTag, std::shared_ptr<const Graph> g, int64_t batch, int precision, std::vector<int32_t> keep,
-           std::vector<int64_t> in_shape)
+           std::vector<int64_t> in_shape, float in_u8_scale)
     : g_(std::move(g)), dry_(true), batch_(batch), prec_(precision), device_(0), keep_(std::move(keep)),
-      in_shape_(std::move(in_shape)) {
+      in_shape_(std::move(in_shape)), u8_scale_(in_u8_scale) {
     if (batch < 1) fail(ENGINE_ERR_INVALID_ARG, "batch must be >= 1");
     build();
 }
@@ -1846,7 +1863,7 @@ void Plan::build() {
     }
     // A dry lowering of the same graph records every root's size and node range; the
     // real lowering then places the roots in one arena at packed offsets.
-    Plan probe(DryTag{}, g_, batch_, prec_, keep_, in_shape_);
+    Plan probe(DryTag{}, g_, batch_, prec_, keep_, in_shape_, u8_scale_);
     size_t total = 0;
     const std::vector<size_t> off = pack_arena(probe.root_bytes_, probe.root_first_, probe.root_last_, &total);
     char* base = static_cast<char*>(alloc(std::max<size_t>(total, 256)));

@@ -47,14 +47,20 @@ struct PlanStep {
     std::string kind;                // kernel family, for plan summaries
 };
 
+// PDEFA_VERBOSE set (and not "0"): lowering and runner decisions are printed to stderr.
+bool verbose();
+
 class Plan {
 public:
     // keep: engine tensor indices whose values stay readable after a run (see
     // debug_view); values no node consumes are always kept, as in the reference.
     // in_shape: shape of one image of input 0 when it differs from the declared one
     // (empty: the declared shape).
+    // in_u8_scale > 0: input 0 is given as 8-bit RGB frames [batch, H, W, 3] at the model
+    // size, read by the stem conv as pixel * in_u8_scale (the identity letterbox, fused);
+    // lowering fails unless the stem is input 0's only consumer.
     Plan(std::shared_ptr<const Graph> g, int64_t batch, int precision, int device,
-         std::vector<int32_t> keep = {}, std::vector<int64_t> in_shape = {});
+         std::vector<int32_t> keep = {}, std::vector<int64_t> in_shape = {}, float in_u8_scale = 0.0f);
     // Device-free lowering: every pass runs and every launch is recorded, but nothing
     // is allocated or copied (addresses are placeholders). Used to validate a model
     // and to inspect its launch list without a GPU.
@@ -68,6 +74,8 @@ public:
     // Input i: device buffer the caller fills with [batch, C, H, W] (NCHW fp32) data.
     float* input_buffer(int i) const { return inputs_.at(i); }
     size_t input_bytes(int i) const { return input_bytes_.at(i); }
+    // > 0: input 0 holds 8-bit RGB frames [batch, H, W, 3] read as pixel * u8_scale()
+    float u8_scale() const { return u8_scale_; }
     // Output i: dense fp32 device buffer in the reference's output layout.
     float* output_buffer(int i) const { return outputs_.at(i); }
     const std::vector<int64_t>& output_shape(int i) const { return out_shapes_.at(i); }
@@ -113,9 +121,10 @@ private:
 
     struct DryTag {};
     Plan(DryTag, std::shared_ptr<const Graph> g, int64_t batch, int precision, std::vector<int32_t> keep = {},
-         std::vector<int64_t> in_shape = {});
+         std::vector<int64_t> in_shape = {}, float in_u8_scale = 0.0f);
     std::vector<int32_t> keep_;
     std::vector<int64_t> in_shape_;
+    float u8_scale_ = 0.0f;
     std::map<int32_t, TView> debug_;
     std::shared_ptr<const Graph> g_;
     bool dry_ = false;

@@ -78,6 +78,10 @@ struct ConvArgs {
     float slope = 0.01f;
     int64_t batch = 1;
     long long wait_limit = 0;   // tcgen05 kernels: bounded-wait limit in SM cycles (0: default)
+    // stem only: read the input as 8-bit RGB frames [batch, H, W, 3] (pixel * in_u8_scale,
+    // the identity letterbox) instead of the fp32 NCHW view `in` (which still gives H, W)
+    const uint8_t* in_u8 = nullptr;
+    float in_u8_scale = 0.0f;
 };
 // Strict fp32 SIMT implicit GEMM. weight: fp32 [kh][kw][cin][cout].
 void launch_conv_simt(const ConvArgs& a, cudaStream_t s);

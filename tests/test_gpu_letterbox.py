@@ -216,3 +216,73 @@ def test_batch_submit_u8_matches_detect_u8(engine_dir):
         for b in range(len(c)):
             np.testing.assert_array_equal(d[b, :c[b]], dw[b, :cw[b]])
         assert meta == mw
+
+
+_FUSED_SCRIPT = r"""
+import sys
+import numpy as np
+import pdefa_b200 as pb
+path, out, prec = sys.argv[1], sys.argv[2], sys.argv[3]
+ctx = pb.Context(precision=pb.BF16 if prec == "bf16" else pb.FP32)
+m = pb.Model(ctx, path)
+rng = np.random.default_rng(33)
+ident = rng.integers(0, 256, (5, 128, 128, 3), dtype=np.uint8)
+other = rng.integers(0, 256, (3, 96, 150, 3), dtype=np.uint8)
+kw = dict(conf_thres=0.2, iou_thres=0.5, max_det=40)
+res = {}
+with pb.BatchInference(ctx, m, batch_size=2, devices=[0]) as bi:
+    for tag, f in (("a", ident), ("b", other), ("c", ident[::-1].copy())):
+        c, d, meta = bi.detect_u8(f, 128, 128, **kw)
+        res["counts_" + tag], res["dets_" + tag] = c, d
+np.savez(out, **res)
+"""
+
+
+def _session_dets(ctx, m, imgs, kw):
+    x, meta = pb.letterbox_u8(imgs, 128, 128)
+    s = pb.Session(ctx, m)
+    s.set_input(0, pb.Tensor.from_numpy(x))
+    s.run()
+    y = s.output(0).to_numpy()
+    return [pb.decode_yolo(y[b], meta, kw["conf_thres"], kw["iou_thres"], kw["max_det"]) for b in range(len(imgs))]
+
+
+@pytest.mark.parametrize("prec", ["bf16", "fp32"])
+def test_detect_u8_fused_stem_matches_letterbox_path(engine_dir, tmp_path, prec):
+    """Frames already at the model size with scale-only preprocessing skip the letterbox
+    kernel: the runner lowers a plan whose stem conv reads the 8-bit pixels itself
+    (pixel * scale, the identity letterbox's value). Its detections equal the letterbox
+    + session + decode pieces run one by one, on the same runner as calls with other
+    geometries (which keep the letterbox). PDEFA_VERBOSE shows which path ran: BF16
+    fuses, FP32 (no tcgen05 stem) keeps the letterbox."""
+    import subprocess
+    import sys
+    g, _ = build_yolov8("n", imgsz=128, seed=0)
+    p = str(engine_dir / "y8n_128_fused.engine")
+    write_engine(p, g)
+    out = str(tmp_path / "fused.npz")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, PDEFA_VERBOSE="1", PYTHONPATH=root + os.pathsep + os.environ.get("PYTHONPATH", ""))
+    r = subprocess.run([sys.executable, "-c", _FUSED_SCRIPT, p, out, prec], capture_output=True, text=True,
+                       timeout=600, env=env, cwd=root)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
+    fused = "8-bit frames read by the stem" in r.stderr
+    assert fused == (prec == "bf16"), r.stderr[-3000:]
+    d = np.load(out)
+    ctx = pb.Context(precision=pb.BF16 if prec == "bf16" else pb.FP32)
+    m = pb.Model(ctx, p)
+    rng = np.random.default_rng(33)
+    ident = rng.integers(0, 256, (5, 128, 128, 3), dtype=np.uint8)
+    other = rng.integers(0, 256, (3, 96, 150, 3), dtype=np.uint8)
+    kw = dict(conf_thres=0.2, iou_thres=0.5, max_det=40)
+    total = 0
+    for tag, f in (("a", ident), ("b", other), ("c", ident[::-1].copy())):
+        exp = _session_dets(ctx, m, f, kw)
+        counts, dets = d["counts_" + tag], d["dets_" + tag]
+        for b in range(len(f)):
+            got = dets[b, :counts[b]]
+            assert len(exp[b]) == counts[b], (tag, b)
+            assert [(e["x1"], e["y1"], e["x2"], e["y2"], e["conf"], e["cls"]) for e in exp[b]] == \
+                [(r["x1"], r["y1"], r["x2"], r["y2"], r["conf"], int(r["cls"])) for r in got], (tag, b)
+            total += int(counts[b])
+    assert total > 0
