@@ -38,7 +38,7 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int kMaxBuf = 4;                        // TMEM accumulator buffers at most
-constexpr int kMaxHalo = 4;                       // window slots (a_mode 2)
+constexpr int kMaxHalo = 8;                       // window slots (a_mode 2)
 constexpr uint32_t kBarrierBytes = 512;           // mbarriers, TMEM slot, abort flag
 // Epilogue warps per CTA: EPI = 4 (one group, one warp per TMEM lane quarter) or 8
 // (two groups that split the columns). Threads: producer warp, MMA warp, epilogue.
@@ -63,6 +63,19 @@ FastDiv make_fastdiv(uint32_t d) {
 __device__ __forceinline__ uint32_t fdiv(uint32_t n, const FastDiv& f) {
     return (uint32_t)(((uint64_t)n * f.m) >> f.p);
 }
+
+// Position in a ring of n slots: slot index and the parity of the pass, advanced
+// without division. The pipeline roles are single threads (or one warp) that step
+// their rings once per k-block; a 64-bit division by a runtime ring size is a long
+// software sequence on the GPU and cost those threads thousands of cycles per tile.
+struct RingPos {
+    int slot = 0;
+    uint32_t phase = 0;     // completed passes & 1
+    bool wrapped = false;   // at least one full pass: every slot was used before
+    __device__ __forceinline__ void next(int n) {
+        if (++slot == n) { slot = 0; phase ^= 1u; wrapped = true; }
+    }
+};
 
 struct TcParams {
     int64_t M;
@@ -98,6 +111,12 @@ struct TcParams {
     // tensor maps (tmA2 / tmB2), instead of a full chunk padded with zeros.
     int tail_ch;
     uint32_t tail_a_bytes, tail_b_bytes;
+    // win2d (a_mode 2): 2-D output tiles of TR rows x TW columns on a pitch of Wp
+    // positions per row (Wp = TW + kw - 1, TR * Wp = 128), so a window is NR = TR +
+    // kh - 1 rows of Wp positions instead of whole padded image rows; tiles
+    // (image, tile row, tile column), tiles_w of them per tile row.
+    int win2d, TR, TW, tiles_w;
+    FastDiv div_tw2;
 };
 
 __device__ __forceinline__ uint64_t make_smem_desc(uint32_t addr, int swb) {
@@ -186,6 +205,60 @@ __device__ __forceinline__ void umma_kblock(uint32_t tmem_d, uint64_t da, uint64
             ::"r"(tmem_d), "l"(da), "l"(db), "r"(idesc), "r"(acc), "r"(ksteps), "r"(bar ? smem_u32(bar) : 0u),
               "r"(bar ? 1u : 0u)
             : "memory");
+    }
+}
+
+// The same with exactly KS MMAs (KS = ksteps, a launch constant). A predicated-off
+// tcgen05.mma still costs the issuing thread about as much as an issued one (9
+// k-blocks of one 32-byte slice: 1574 cycles with three predicated-off MMAs each,
+// 658 without, measured on B200), so narrow chunks (KS 1, 2) issue no padding.
+template <int KIND, int KS>
+__device__ __forceinline__ void umma_kblock_n(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc,
+                                              uint64_t* bar) {
+    if (KS == 4) {
+        umma_kblock<KIND>(tmem_d, da, db, idesc, acc, 4, bar);
+    } else if (KS == 2) {
+        if (KIND == 0)
+            asm volatile(
+                "{\n\t.reg .pred pa, pt, pc;\n\t.reg .b64 a1, b1;\n\t"
+                "setp.ne.b32 pa, %4, 0;\n\tsetp.eq.u32 pt, 0, 0;\n\tsetp.ne.b32 pc, %6, 0;\n\t"
+                "add.s64 a1, %1, 2;\n\tadd.s64 b1, %2, 2;\n\t"
+                "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, pa;\n\t"
+                "tcgen05.mma.cta_group::1.kind::f16 [%0], a1, b1, %3, pt;\n\t"
+                "@pc tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%5];\n\t}"
+                ::"r"(tmem_d), "l"(da), "l"(db), "r"(idesc), "r"(acc), "r"(bar ? smem_u32(bar) : 0u),
+                  "r"(bar ? 1u : 0u)
+                : "memory");
+        else
+            asm volatile(
+                "{\n\t.reg .pred pa, pt, pc;\n\t.reg .b64 a1, b1;\n\t"
+                "setp.ne.b32 pa, %4, 0;\n\tsetp.eq.u32 pt, 0, 0;\n\tsetp.ne.b32 pc, %6, 0;\n\t"
+                "add.s64 a1, %1, 2;\n\tadd.s64 b1, %2, 2;\n\t"
+                "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, pa;\n\t"
+                "tcgen05.mma.cta_group::1.kind::tf32 [%0], a1, b1, %3, pt;\n\t"
+                "@pc tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%5];\n\t}"
+                ::"r"(tmem_d), "l"(da), "l"(db), "r"(idesc), "r"(acc), "r"(bar ? smem_u32(bar) : 0u),
+                  "r"(bar ? 1u : 0u)
+                : "memory");
+    } else {
+        if (KIND == 0)
+            asm volatile(
+                "{\n\t.reg .pred pa, pc;\n\t"
+                "setp.ne.b32 pa, %4, 0;\n\tsetp.ne.b32 pc, %6, 0;\n\t"
+                "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, pa;\n\t"
+                "@pc tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%5];\n\t}"
+                ::"r"(tmem_d), "l"(da), "l"(db), "r"(idesc), "r"(acc), "r"(bar ? smem_u32(bar) : 0u),
+                  "r"(bar ? 1u : 0u)
+                : "memory");
+        else
+            asm volatile(
+                "{\n\t.reg .pred pa, pc;\n\t"
+                "setp.ne.b32 pa, %4, 0;\n\tsetp.ne.b32 pc, %6, 0;\n\t"
+                "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, pa;\n\t"
+                "@pc tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%5];\n\t}"
+                ::"r"(tmem_d), "l"(da), "l"(db), "r"(idesc), "r"(acc), "r"(bar ? smem_u32(bar) : 0u),
+                  "r"(bar ? 1u : 0u)
+                : "memory");
     }
 }
 
@@ -379,15 +452,25 @@ __device__ void epilogue_loop(const TcParams& p, const CUtensorMap* tmOut, uint8
     const bool leader = (warp & 3) == 2 && lane == 0;   // warp 2 / warp 6, lane 0
     const int nchunks = p.bn >> 4;
     const uint32_t chunk_bytes = p.out_dt == BF16 ? 128u * 32u : 128u * 64u;
-    int64_t i = 0;
-    for (int64_t t = blockIdx.x; t < total; t += gridDim.x, ++i) {
-        const int buf = (int)(i % p.nbuf);
-        const uint32_t use = (uint32_t)(i / p.nbuf);     // how often this buffer was filled before
+    RingPos acc;
+    for (int64_t t = blockIdx.x; t < total; t += gridDim.x, acc.next(p.nbuf)) {
+        const int buf = acc.slot;
+        const uint32_t use = acc.phase;                  // parity of this buffer's fills before
         const uint32_t mt = fdiv((uint32_t)t, p.div_ntiles);
         const int n0 = (int)((uint32_t)t - mt * (uint32_t)p.n_tiles) * p.bn;
         uint32_t b, ho, wo;
         bool live;
-        if (p.a_mode == 2) {
+        if (p.a_mode == 2 && p.win2d) {
+            // row -> (row i, column j) of the tile's Wp-wide position grid; columns
+            // j >= TW and positions past the image are not outputs
+            b = fdiv(mt, p.div_tpi);
+            const uint32_t r = mt - b * p.div_tpi.d;
+            const uint32_t th = fdiv(r, p.div_tw2), tw = r - th * p.div_tw2.d;
+            const uint32_t i2 = fdiv((uint32_t)row, p.div_wp), j2 = (uint32_t)row - i2 * p.div_wp.d;
+            ho = th * (uint32_t)p.TR + i2;
+            wo = tw * (uint32_t)p.TW + j2;
+            live = (int)j2 < p.TW && (int)ho < p.Ho && (int)wo < p.Wo;
+        } else if (p.a_mode == 2) {
             // row -> padded position P of image b; columns x >= Wo are padding
             b = fdiv(mt, p.div_tpi);
             const uint32_t P = (mt - b * p.div_tpi.d) * (uint32_t)BM + (uint32_t)row;
@@ -478,21 +561,22 @@ struct MmaSmem {
 // costs it tens of cycles, so the operand mode is a template parameter and the tap
 // and chunk loops carry no per-k-block mode tests. WIN: a_mode 2 (windows; taps are
 // shifted windows); otherwise A comes from the ring (im2col or 2-D tiles). BRES:
-// weights resident in shared memory instead of streamed through the ring.
-template <int KIND, int WIN, bool BRES>
+// weights resident in shared memory instead of streamed through the ring. KS: MMAs
+// per k-block (swb / 32).
+template <int KIND, int WIN, bool BRES, int KS>
 __device__ __forceinline__ void mma_issuer(const TcParams& p, const MmaSmem& m, volatile int* abort_flag, int64_t total) {
-    const int ksteps = p.swb / 32;
     const int taps = p.taps, chunks = p.cin_chunks, kw = p.kw;
     const uint64_t bdesc0 = make_smem_desc(m.bres, p.swb);
     const uint32_t bstep = (p.btile_bytes >> 4);          // descriptor units per resident k-block
-    int64_t it = 0, hit = 0, i = 0;
+    const int rows = taps / kw;
+    RingPos ring, win, acc;                               // operand ring, window slots, accumulators
     if (BRES && blockIdx.x < total && !mbar_wait_bounded(m.bres_full, 0, p.wait_limit)) {
         atomicExch(p.err, 2);
         *abort_flag = 1;
     }
-    for (int64_t t = blockIdx.x; t < total && !*abort_flag; t += gridDim.x, ++i) {
-        const int buf = (int)(i % p.nbuf);
-        if (i >= p.nbuf && !mbar_wait_bounded(&m.tempty[buf], (uint32_t)(((i / p.nbuf) & 1) ^ 1), p.wait_limit)) {
+    for (int64_t t = blockIdx.x; t < total && !*abort_flag; t += gridDim.x, acc.next(p.nbuf)) {
+        const int buf = acc.slot;
+        if (acc.wrapped && !mbar_wait_bounded(&m.tempty[buf], acc.phase ^ 1u, p.wait_limit)) {
             atomicExch(p.err, 5);
             *abort_flag = 1;
             break;
@@ -504,13 +588,14 @@ __device__ __forceinline__ void mma_issuer(const TcParams& p, const MmaSmem& m, 
             const uint32_t mt = fdiv((uint32_t)t, p.div_ntiles);
             const uint32_t b = fdiv(mt, p.div_tpi);
             const uint32_t P0 = (mt - b * p.div_tpi.d) * (uint32_t)BM;
-            const uint32_t off0 = P0 - fdiv(P0, p.div_wp) * p.div_wp.d;
+            // 1-D windows start at the padded row of P0; a 2-D tile starts at position 0
+            const uint32_t off0 = p.win2d ? 0u : P0 - fdiv(P0, p.div_wp) * p.div_wp.d;
             for (int cc = 0; cc < chunks && ok; ++cc) {
-                const int hs = (int)(hit % m.HS);
-                if (!mbar_wait_bounded(&m.hfull[hs], (uint32_t)((hit / m.HS) & 1), p.wait_limit)) { ok = false; break; }
+                const int hs = win.slot;
+                if (!mbar_wait_bounded(&m.hfull[hs], win.phase, p.wait_limit)) { ok = false; break; }
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 const uint64_t adesc0 = make_smem_desc(m.halo + (uint32_t)hs * p.halo_bytes + off0 * (uint32_t)p.swb, p.swb);
-                for (int r = 0, tap = 0; r < p.taps / kw; ++r) {
+                for (int r = 0, tap = 0; r < rows; ++r) {
                     for (int s2 = 0; s2 < kw; ++s2, ++tap) {
                         const uint64_t da = adesc0 + ((uint64_t)((uint32_t)(r * p.Wp + s2) * (uint32_t)p.swb) >> 4);
                         uint64_t db;
@@ -518,27 +603,27 @@ __device__ __forceinline__ void mma_issuer(const TcParams& p, const MmaSmem& m, 
                         if (BRES) {
                             db = bdesc0 + (uint64_t)(cc * taps + tap) * bstep;
                         } else {
-                            const int st = (int)(it % m.S);
-                            if (!mbar_wait_bounded(&m.full[st], (uint32_t)((it / m.S) & 1), p.wait_limit)) { ok = false; break; }
-                            ++it;
+                            const int st = ring.slot;
+                            if (!mbar_wait_bounded(&m.full[st], ring.phase, p.wait_limit)) { ok = false; break; }
+                            ring.next(m.S);
                             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                             db = make_smem_desc(m.ring + (uint32_t)m.S * m.a_bytes + (uint32_t)st * m.b_bytes, p.swb);
                             release = &m.empty[st];
                         }
-                        umma_kblock<KIND>(d, da, db, p.idesc, (cc | tap) != 0, ksteps, release);
+                        umma_kblock_n<KIND, KS>(d, da, db, p.idesc, (cc | tap) != 0, release);
                     }
                     if (!ok) break;
                 }
                 if (!ok) break;
                 umma_commit(&m.hempty[hs]);
-                ++hit;
+                win.next(m.HS);
             }
         } else {
             for (int tap = 0; tap < taps && ok; ++tap) {
                 for (int cc = 0; cc < chunks; ++cc) {
-                    const int st = (int)(it % m.S);
-                    if (!mbar_wait_bounded(&m.full[st], (uint32_t)((it / m.S) & 1), p.wait_limit)) { ok = false; break; }
-                    ++it;
+                    const int st = ring.slot;
+                    if (!mbar_wait_bounded(&m.full[st], ring.phase, p.wait_limit)) { ok = false; break; }
+                    ring.next(m.S);
                     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                     // the tail chunk (if any) has 32-byte rows: its own swizzle, one K slice
                     const bool tail = p.tail_ch && cc == chunks - 1;
@@ -546,7 +631,8 @@ __device__ __forceinline__ void mma_issuer(const TcParams& p, const MmaSmem& m, 
                     const uint64_t da = make_smem_desc(m.ring + (uint32_t)st * m.a_bytes, swbk);
                     const uint64_t db = BRES ? bdesc0 + (uint64_t)(tap * chunks + cc) * bstep
                                              : make_smem_desc(m.ring + (uint32_t)m.S * m.a_bytes + (uint32_t)st * m.b_bytes, swbk);
-                    umma_kblock<KIND>(d, da, db, p.idesc, (tap | cc) != 0, tail ? 1 : ksteps, &m.empty[st]);
+                    if (KS == 4) umma_kblock<KIND>(d, da, db, p.idesc, (tap | cc) != 0, tail ? 1 : 4, &m.empty[st]);
+                    else umma_kblock_n<KIND, KS>(d, da, db, p.idesc, (tap | cc) != 0, &m.empty[st]);
                 }
             }
         }
@@ -554,6 +640,18 @@ __device__ __forceinline__ void mma_issuer(const TcParams& p, const MmaSmem& m, 
         umma_commit(&m.tfull[buf]);
     }
     umma_commit(m.mma_done);
+}
+
+template <int KIND, int KS>
+__device__ __forceinline__ void mma_issuer_ks(const TcParams& p, const MmaSmem& m, volatile int* abort_flag,
+                                              int64_t total) {
+    if (p.a_mode == 2) {
+        if (p.b_res) mma_issuer<KIND, 2, true, KS>(p, m, abort_flag, total);
+        else mma_issuer<KIND, 2, false, KS>(p, m, abort_flag, total);
+    } else {
+        if (p.b_res) mma_issuer<KIND, 0, true, KS>(p, m, abort_flag, total);
+        else mma_issuer<KIND, 0, false, KS>(p, m, abort_flag, total);
+    }
 }
 
 // Persistent, warp-specialized kernel. 64 + 32*EPI threads:
@@ -630,6 +728,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             // ---------------- TMA producer ----------------
             int64_t it = 0;   // global ring counter across tiles
             int64_t hit = 0;  // global window counter (a_mode 2)
+            RingPos rp, wp;   // the same as ring / window slot positions
             const bool ring_used = S > 0;     // no ring: windows + resident weights only
             if (p.b_res && blockIdx.x < total) {
                 mbar_expect_tx(bres_full, p.bres_bytes);
@@ -650,53 +749,65 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     const uint32_t r = m0 - b * p.div_hw.d;
                     ho = (int)fdiv(r, p.div_wo);
                     wo = (int)(r - (uint32_t)ho * p.div_wo.d);
+                } else if (p.a_mode == 2 && p.win2d) {
+                    b = fdiv(mt, p.div_tpi);
+                    const uint32_t r = mt - b * p.div_tpi.d;
+                    const uint32_t th = fdiv(r, p.div_tw2);
+                    ho = (int)th * p.TR;                                  // first output row
+                    wo = (int)(r - th * p.div_tw2.d) * p.TW;              // first output column
                 } else if (p.a_mode == 2) {
                     b = fdiv(mt, p.div_tpi);
                     const uint32_t P0 = (mt - b * p.div_tpi.d) * (uint32_t)BM;
                     ho = (int)fdiv(P0, p.div_wp);     // first window row (output row of P0)
                 }
                 bool stop = false;
+                // k-block coordinates, stepped in k order: windows run through the taps
+                // of one channel chunk, the ring through the chunks of one tap (r, s)
+                int tap = 0, cc = 0, r = 0, s = 0;
                 for (int kb = 0; kb < nk && !stop; ++kb) {
-                    int tap, cc;
-                    if (p.a_mode == 2) {
-                        cc = kb / p.taps; tap = kb - cc * p.taps;
-                        if (tap == 0) {
-                            const int hs = (int)(hit % HS);
-                            if (hit >= HS && !mbar_wait_bounded(&hempty[hs], (uint32_t)(((hit / HS) & 1) ^ 1), p.wait_limit)) {
-                                atomicExch(p.err, 7);
-                                *abort_flag = 1;
-                                stop = true;
-                                break;
-                            }
-                            mbar_expect_tx(&hfull[hs], p.halo_tx);
-                            tma_load_4d(halo + (uint32_t)hs * p.halo_bytes, &tmA, &hfull[hs], cc * p.ch, -p.pw,
-                                        ho - p.ph, (int)b);
-                            ++hit;
+                    if (p.a_mode == 2 && tap == 0) {
+                        const int hs = wp.slot;
+                        if (wp.wrapped && !mbar_wait_bounded(&hempty[hs], wp.phase ^ 1u, p.wait_limit)) {
+                            atomicExch(p.err, 7);
+                            *abort_flag = 1;
+                            stop = true;
+                            break;
                         }
-                    } else {
-                        tap = kb / p.cin_chunks; cc = kb - tap * p.cin_chunks;
+                        mbar_expect_tx(&hfull[hs], p.halo_tx);
+                        tma_load_4d(halo + (uint32_t)hs * p.halo_bytes, &tmA, &hfull[hs], cc * p.ch, wo - p.pw,
+                                    ho - p.ph, (int)b);
+                        wp.next(HS);
+                        ++hit;
                     }
-                    if (!ring_used) continue;
-                    const int st = (int)(it % S);
-                    if (it >= S && !mbar_wait_bounded(&empty[st], (uint32_t)(((it / S) & 1) ^ 1), p.wait_limit)) {
-                        atomicExch(p.err, 1);
-                        *abort_flag = 1;
-                        break;
+                    if (ring_used) {
+                        const int st = rp.slot;
+                        if (rp.wrapped && !mbar_wait_bounded(&empty[st], rp.phase ^ 1u, p.wait_limit)) {
+                            atomicExch(p.err, 1);
+                            *abort_flag = 1;
+                            break;
+                        }
+                        const uint32_t sa = ring + (uint32_t)st * a_bytes;
+                        const uint32_t sb = ring + (uint32_t)S * a_bytes + (uint32_t)st * b_bytes;
+                        rp.next(S);
+                        ++it;
+                        const bool tail = p.tail_ch && cc == p.cin_chunks - 1;
+                        mbar_expect_tx(&full[st], tail ? p.tail_a_bytes + (p.b_res ? 0u : p.tail_b_bytes) : a_bytes + b_bytes);
+                        const CUtensorMap* mA = tail ? &tmA2 : &tmA;
+                        if (p.a_mode == 0) {
+                            tma_load_im2col_4d(sa, mA, &full[st], cc * p.ch, wo * p.sw - p.pw, ho * p.sh - p.ph,
+                                               (int)b, (uint16_t)(s * p.dw), (uint16_t)(r * p.dh));
+                        } else if (p.a_mode == 1) {
+                            tma_load_2d(sa, mA, &full[st], cc * p.ch, (int)m0);
+                        }
+                        if (!p.b_res) tma_load_3d(sb, tail ? &tmB2 : &tmB, &full[st], cc * p.ch, tap, n0);
                     }
-                    const uint32_t sa = ring + (uint32_t)st * a_bytes;
-                    const uint32_t sb = ring + (uint32_t)S * a_bytes + (uint32_t)st * b_bytes;
-                    ++it;
-                    const bool tail = p.tail_ch && cc == p.cin_chunks - 1;
-                    mbar_expect_tx(&full[st], tail ? p.tail_a_bytes + (p.b_res ? 0u : p.tail_b_bytes) : a_bytes + b_bytes);
-                    const CUtensorMap* mA = tail ? &tmA2 : &tmA;
-                    if (p.a_mode == 0) {
-                        const int r = tap / p.kw, s = tap - r * p.kw;
-                        tma_load_im2col_4d(sa, mA, &full[st], cc * p.ch, wo * p.sw - p.pw, ho * p.sh - p.ph,
-                                           (int)b, (uint16_t)(s * p.dw), (uint16_t)(r * p.dh));
-                    } else if (p.a_mode == 1) {
-                        tma_load_2d(sa, mA, &full[st], cc * p.ch, (int)m0);
+                    if (p.a_mode == 2) {
+                        if (++tap == p.taps) { tap = 0; ++cc; }
+                    } else if (++cc == p.cin_chunks) {
+                        cc = 0;
+                        ++tap;
+                        if (++s == p.kw) { s = 0; ++r; }
                     }
-                    if (!p.b_res) tma_load_3d(sb, tail ? &tmB2 : &tmB, &full[st], cc * p.ch, tap, n0);
                 }
             }
             // Drain: the last use of every slot must have landed before the CTA exits.
@@ -712,13 +823,9 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             // ---------------- MMA issuer ----------------
             MmaSmem m{ring, halo, bres, a_bytes, b_bytes, S, HS, full, empty, tfull, tempty, hfull, hempty, bres_full,
                       mma_done, tmem};
-            if (p.a_mode == 2) {
-                if (p.b_res) mma_issuer<KIND, 2, true>(p, m, abort_flag, total);
-                else mma_issuer<KIND, 2, false>(p, m, abort_flag, total);
-            } else {
-                if (p.b_res) mma_issuer<KIND, 0, true>(p, m, abort_flag, total);
-                else mma_issuer<KIND, 0, false>(p, m, abort_flag, total);
-            }
+            if (p.swb == 32) mma_issuer_ks<KIND, 1>(p, m, abort_flag, total);
+            else if (p.swb == 64) mma_issuer_ks<KIND, 2>(p, m, abort_flag, total);
+            else mma_issuer_ks<KIND, 4>(p, m, abort_flag, total);
         }
         __syncwarp();
     } else {
@@ -923,14 +1030,27 @@ void launch_conv_tc(const ConvArgs& a, int op_dt, int* err, cudaStream_t s) {
     const uint32_t fixed = 1024 + kBarrierBytes + 1024 + (tma_store ? staging : 0u);   // alignment, barriers, reserve
     const uint32_t btile = (uint32_t)bn * swb;
     const uint32_t bres_all = (uint32_t)nk * btile;
-    const uint32_t win_tx = (uint32_t)NR * (uint32_t)Wp * (uint32_t)swb;
-    const uint32_t win_slot = (win_tx + 1023u) & ~1023u;
-    const bool window_ok = !one && a.sh == 1 && a.sw == 1 && a.dh == 1 && a.dw == 1 && Wp <= 256 && NR <= 256 &&
-                           Wo == Wp - a.kw + 1;
-    struct Cand { int mode, bres, ctas, stages; };
+    const bool s1 = !one && a.sh == 1 && a.sw == 1 && a.dh == 1 && a.dw == 1;
+    // 2-D window tiles: 8 output rows x (16 - kw + 1) columns on a 16-position pitch;
+    // a tap's A operand is the window shifted by r*16 + s rows, which for the last
+    // (non-output) positions of the tile reaches up to kw - 1 rows past the window's
+    // NR*16, so the slot has room for them (never written, never stored).
+    constexpr int kPitch2 = 16;
+    const int TR2 = BM / kPitch2, TW2 = kPitch2 - (a.kw - 1), NR2 = TR2 + a.kh - 1;
+    static int win2d_env = -1, win_ring = -1;
+    if (win2d_env < 0) { const char* e = std::getenv("PDEFA_WIN2D"); win2d_env = e ? std::atoi(e) : 0; }
+    if (win_ring < 0) { const char* e = std::getenv("PDEFA_WIN_RING"); win_ring = e ? std::max(2, std::min(kMaxHalo, std::atoi(e))) : 2; }
+    const bool win2d = win2d_env > 0 && s1 && TW2 >= 8 && Wo > 2 * TW2 && !tail_ch && (swb < 128 || win2d_env > 1);
+    const int wWp = win2d ? kPitch2 : Wp, wNR = win2d ? NR2 : NR;
+    const uint32_t win_rows = win2d ? (uint32_t)std::max(NR2 * kPitch2, BM + (a.kh - 1) * kPitch2 + a.kw - 1)
+                                    : (uint32_t)(NR * Wp);
+    const uint32_t win_tx = (uint32_t)wNR * (uint32_t)wWp * (uint32_t)swb;
+    const uint32_t win_slot = (win_rows * (uint32_t)swb + 1023u) & ~1023u;
+    const bool window_ok = win2d || (s1 && Wp <= 256 && NR <= 256 && Wo == Wp - a.kw + 1);
+    struct Cand { int mode, bres, ctas, stages, hs; };
     // most CTAs (<= max_ctas) a configuration fits, with its ring depth; ctas 0 = none
     auto fit = [&](int mode, int bres) {
-        Cand c{mode, bres, 0, 0};
+        Cand c{mode, bres, 0, 0, mode == 2 ? 2 : 0};
         if (bres && (bn != a.cout || bres_all > 200u * 1024u || tail_ch)) return c;
         const uint32_t a_st = mode == 2 ? 0u : (uint32_t)BM * swb;
         const uint32_t b_st = bres ? 0u : btile;
@@ -943,17 +1063,21 @@ void launch_conv_tc(const ConvArgs& a, int op_dt, int* err, cudaStream_t s) {
             if (room(n) >= 0 && room(n) >= (int64_t)min_st * st) {
                 c.ctas = n;
                 c.stages = st == 0 ? 0 : (int)std::min<int64_t>(12, room(n) / st);
+                // windows without a ring (resident weights): spare room deepens the
+                // window ring, so the producer runs further ahead of the MMAs
+                if (mode == 2 && st == 0 && win_ring > 2)
+                    c.hs = 2 + (int)std::min<int64_t>(win_ring - 2, room(n) / win_slot);
                 return c;
             }
         }
         return c;
     };
-    Cand best{-1, 0, 0, 0};
+    Cand best{-1, 0, 0, 0, 0};
     if (one && pixel_dense(a.in)) {
         const Cand s0 = fit(1, 0), s1 = fit(1, 1);
         best = s1.ctas > 0 && s1.ctas >= s0.ctas ? s1 : s0;
     } else {
-        if (window_ok && swb < 128 && !tail_ch) {
+        if (window_ok && (swb < 128 || win2d) && !tail_ch) {
             const Cand w1 = fit(2, 1), w0 = fit(2, 0);
             if (w1.ctas > 0) best = w1;
             else if (w0.ctas > 0) best = w0;
@@ -979,10 +1103,12 @@ void launch_conv_tc(const ConvArgs& a, int op_dt, int* err, cudaStream_t s) {
     const uint32_t stage2 = p.stage_a_bytes + p.stage_b_bytes;
     p.btile_bytes = btile;
     p.bres_bytes = p.b_res ? bres_all : 0u;
-    p.hstages = p.a_mode == 2 ? 2 : 0;
+    p.hstages = p.a_mode == 2 ? best.hs : 0;
     const uint32_t halo_tx = p.a_mode == 2 ? win_tx : 0u;
     const uint32_t halo_slot = p.a_mode == 2 ? win_slot : 0u;
-    p.Wp = Wp; p.NR = NR;
+    p.Wp = p.a_mode == 2 ? wWp : Wp;
+    p.NR = p.a_mode == 2 ? wNR : NR;
+    p.win2d = p.a_mode == 2 && win2d;
     p.halo_tx = halo_tx;
     p.halo_bytes = halo_slot;
     p.stages = stages;
@@ -1033,7 +1159,7 @@ void launch_conv_tc(const ConvArgs& a, int op_dt, int* err, cudaStream_t s) {
         cuuint64_t dims[4] = {(cuuint64_t)a.cin, (cuuint64_t)a.in.shape[2], (cuuint64_t)a.in.shape[1], (cuuint64_t)a.batch};
         cuuint64_t strides[3] = {(cuuint64_t)(a.in.stride[2] * esz), (cuuint64_t)(a.in.stride[1] * esz),
                                  (cuuint64_t)(a.in.img_stride * esz)};
-        cuuint32_t box[4] = {(cuuint32_t)ch, (cuuint32_t)Wp, (cuuint32_t)NR, 1};
+        cuuint32_t box[4] = {(cuuint32_t)ch, (cuuint32_t)p.Wp, (cuuint32_t)p.NR, 1};
         cuuint32_t es[4] = {1, 1, 1, 1};
         CUresult r = g_tiled(&tmA, tdt, 4, const_cast<void*>(a.in.ptr), dims, strides, box, es,
                              CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle_of(swb), CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -1070,7 +1196,15 @@ void launch_conv_tc(const ConvArgs& a, int op_dt, int* err, cudaStream_t s) {
         if (!tail_ch) { tmA2 = tmA; tmB2 = tmB; }   // unused
     }
     p.n_tiles = a.cout / bn;
-    if (p.a_mode == 2) {
+    if (p.win2d) {
+        p.TR = TR2; p.TW = TW2;
+        p.tiles_w = (Wo + TW2 - 1) / TW2;
+        const uint32_t tpi = (uint32_t)((Ho + TR2 - 1) / TR2) * (uint32_t)p.tiles_w;
+        p.div_tpi = make_fastdiv(tpi);
+        p.div_tw2 = make_fastdiv((uint32_t)p.tiles_w);
+        p.div_wp = make_fastdiv((uint32_t)kPitch2);
+        p.m_tiles = (int64_t)tpi * a.batch;
+    } else if (p.a_mode == 2) {
         // tiles never straddle images: positions P = y*Wp + x of one image, Ho*Wp of them
         p.Q = (uint32_t)Ho * (uint32_t)Wp;
         const uint32_t tpi = (p.Q + BM - 1) / BM;
