@@ -117,8 +117,10 @@ ENGINE_API EngineStatus pdefa_decode_yolo(const float* preds, int32_t preds_on_d
 
 /* Device-side variant of pdefa_decode_yolo for callers that manage memory: all
  * pointers are device pointers on the current device (d_metas may be NULL), work is
- * caller-provided scratch of pdefa_decode_work_bytes(batch, anchors) bytes, and the
- * call only enqueues one kernel on `stream` (no allocation, no synchronisation). */
+ * caller-provided scratch of pdefa_decode_work_bytes(batch, anchors) bytes (16-byte
+ * aligned, as cudaMalloc returns; d_dets 8-byte aligned, else ENGINE_ERR_INVALID_ARG),
+ * and the call only enqueues one kernel on `stream` (no allocation, no
+ * synchronisation). */
 ENGINE_API size_t       pdefa_decode_work_bytes(int64_t batch, int64_t anchors);
 ENGINE_API EngineStatus pdefa_decode_yolo_device(const float* d_preds, int64_t batch, int64_t channels,
                                                  int64_t anchors, const PdefaPreprocessMeta* d_metas,

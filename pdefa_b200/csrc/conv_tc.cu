@@ -38,7 +38,7 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int kMaxBuf = 4;                        // TMEM accumulator buffers at most
-constexpr int kMaxHalo = 8;                       // window slots (a_mode 2)
+constexpr int kMaxHalo = 4;                       // window slots (a_mode 2)
 constexpr uint32_t kBarrierBytes = 512;           // mbarriers, TMEM slot, abort flag
 // Epilogue warps per CTA: EPI = 4 (one group, one warp per TMEM lane quarter) or 8
 // (two groups that split the columns). Threads: producer warp, MMA warp, epilogue.
@@ -111,12 +111,6 @@ struct TcParams {
     // tensor maps (tmA2 / tmB2), instead of a full chunk padded with zeros.
     int tail_ch;
     uint32_t tail_a_bytes, tail_b_bytes;
-    // win2d (a_mode 2): 2-D output tiles of TR rows x TW columns on a pitch of Wp
-    // positions per row (Wp = TW + kw - 1, TR * Wp = 128), so a window is NR = TR +
-    // kh - 1 rows of Wp positions instead of whole padded image rows; tiles
-    // (image, tile row, tile column), tiles_w of them per tile row.
-    int win2d, TR, TW, tiles_w;
-    FastDiv div_tw2;
 };
 
 __device__ __forceinline__ uint64_t make_smem_desc(uint32_t addr, int swb) {
@@ -460,17 +454,7 @@ __device__ void epilogue_loop(const TcParams& p, const CUtensorMap* tmOut, uint8
         const int n0 = (int)((uint32_t)t - mt * (uint32_t)p.n_tiles) * p.bn;
         uint32_t b, ho, wo;
         bool live;
-        if (p.a_mode == 2 && p.win2d) {
-            // row -> (row i, column j) of the tile's Wp-wide position grid; columns
-            // j >= TW and positions past the image are not outputs
-            b = fdiv(mt, p.div_tpi);
-            const uint32_t r = mt - b * p.div_tpi.d;
-            const uint32_t th = fdiv(r, p.div_tw2), tw = r - th * p.div_tw2.d;
-            const uint32_t i2 = fdiv((uint32_t)row, p.div_wp), j2 = (uint32_t)row - i2 * p.div_wp.d;
-            ho = th * (uint32_t)p.TR + i2;
-            wo = tw * (uint32_t)p.TW + j2;
-            live = (int)j2 < p.TW && (int)ho < p.Ho && (int)wo < p.Wo;
-        } else if (p.a_mode == 2) {
+        if (p.a_mode == 2) {
             // row -> padded position P of image b; columns x >= Wo are padding
             b = fdiv(mt, p.div_tpi);
             const uint32_t P = (mt - b * p.div_tpi.d) * (uint32_t)BM + (uint32_t)row;
@@ -588,8 +572,7 @@ __device__ __forceinline__ void mma_issuer(const TcParams& p, const MmaSmem& m, 
             const uint32_t mt = fdiv((uint32_t)t, p.div_ntiles);
             const uint32_t b = fdiv(mt, p.div_tpi);
             const uint32_t P0 = (mt - b * p.div_tpi.d) * (uint32_t)BM;
-            // 1-D windows start at the padded row of P0; a 2-D tile starts at position 0
-            const uint32_t off0 = p.win2d ? 0u : P0 - fdiv(P0, p.div_wp) * p.div_wp.d;
+            const uint32_t off0 = P0 - fdiv(P0, p.div_wp) * p.div_wp.d;
             for (int cc = 0; cc < chunks && ok; ++cc) {
                 const int hs = win.slot;
                 if (!mbar_wait_bounded(&m.hfull[hs], win.phase, p.wait_limit)) { ok = false; break; }
@@ -749,12 +732,6 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     const uint32_t r = m0 - b * p.div_hw.d;
                     ho = (int)fdiv(r, p.div_wo);
                     wo = (int)(r - (uint32_t)ho * p.div_wo.d);
-                } else if (p.a_mode == 2 && p.win2d) {
-                    b = fdiv(mt, p.div_tpi);
-                    const uint32_t r = mt - b * p.div_tpi.d;
-                    const uint32_t th = fdiv(r, p.div_tw2);
-                    ho = (int)th * p.TR;                                  // first output row
-                    wo = (int)(r - th * p.div_tw2.d) * p.TW;              // first output column
                 } else if (p.a_mode == 2) {
                     b = fdiv(mt, p.div_tpi);
                     const uint32_t P0 = (mt - b * p.div_tpi.d) * (uint32_t)BM;
@@ -774,7 +751,7 @@ conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                             break;
                         }
                         mbar_expect_tx(&hfull[hs], p.halo_tx);
-                        tma_load_4d(halo + (uint32_t)hs * p.halo_bytes, &tmA, &hfull[hs], cc * p.ch, wo - p.pw,
+                        tma_load_4d(halo + (uint32_t)hs * p.halo_bytes, &tmA, &hfull[hs], cc * p.ch, -p.pw,
                                     ho - p.ph, (int)b);
                         wp.next(HS);
                         ++hit;
@@ -1030,27 +1007,14 @@ void launch_conv_tc(const ConvArgs& a, int op_dt, int* err, cudaStream_t s) {
     const uint32_t fixed = 1024 + kBarrierBytes + 1024 + (tma_store ? staging : 0u);   // alignment, barriers, reserve
     const uint32_t btile = (uint32_t)bn * swb;
     const uint32_t bres_all = (uint32_t)nk * btile;
-    const bool s1 = !one && a.sh == 1 && a.sw == 1 && a.dh == 1 && a.dw == 1;
-    // 2-D window tiles: 8 output rows x (16 - kw + 1) columns on a 16-position pitch;
-    // a tap's A operand is the window shifted by r*16 + s rows, which for the last
-    // (non-output) positions of the tile reaches up to kw - 1 rows past the window's
-    // NR*16, so the slot has room for them (never written, never stored).
-    constexpr int kPitch2 = 16;
-    const int TR2 = BM / kPitch2, TW2 = kPitch2 - (a.kw - 1), NR2 = TR2 + a.kh - 1;
-    static int win2d_env = -1, win_ring = -1;
-    if (win2d_env < 0) { const char* e = std::getenv("PDEFA_WIN2D"); win2d_env = e ? std::atoi(e) : 0; }
-    if (win_ring < 0) { const char* e = std::getenv("PDEFA_WIN_RING"); win_ring = e ? std::max(2, std::min(kMaxHalo, std::atoi(e))) : 2; }
-    const bool win2d = win2d_env > 0 && s1 && TW2 >= 8 && Wo > 2 * TW2 && !tail_ch && (swb < 128 || win2d_env > 1);
-    const int wWp = win2d ? kPitch2 : Wp, wNR = win2d ? NR2 : NR;
-    const uint32_t win_rows = win2d ? (uint32_t)std::max(NR2 * kPitch2, BM + (a.kh - 1) * kPitch2 + a.kw - 1)
-                                    : (uint32_t)(NR * Wp);
-    const uint32_t win_tx = (uint32_t)wNR * (uint32_t)wWp * (uint32_t)swb;
-    const uint32_t win_slot = (win_rows * (uint32_t)swb + 1023u) & ~1023u;
-    const bool window_ok = win2d || (s1 && Wp <= 256 && NR <= 256 && Wo == Wp - a.kw + 1);
-    struct Cand { int mode, bres, ctas, stages, hs; };
+    const uint32_t win_tx = (uint32_t)NR * (uint32_t)Wp * (uint32_t)swb;
+    const uint32_t win_slot = (win_tx + 1023u) & ~1023u;
+    const bool window_ok = !one && a.sh == 1 && a.sw == 1 && a.dh == 1 && a.dw == 1 && Wp <= 256 && NR <= 256 &&
+                           Wo == Wp - a.kw + 1;
+    struct Cand { int mode, bres, ctas, stages; };
     // most CTAs (<= max_ctas) a configuration fits, with its ring depth; ctas 0 = none
     auto fit = [&](int mode, int bres) {
-        Cand c{mode, bres, 0, 0, mode == 2 ? 2 : 0};
+        Cand c{mode, bres, 0, 0};
         if (bres && (bn != a.cout || bres_all > 200u * 1024u || tail_ch)) return c;
         const uint32_t a_st = mode == 2 ? 0u : (uint32_t)BM * swb;
         const uint32_t b_st = bres ? 0u : btile;
@@ -1063,21 +1027,17 @@ void launch_conv_tc(const ConvArgs& a, int op_dt, int* err, cudaStream_t s) {
             if (room(n) >= 0 && room(n) >= (int64_t)min_st * st) {
                 c.ctas = n;
                 c.stages = st == 0 ? 0 : (int)std::min<int64_t>(12, room(n) / st);
-                // windows without a ring (resident weights): spare room deepens the
-                // window ring, so the producer runs further ahead of the MMAs
-                if (mode == 2 && st == 0 && win_ring > 2)
-                    c.hs = 2 + (int)std::min<int64_t>(win_ring - 2, room(n) / win_slot);
                 return c;
             }
         }
         return c;
     };
-    Cand best{-1, 0, 0, 0, 0};
+    Cand best{-1, 0, 0, 0};
     if (one && pixel_dense(a.in)) {
         const Cand s0 = fit(1, 0), s1 = fit(1, 1);
         best = s1.ctas > 0 && s1.ctas >= s0.ctas ? s1 : s0;
     } else {
-        if (window_ok && (swb < 128 || win2d) && !tail_ch) {
+        if (window_ok && swb < 128 && !tail_ch) {
             const Cand w1 = fit(2, 1), w0 = fit(2, 0);
             if (w1.ctas > 0) best = w1;
             else if (w0.ctas > 0) best = w0;
@@ -1103,12 +1063,10 @@ void launch_conv_tc(const ConvArgs& a, int op_dt, int* err, cudaStream_t s) {
     const uint32_t stage2 = p.stage_a_bytes + p.stage_b_bytes;
     p.btile_bytes = btile;
     p.bres_bytes = p.b_res ? bres_all : 0u;
-    p.hstages = p.a_mode == 2 ? best.hs : 0;
+    p.hstages = p.a_mode == 2 ? 2 : 0;
     const uint32_t halo_tx = p.a_mode == 2 ? win_tx : 0u;
     const uint32_t halo_slot = p.a_mode == 2 ? win_slot : 0u;
-    p.Wp = p.a_mode == 2 ? wWp : Wp;
-    p.NR = p.a_mode == 2 ? wNR : NR;
-    p.win2d = p.a_mode == 2 && win2d;
+    p.Wp = Wp; p.NR = NR;
     p.halo_tx = halo_tx;
     p.halo_bytes = halo_slot;
     p.stages = stages;
@@ -1159,7 +1117,7 @@ void launch_conv_tc(const ConvArgs& a, int op_dt, int* err, cudaStream_t s) {
         cuuint64_t dims[4] = {(cuuint64_t)a.cin, (cuuint64_t)a.in.shape[2], (cuuint64_t)a.in.shape[1], (cuuint64_t)a.batch};
         cuuint64_t strides[3] = {(cuuint64_t)(a.in.stride[2] * esz), (cuuint64_t)(a.in.stride[1] * esz),
                                  (cuuint64_t)(a.in.img_stride * esz)};
-        cuuint32_t box[4] = {(cuuint32_t)ch, (cuuint32_t)p.Wp, (cuuint32_t)p.NR, 1};
+        cuuint32_t box[4] = {(cuuint32_t)ch, (cuuint32_t)Wp, (cuuint32_t)NR, 1};
         cuuint32_t es[4] = {1, 1, 1, 1};
         CUresult r = g_tiled(&tmA, tdt, 4, const_cast<void*>(a.in.ptr), dims, strides, box, es,
                              CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle_of(swb), CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -1196,15 +1154,7 @@ void launch_conv_tc(const ConvArgs& a, int op_dt, int* err, cudaStream_t s) {
         if (!tail_ch) { tmA2 = tmA; tmB2 = tmB; }   // unused
     }
     p.n_tiles = a.cout / bn;
-    if (p.win2d) {
-        p.TR = TR2; p.TW = TW2;
-        p.tiles_w = (Wo + TW2 - 1) / TW2;
-        const uint32_t tpi = (uint32_t)((Ho + TR2 - 1) / TR2) * (uint32_t)p.tiles_w;
-        p.div_tpi = make_fastdiv(tpi);
-        p.div_tw2 = make_fastdiv((uint32_t)p.tiles_w);
-        p.div_wp = make_fastdiv((uint32_t)kPitch2);
-        p.m_tiles = (int64_t)tpi * a.batch;
-    } else if (p.a_mode == 2) {
+    if (p.a_mode == 2) {
         // tiles never straddle images: positions P = y*Wp + x of one image, Ho*Wp of them
         p.Q = (uint32_t)Ho * (uint32_t)Wp;
         const uint32_t tpi = (p.Q + BM - 1) / BM;

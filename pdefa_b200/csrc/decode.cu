@@ -19,6 +19,7 @@
 #include <cfloat>
 #include <atomic>
 #include <climits>
+#include <cstddef>
 
 #include <mutex>
 
@@ -32,6 +33,7 @@ namespace pb {
 namespace {
 
 constexpr int kThreads = 1024;
+constexpr int kWarps = kThreads / 32;
 constexpr int kMaxKeys = 16384;
 constexpr int kMaxClasses = 1024;
 constexpr int kSub = 256;          // boxes settled per greedy sub-block
@@ -50,6 +52,10 @@ struct Det {
     int32_t reserved;
 };
 static_assert(sizeof(Det) == 48, "Det must match PdefaDetection");
+// the NMS reads a record's tail (conf, cls, anchor, reserved) as one 16-byte load
+static_assert(offsetof(Det, conf) == 32 && offsetof(Det, cls) == 36 && offsetof(Det, anchor) == 40 &&
+                  offsetof(Det, reserved) == 44,
+              "Det tail layout");
 
 __device__ __forceinline__ uint32_t desc_key(float f) {
     uint32_t u = __float_as_uint(f == 0.0f ? 0.0f : f);       // -0.0 orders as +0.0
@@ -104,8 +110,11 @@ __device__ __forceinline__ double clamp_ref(double v, double hi) {
 // Bitonic sort of np (a power of two) keys, ascending. Strides of 128 and more run
 // in shared memory with a barrier per pass (every thread takes whole compare-exchange
 // pairs); the strides below 128 of every stage run in registers: warp w holds
-// 128-key groups g = w, w + 32, ... as 4 consecutive keys per lane, strides 1 and 2
-// within a lane, 4 ... 64 across lanes by shuffles, with one barrier per stage.
+// 128-key groups g = w, w + kWarps, ... with key g*128 + 32*r + lane in register r of
+// its lane (r = 0..3), so every warp load and store of the group touches consecutive
+// keys (no bank conflicts: the sort moves its keys through shared memory once per
+// stage and is bound by that bandwidth); strides 32 and 64 pair registers of one
+// lane, strides 1 ... 16 pair lanes by shuffles, with one barrier per stage.
 __device__ __forceinline__ void cmp_swap_reg(unsigned long long& lo, unsigned long long& hi, bool asc) {
     if ((lo > hi) == asc) { const unsigned long long t = lo; lo = hi; hi = t; }
 }
@@ -129,38 +138,36 @@ __device__ void bitonic_sort(unsigned long long* keys, int np) {
         return;
     }
     const int half = np >> 1;
-    // stages k (sequence length): register passes for strides min(k/2, 64) ... 1
+    // stage k (sequence length): register passes for strides min(k/2, 64) ... 1
     auto reg_passes = [&](int k) {
-        for (int g = warp; g < (np >> 7); g += kThreads / 32) {
-            const int e0 = g * 128 + lane * 4;          // this lane's first key
-            unsigned long long v[4];
-#pragma unroll
-            for (int r = 0; r < 4; ++r) v[r] = keys[e0 + r];
+        for (int g = warp; g < (np >> 7); g += kWarps) {
+            unsigned long long* const base = keys + g * 128 + lane;
+            unsigned long long v0 = base[0], v1 = base[32], v2 = base[64], v3 = base[96];
+            const int e0 = g * 128 + lane;       // key index of v0; v_r is e0 + 32 r
             for (int j = (k >> 1) < 64 ? (k >> 1) : 64; j > 0; j >>= 1) {
-                if (j >= 4) {
-                    const int lx = j >> 2;              // partner lane distance
-#pragma unroll
-                    for (int r = 0; r < 4; ++r) {
-                        const int e = e0 + r;
-                        const unsigned long long o = __shfl_xor_sync(0xffffffffu, v[r], lx);
-                        const bool asc = (e & k) == 0;
-                        const bool lower = (e & j) == 0;
-                        // the lower element keeps the smaller key when ascending
-                        const bool take_min = lower == asc;
-                        v[r] = take_min ? (o < v[r] ? o : v[r]) : (o > v[r] ? o : v[r]);
-                    }
-                } else if (j == 2) {
-                    const bool asc0 = (e0 & k) == 0;     // keys e0 .. e0+3 share bit log2(k) >= 2
-                    cmp_swap_reg(v[0], v[2], asc0);
-                    cmp_swap_reg(v[1], v[3], asc0);
+                if (j == 64) {
+                    // pairs (v0, v2), (v1, v3); k >= 128, so bit k is shared by all four
+                    const bool asc = (e0 & k) == 0;
+                    cmp_swap_reg(v0, v2, asc);
+                    cmp_swap_reg(v1, v3, asc);
+                } else if (j == 32) {
+                    cmp_swap_reg(v0, v1, (e0 & k) == 0);
+                    cmp_swap_reg(v2, v3, ((e0 + 64) & k) == 0);
                 } else {
-                    // stride 1: for k = 2 the pairs (0, 1) and (2, 3) sort in opposite directions
-                    cmp_swap_reg(v[0], v[1], (e0 & k) == 0);
-                    cmp_swap_reg(v[2], v[3], ((e0 + 2) & k) == 0);
+                    // partner lane ^ j holds the other key of each pair
+                    const bool lower = (lane & j) == 0;
+                    // the lower element keeps the smaller key when ascending
+                    auto step = [&](unsigned long long x, int e) {
+                        const unsigned long long o = __shfl_xor_sync(0xffffffffu, x, j);
+                        return (lower == ((e & k) == 0)) ? (o < x ? o : x) : (o > x ? o : x);
+                    };
+                    v0 = step(v0, e0);
+                    v1 = step(v1, e0 + 32);
+                    v2 = step(v2, e0 + 64);
+                    v3 = step(v3, e0 + 96);
                 }
             }
-#pragma unroll
-            for (int r = 0; r < 4; ++r) keys[e0 + r] = v[r];
+            base[0] = v0; base[32] = v1; base[64] = v2; base[96] = v3;
         }
         __syncthreads();
     };
@@ -236,42 +243,80 @@ __global__ void __launch_bounds__(kThreads, 1) decode_nms_kernel(DecodeArgs p) {
     if (tid == 0) { s_n = 0; s_kept = 0; }
     __syncthreads();
 
-    // ---- 1. ordered compaction of the candidates marked by decode_candidates_kernel ----
-    // Records sit at their anchor slot; candidate k moves to slot k <= its anchor. Each
-    // chunk reads all its records before the scan's barriers and writes after them,
-    // and later chunks only read slots beyond every slot written so far.
-    for (int64_t a0 = 0; a0 < A; a0 += kThreads) {
-        const int64_t a = a0 + tid;
-        bool flag = false;
-        Det d;
-        if (a < A) {
-            d = cand[a];
-            flag = d.reserved != 0;
-        }
-        const unsigned bal = __ballot_sync(0xffffffffu, flag);
-        if (lane == 0) warp_tot[warp] = __popc(bal);
+    // ---- 1. the candidates marked by decode_candidates_kernel, in anchor order ----
+    // keys[k] = anchor of candidate k (records stay at their anchor slots). Every
+    // thread reads the 16-byte tails (conf, cls, anchor, flag) of kChunks records of a
+    // round before one block scan of all their flags, so a round costs one record
+    // latency and three barriers for kChunks * kThreads anchors. The first call also
+    // records each class's first candidate.
+    constexpr int kChunks = 4;
+    __shared__ int chunk_tot[kChunks * kWarps];
+    auto compact = [&](bool classes) {
+        if (tid == 0) s_n = 0;
         __syncthreads();
-        if (warp == 0) {
-            int v = warp_tot[lane];
-            for (int o = 1; o < 32; o <<= 1) {
-                const int t = __shfl_up_sync(0xffffffffu, v, o);
-                if (lane >= o) v += t;
+        for (int64_t a0 = 0; a0 < A; a0 += (int64_t)kChunks * kThreads) {
+            bool flag[kChunks];
+            int cls[kChunks];
+            unsigned bal[kChunks];
+#pragma unroll
+            for (int c = 0; c < kChunks; ++c) {
+                const int64_t a = a0 + c * kThreads + tid;
+                flag[c] = false;
+                cls[c] = 0;
+                if (a < A) {
+                    const int4 tail = *reinterpret_cast<const int4*>(reinterpret_cast<const char*>(cand + a) + 32);
+                    flag[c] = tail.w != 0;        // reserved
+                    cls[c] = tail.y;
+                }
             }
-            warp_tot[lane] = v;  // inclusive
-        }
-        __syncthreads();
-        if (flag) {
-            const int k = s_n + (warp ? warp_tot[warp - 1] : 0) + __popc(bal & ((1u << lane) - 1u));
-            if (k < kMaxKeys) {
-                d.reserved = 0;
-                cand[k] = d;
-                atomicMin(&first[d.cls], k);
+#pragma unroll
+            for (int c = 0; c < kChunks; ++c) {
+                bal[c] = __ballot_sync(0xffffffffu, flag[c]);
+                if (lane == 0) chunk_tot[c * kWarps + warp] = __popc(bal[c]);
             }
+            __syncthreads();
+            if (warp == 0) {
+                // inclusive scan over (chunk, warp) in anchor order, kChunks * kWarps <= 64 counts
+                constexpr int kPer = (kChunks * kWarps + 31) / 32;
+                int v[kPer], tot = 0;
+#pragma unroll
+                for (int q = 0; q < kPer; ++q) {
+                    const int e = lane * kPer + q;
+                    v[q] = e < kChunks * kWarps ? chunk_tot[e] : 0;
+                    tot += v[q];
+                }
+                int incl = tot;
+                for (int o = 1; o < 32; o <<= 1) {
+                    const int t = __shfl_up_sync(0xffffffffu, incl, o);
+                    if (lane >= o) incl += t;
+                }
+                int run = incl - tot;
+#pragma unroll
+                for (int q = 0; q < kPer; ++q) {
+                    const int e = lane * kPer + q;
+                    run += v[q];
+                    if (e < kChunks * kWarps) chunk_tot[e] = run;
+                }
+            }
+            __syncthreads();
+            const int base = s_n;
+#pragma unroll
+            for (int c = 0; c < kChunks; ++c) {
+                if (flag[c]) {
+                    const int e = c * kWarps + warp;
+                    const int k = base + (e ? chunk_tot[e - 1] : 0) + __popc(bal[c] & ((1u << lane) - 1u));
+                    if (k < kMaxKeys) {
+                        keys[k] = (unsigned long long)(a0 + c * kThreads + tid);
+                        if (classes) atomicMin(&first[cls[c]], k);
+                    }
+                }
+            }
+            __syncthreads();
+            if (tid == 0) s_n = base + chunk_tot[kChunks * kWarps - 1];
+            __syncthreads();
         }
-        __syncthreads();
-        if (tid == 0) s_n += warp_tot[31];
-        __syncthreads();
-    }
+    };
+    compact(true);
     const int n = s_n;
     if (n > kMaxKeys) {
         if (tid == 0) p.counts[b] = -1;
@@ -293,17 +338,18 @@ __global__ void __launch_bounds__(kThreads, 1) decode_nms_kernel(DecodeArgs p) {
     // ---- 3. the output order: (conf desc, class group, index) ----
     // The greedy pass below settles boxes in this order and stops at max_det kept, so
     // with many candidates it usually needs only a prefix of the order: segment 0 is
-    // the prefix {conf key <= T}, T the conf key of the R-th box (radix select over the
-    // 32-bit conf keys; ties at T keep it a prefix); only when the pass runs out of it
-    // before max_det boxes are kept is segment 1, the rest, sorted and the pass
-    // continued on it. Without selection segment 0 is all n boxes.
+    // the prefix {key <= T}, T the R-th smallest key (radix select over the whole
+    // keys, which are distinct: exactly R boxes, however many confidences tie); only
+    // when the pass runs out of it before max_det boxes are kept is segment 1, the
+    // rest, sorted and the pass continued on it. Without selection segment 0 is all n
+    // boxes.
     __shared__ int hist[256];
-    __shared__ uint32_t s_prefix;
+    __shared__ unsigned long long s_prefix;
     __shared__ int s_rem, s_sel;
-    // R a little under a power of two, so that ties at T rarely double the sort size
+    // R a little under a power of two (the sort pads to one)
     const int R = p.max_det * 8 > 3968 ? p.max_det * 8 : 3968;
     const bool select = n > R && R <= kMaxKeys / 2;
-    uint32_t T = 0xFFFFFFFFu;
+    unsigned long long T = ~0ull;
     // ---- 4. one greedy pass in output order ----
     // A box's same-class predecessors in the reference's per-class order all come
     // before it in this order, so deciding boxes in this order keeps exactly the
@@ -328,7 +374,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_nms_kernel(DecodeArgs p) {
     int* flag = reinterpret_cast<int*>(mask + kSub * (kSub / 32));     // 2 * kSub
     __shared__ uint32_t kbits[kSub / 32];
     __shared__ int s_np;
-    constexpr int kWarps = kThreads / 32;
     // 2 ulp(thr) for thr in (0, 1) (used only there)
     const double two_ulp = p.iou > 0.0 && p.iou < 1.0
         ? 2.0 * (__longlong_as_double(__double_as_longlong(p.iou) + 1) - p.iou) : 0.0;
@@ -376,12 +421,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_nms_kernel(DecodeArgs p) {
         if (lane == 0) warp_tot[warp] = __popc(bal);
         __syncthreads();
         if (warp == 0) {
-            int v = warp_tot[lane];
+            int v = lane < kWarps ? warp_tot[lane] : 0;
             for (int o = 1; o < 32; o <<= 1) {
                 const int t2 = __shfl_up_sync(0xffffffffu, v, o);
                 if (lane >= o) v += t2;
             }
-            warp_tot[lane] = v;
+            if (lane < kWarps) warp_tot[lane] = v;
         }
         __syncthreads();
         if (keep) {
@@ -389,26 +434,37 @@ __global__ void __launch_bounds__(kThreads, 1) decode_nms_kernel(DecodeArgs p) {
             sub[q] = d;
             sub_f[q] = outer_bounds(d);
         }
-        if (tid == 0) s_np = dst + warp_tot[31];
+        if (tid == 0) s_np = dst + warp_tot[kWarps - 1];
         __syncthreads();
     };
     for (int seg = 0; seg < 2; ++seg) {
+    // key of candidate i: (conf desc, class group, anchor); the anchor (< 2^14) orders
+    // like the candidate index and locates the record
+    if (seg == 1) compact(false);           // segment 0's sort overwrote the anchor list
     for (int i = tid; i < n; i += kThreads) {
-        const Det& d = cand[i];
-        keys[i] = ((unsigned long long)desc_key(d.conf) << 26) | ((unsigned long long)grp[d.cls] << 16) |
-                  (unsigned long long)i;
+        const int a = (int)keys[i];
+        const int2 cc = *reinterpret_cast<const int2*>(reinterpret_cast<const char*>(cand + a) + 32);   // conf, cls
+        keys[i] = ((unsigned long long)desc_key(__int_as_float(cc.x)) << 26) |
+                  ((unsigned long long)grp[cc.y] << 16) | (unsigned long long)a;
     }
     __syncthreads();
     if (select && seg == 0) {
         if (tid == 0) { s_prefix = 0; s_rem = R; }
         __syncthreads();
-        for (int shift = 24; shift >= 0; shift -= 8) {
+        // keys < 2^58: eight 8-bit digits from bit 56 down. Lanes with the same bin add
+        // once per warp (many confidences tie, and a bin hit by a whole warp would
+        // otherwise take 32 serialised atomics).
+        for (int shift = 56; shift >= 0; shift -= 8) {
             for (int i = tid; i < 256; i += kThreads) hist[i] = 0;
             __syncthreads();
-            const uint32_t pre_k = s_prefix;
-            for (int i = tid; i < n; i += kThreads) {
-                const uint32_t dk = (uint32_t)(keys[i] >> 26);
-                if (shift == 24 || (dk >> (shift + 8)) == pre_k) atomicAdd(&hist[(dk >> shift) & 255], 1);
+            const unsigned long long pre_k = s_prefix;
+            for (int i0 = 0; i0 < n; i0 += kThreads) {
+                const int i = i0 + tid;
+                const unsigned long long key = i < n ? keys[i] : 0ull;
+                const bool in = i < n && (shift == 56 || (key >> (shift + 8)) == pre_k);
+                const int bin = in ? (int)((key >> shift) & 255) : -1;
+                const unsigned peers = __match_any_sync(0xffffffffu, bin);
+                if (in && __ffs(peers) - 1 == lane) atomicAdd(&hist[bin], __popc(peers));
             }
             __syncthreads();
             if (warp == 0) {
@@ -426,7 +482,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_nms_kernel(DecodeArgs p) {
                 if (excl < rem && rem <= incl) {
                     int q = 0;
                     while (excl + v[q] < rem) { excl += v[q]; ++q; }
-                    s_prefix = (pre_k << 8) | (uint32_t)(lane * 8 + q);
+                    s_prefix = (pre_k << 8) | (unsigned long long)(lane * 8 + q);
                     s_rem = rem - excl;
                 }
             }
@@ -440,7 +496,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_nms_kernel(DecodeArgs p) {
         unsigned long long mine[kMaxKeys / kThreads];
         int cnt_mine = 0;
         for (int i = tid; i < n; i += kThreads) {
-            const bool in0 = (uint32_t)(keys[i] >> 26) <= T;
+            const bool in0 = keys[i] <= T;
             if (in0 == (seg == 0)) mine[cnt_mine++] = keys[i];
         }
         if (tid == 0) s_sel = 0;
@@ -463,7 +519,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_nms_kernel(DecodeArgs p) {
         // (a) fill the pending list
         while (s_np < kSub && cursor < ns) {
             const int cnt = ns - cursor < kSub ? ns - cursor : kSub;
-            for (int i = tid; i < cnt; i += kThreads) raw[i] = cand[keys[cursor + i] & 0xFFFF];
+            for (int i = tid; i < cnt; i += kThreads) {
+                Det d = cand[keys[cursor + i] & 0xFFFF];
+                d.reserved = 0;                  // the candidate flag is not part of the output
+                raw[i] = d;
+            }
             __syncthreads();
             test_kept(raw, cnt, 0, s_kept);
             __syncthreads();
@@ -568,6 +628,8 @@ void launch_decode_nms(const DecodeArgs& a, cudaStream_t s) {
     if (a.max_det < 0) fail(ENGINE_ERR_INVALID_ARG, "decode: max_det must be >= 0");
     if (a.batch < 0 || a.batch > INT_MAX) fail(ENGINE_ERR_INVALID_ARG, "decode: batch must be in [0, 2^31)");
     if (a.batch == 0) return;
+    if ((uintptr_t)a.work % 16 || (a.max_det > 0 && (uintptr_t)a.dets % 8))
+        fail(ENGINE_ERR_INVALID_ARG, "decode: work must be 16-byte and dets 8-byte aligned");
     const size_t smem = kNmsSmem;
     int dev = 0;
     PB_CUDA(cudaGetDevice(&dev));

@@ -341,6 +341,45 @@ def test_gpu_decode_full_size_against_restatement(y8n_640, max_det, iou, conf):
                (e["x1"], e["y1"], e["x2"], e["y2"], e["conf"], e["cls"])
 
 
+def test_gpu_decode_iou_near_threshold():
+    """Same-class box pairs whose IoU sweeps across iou_thres in steps of ~3e-8: the
+    NMS decides most pairs from float bounds and must leave every close call (within
+    ~1e-6 of the threshold) to the float64 test, so the kept lists equal the restated
+    reference's bit for bit on both sides of the threshold."""
+    from oracle import decode_ref
+    P, thr = 512, 0.45
+    A = 2 * P
+    w = (100.0 + (np.arange(P) - P // 2) * 7.62939453125e-06).astype(np.float32)   # float32 steps near 100
+    d = np.float32(37.93103)                                                      # IoU ~ (w - d) / (w + d) = 0.45
+    cls = np.arange(P) % 80
+    cell = np.arange(P) // 80
+    cx = (60.0 + cell * 300.0).astype(np.float32)
+    cy = (60.0 + (np.arange(P) % 80) * 3.0).astype(np.float32)    # classes differ, so overlap across classes is harmless
+    preds = np.zeros((84, A), np.float32)
+    preds[0, 0::2], preds[0, 1::2] = cx, cx + d
+    preds[1, 0::2], preds[1, 1::2] = cy, cy
+    preds[2, 0::2], preds[2, 1::2] = w, w
+    preds[3, 0::2], preds[3, 1::2] = w, w
+    preds[4 + cls, 2 * np.arange(P)] = 0.9
+    preds[4 + cls, 2 * np.arange(P) + 1] = 0.8
+    # the reference's float64 IoU of each pair: the sweep must straddle the threshold closely
+    x1a, x2a = cx.astype(np.float64) - w * 0.5, cx.astype(np.float64) + w * 0.5
+    cxb = (cx + d).astype(np.float64)
+    x1b, x2b = cxb - w * 0.5, cxb + w * 0.5
+    y1, y2 = cy.astype(np.float64) - w * 0.5, cy.astype(np.float64) + w * 0.5
+    inter = (np.minimum(x2a, x2b) - np.maximum(x1a, x1b)) * (y2 - y1)
+    area = (x2a - x1a) * (y2 - y1)
+    iou = inter / (area + area - inter + 1e-9)
+    assert ((iou > thr) & (iou < thr + 1e-6)).sum() >= 10 and ((iou <= thr) & (iou > thr - 1e-6)).sum() >= 10
+    got = pb.decode_yolo(preds[None], None, 0.25, thr, A)
+    exp = decode_ref.decode(preds, conf_thres=0.25, iou_thres=thr, max_det=A)
+    assert P < len(exp) < A
+    assert len(got) == len(exp)
+    for g, e in zip(got, exp):
+        assert (g["x1"], g["y1"], g["x2"], g["y2"], g["conf"], g["cls"]) == \
+               (e["x1"], e["y1"], e["x2"], e["y2"], e["conf"], e["cls"])
+
+
 # ---------------------------------------------------------------- ops
 def test_elementwise_and_shape_ops():
     rng = np.random.default_rng(4)
