@@ -1020,8 +1020,12 @@ void launch_conv_tc(const ConvArgs& a, int op_dt, int* err, cudaStream_t s) {
         const uint32_t b_st = bres ? 0u : btile;
         const uint32_t st = a_st + b_st;
         const uint32_t fixed_c = fixed + (bres ? bres_all : 0u) + (mode == 2 ? 2u * win_slot : 0u);
-        // two ring slots suffice: more CTAs beat a deeper ring (swept on B200)
-        const int min_st = st == 0 ? 0 : 2;
+        // two ring slots suffice: more CTAs beat a deeper ring (swept on B200), except
+        // for tail chunks (below)
+        // with a tail chunk (two k-blocks per tap, one of them small) a third slot
+        // pays: 80 -> 80 3x3 at 80x80 0.534 -> 0.483 ms; other convs lost with it
+        // (64 -> 80 0.275 -> 0.341, the stride-2 convs 25-35%)
+        const int min_st = st == 0 ? 0 : (tail_ch ? 3 : 2);
         auto room = [&](int n) { return (int64_t)(228u * 1024u) / n - (int64_t)fixed_c; };
         for (int n = max_ctas; n >= 1; --n) {
             if (room(n) >= 0 && room(n) >= (int64_t)min_st * st) {

@@ -38,11 +38,12 @@ constexpr int kMaxKeys = 16384;
 constexpr int kMaxClasses = 1024;
 constexpr int kSub = 256;          // boxes settled per greedy sub-block
 constexpr int kKeptSmem = 512;     // kept boxes mirrored in shared memory
+constexpr int kClsTab = 4096;      // per-class lists of mirrored kept boxes (entries in all)
 // keys | class first/group | raw chunk (kSub) + pending survivors (2 kSub) Det records |
 // kept boxes' float bounds + classes (kKeptSmem) | pending boxes' float bounds (2 kSub) |
-// in-block matrix | survivor flags
+// in-block matrix | survivor flags | per-class kept lists
 constexpr size_t kNmsSmem = kMaxKeys * 8 + 2 * kMaxClasses * 4 + 3 * kSub * 48 + kKeptSmem * 20 +
-                            2 * kSub * 16 + kSub * (kSub / 32) * 4 + 2 * kSub * 4;
+                            2 * kSub * 16 + kSub * (kSub / 32) * 4 + 2 * kSub * 4 + kClsTab * 4;
 
 struct Det {
     double x1, y1, x2, y2;
@@ -334,6 +335,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_nms_kernel(DecodeArgs p) {
         grp[c] = g;
     }
     __syncthreads();
+    // the class-first array becomes the per-class kept counts (all zero)
+    for (int c = tid; c < kMaxClasses; c += kThreads) first[c] = 0;
+    __syncthreads();
 
     // ---- 3. the output order: (conf desc, class group, index) ----
     // The greedy pass below settles boxes in this order and stops at max_det kept, so
@@ -372,18 +376,53 @@ __global__ void __launch_bounds__(kThreads, 1) decode_nms_kernel(DecodeArgs p) {
     // non-overlapping pairs skip the float64 IoU when IoU 0 cannot exceed the threshold
     const bool prefilter = p.iou >= 0.0;
     int* flag = reinterpret_cast<int*>(mask + kSub * (kSub / 32));     // 2 * kSub
+    // kept boxes below kKeptSmem listed by class: cls_tab[cls * cap + e], e < cls_cnt[cls]
+    // (the class-first array, free once the group ranks exist); a class with more than
+    // cap of them is scanned instead
+    int* cls_tab = flag + 2 * kSub;                                    // kClsTab
+    int* cls_cnt = first;
+    const int cap = kClsTab / (nc > 64 ? nc : 64) < 64 ? kClsTab / (nc > 64 ? nc : 64) : 64;
     __shared__ uint32_t kbits[kSub / 32];
     __shared__ int s_np;
     // 2 ulp(thr) for thr in (0, 1) (used only there)
     const double two_ulp = p.iou > 0.0 && p.iou < 1.0
         ? 2.0 * (__longlong_as_double(__double_as_longlong(p.iou) + 1) - p.iou) : 0.0;
     // flag[j] = 1 when box j of `list` (cnt <= kSub boxes) is suppressed by a kept box in
-    // [k0, k1). Lanes take the boxes (32 per warp); the warps sharing a group of 32 split
-    // the kept range, so every kept box is read by all lanes at once (a broadcast).
+    // [k0, k1). Kept boxes below kKeptSmem: four threads per box (consecutive lanes)
+    // split its class's list (or, for a class past its list's capacity, the mirrored
+    // kept range). Kept boxes from kKeptSmem on (max_det above the mirror): lanes take
+    // the boxes (32 per warp) and the warps sharing a group of 32 split that kept range,
+    // so every kept box is read by all lanes at once.
     auto test_kept = [&](const Det* list, int cnt, int k0, int k1) {
-        if (tid < cnt) flag[tid] = 0;
-        __syncthreads();
-        const int groups = (cnt + 31) >> 5;
+        {
+            const int j = tid >> 2, q = tid & 3;
+            const int lim = k1 < kKeptSmem ? k1 : kKeptSmem;
+            bool sup = false;
+            if (j < cnt && k0 < lim) {
+                const Det c = list[j];
+                const float4 cf = outer_bounds(c);
+                const int nk = cls_cnt[c.cls];
+                if (nk <= cap) {
+                    const int* tab = cls_tab + c.cls * cap;
+                    for (int e = q; e < nk && !sup; e += 4) {
+                        const int r = tab[e];
+                        if (r >= k0 && r < lim && !(prefilter && apart(kept_f[r], cf)) &&
+                            iou_exceeds(out[r], c, p.iou, two_ulp))
+                            sup = true;
+                    }
+                } else {
+                    for (int r = k0 + q; r < lim && !sup; r += 4)
+                        if (kept_c[r] == c.cls && !(prefilter && apart(kept_f[r], cf)) &&
+                            iou_exceeds(out[r], c, p.iou, two_ulp))
+                            sup = true;
+                }
+            }
+            const unsigned bal = __ballot_sync(0xffffffffu, sup);
+            if (q == 0 && j < cnt) flag[j] = ((bal >> (lane & ~3)) & 0xFu) ? 1 : 0;
+        }
+        const int s0 = k0 > kKeptSmem ? k0 : kKeptSmem;
+        if (k1 > s0) __syncthreads();           // the scan below adds to the results above
+        const int groups = k1 > s0 ? (cnt + 31) >> 5 : 0;
         if (groups > 0) {
             const int slices = kWarps / groups;
             const int gsel = warp % groups, slice = warp / groups;
@@ -394,18 +433,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_nms_kernel(DecodeArgs p) {
             const float4 cf = valid ? outer_bounds(c) : make_float4(0.f, 0.f, 0.f, 0.f);
             bool sup = !valid;
             if (slice < slices) {
-                for (int r = k0 + slice; r < k1; r += slices) {
+                for (int r = s0 + slice; r < k1; r += slices) {
                     if (!sup) {
-                        if (r < kKeptSmem) {
-                            if (kept_c[r] == c.cls && !(prefilter && apart(kept_f[r], cf)) &&
-                                iou_exceeds(out[r], c, p.iou, two_ulp))
-                                sup = true;
-                        } else {
-                            const Det& o = out[r];
-                            if (o.cls == c.cls && iou_exceeds(o, c, p.iou, two_ulp)) sup = true;
-                        }
+                        const Det& o = out[r];
+                        if (o.cls == c.cls && iou_exceeds(o, c, p.iou, two_ulp)) sup = true;
                     }
-                    if (((r - k0) & 7) == 7 && __all_sync(0xffffffffu, sup)) break;
+                    if (((r - s0) & 7) == 7 && __all_sync(0xffffffffu, sup)) break;
                 }
             }
             if (valid && sup) flag[j] = 1;
@@ -590,6 +623,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_nms_kernel(DecodeArgs p) {
             if (pos < kKeptSmem) {
                 kept_f[pos] = sub_f[tid];
                 kept_c[pos] = sub[tid].cls;
+                const int slot = atomicAdd(&cls_cnt[sub[tid].cls], 1);
+                if (slot < cap) cls_tab[sub[tid].cls * cap + slot] = pos;
             }
         }
         __syncthreads();

@@ -397,6 +397,70 @@ __global__ void __launch_bounds__(256) maxpool_s1_tile_kernel(Pool2dArgs a, int 
     }
 }
 
+// Chained stride-1 'same' max pools (SPPF) of one image's slice of gc channel cells:
+// the input is loaded once into shared memory, then each pool of the chain runs a row
+// pass into `rows` and a column pass back into `cells`, storing its result. Indices are
+// split by shifts (gc is a power of two) and a multiply-shift by W (exact for the
+// pixel counts allowed here: pix < 2^16), so no integer division runs per element.
+struct PoolChainArgs {
+    Pool2dArgs a;
+    TView out[3];
+    int n, gc_log2;
+    uint32_t w_magic;        // ceil(2^16 / W): pix / W == (pix * w_magic) >> 16 (see launch_maxpool_chain)
+};
+
+template <bool BF>
+__global__ void __launch_bounds__(256) maxpool_chain_kernel(PoolChainArgs P) {
+    extern __shared__ uint4 cells[];        // [H][W][gc] current map, then [H][W][gc] row maxima
+    constexpr int kVec = BF ? 8 : 4;
+    constexpr int kEsz = BF ? 2 : 4;
+    const Pool2dArgs& a = P.a;
+    const int H = (int)a.in.shape[1], W = (int)a.in.shape[2];
+    const int gc = 1 << P.gc_log2, gmask = gc - 1;
+    const int HW = H * W, total = HW * gc;
+    uint4* const rows = cells + total;
+    const int64_t b = blockIdx.y;
+    const int g0 = blockIdx.x * gc;
+    const char* const in = static_cast<const char*>(a.in.ptr) + (b * a.in.img_stride + (int64_t)g0 * kVec) * kEsz;
+    for (int i = threadIdx.x; i < total; i += blockDim.x) {
+        const int c = i & gmask, pix = i >> P.gc_log2;
+        const int h = (int)((uint32_t)pix * P.w_magic >> 16), w = pix - h * W;
+        cells[i] = *reinterpret_cast<const uint4*>(in + (h * a.in.stride[1] + w * a.in.stride[2] + c * kVec) * kEsz);
+    }
+    for (int k = 0; k < P.n; ++k) {
+        __syncthreads();
+        for (int i = threadIdx.x; i < total; i += blockDim.x) {
+            const int c = i & gmask, pix = i >> P.gc_log2;
+            const int h = (int)((uint32_t)pix * P.w_magic >> 16), w = pix - h * W;
+            float best[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) best[j] = -FLT_MAX;
+            for (int t = 0; t < a.kw; ++t) {
+                const int ww = w - a.pw + t;
+                if (ww >= 0 && ww < W) cell_max<BF>(best, cells[((h * W + ww) << P.gc_log2) + c]);
+            }
+            rows[i] = cell_pack<BF>(best);
+        }
+        __syncthreads();
+        const TView& o = P.out[k];
+        char* const out = static_cast<char*>(const_cast<void*>(o.ptr)) + (b * o.img_stride + (int64_t)g0 * kVec) * kEsz;
+        for (int i = threadIdx.x; i < total; i += blockDim.x) {
+            const int c = i & gmask, pix = i >> P.gc_log2;
+            const int h = (int)((uint32_t)pix * P.w_magic >> 16), w = pix - h * W;
+            float best[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) best[j] = -FLT_MAX;
+            for (int t = 0; t < a.kh; ++t) {
+                const int hh = h - a.ph + t;
+                if (hh >= 0 && hh < H) cell_max<BF>(best, rows[((hh * W + w) << P.gc_log2) + c]);
+            }
+            const uint4 v = cell_pack<BF>(best);
+            cells[i] = v;                    // the next pool's input (rows only are read above)
+            *reinterpret_cast<uint4*>(out + (h * o.stride[1] + w * o.stride[2] + c * kVec) * kEsz) = v;
+        }
+    }
+}
+
 // Nearest 2x upsample (out(h, w) = in(h / 2, w / 2), the reference's floor(h * Hin / H)
 // for an exact factor of two): one thread reads one 16-byte channel cell and writes
 // it to its four output pixels.
@@ -526,6 +590,57 @@ void launch_pool2d(const Pool2dArgs& a, cudaStream_t s) {
     }
     pool2d_kernel<<<grid_for(total, 256), 256, 0, s>>>(a, total);
     PB_CUDA(cudaGetLastError());
+}
+
+// The chain kernel's configuration (log2 of the channel cells per CTA), or -1 when the
+// shapes or layouts do not allow it.
+static int maxpool_chain_cells_log2(const Pool2dArgs& a, const TView* out, int n) {
+    if (n < 1 || n > 3 || a.mode != 0 || a.sh != 1 || a.sw != 1 || a.batch > 65535 || a.batch < 1) return -1;
+    const int64_t H = a.in.shape[1], W = a.in.shape[2];
+    // 'same' pooling (the output is the next pool's input) with an in-image tap in every window
+    if (a.kh != 2 * a.ph + 1 || a.kw != 2 * a.pw + 1 || H * W >= 4096 || W < 1) return -1;
+    // pix * w_magic / 2^16 = pix / W + d with w_magic = 2^16 / W + e, 0 <= e < 1, so
+    // 0 <= d < pix / 2^16 < H * W / 2^16; the floor stays pix / W while d < 1 / W, i.e.
+    // for H * W * W <= 2^16 (SPPF's 20 x 20 maps: 8000)
+    if (H * W * W > 65536) return -1;
+    if (!nhwc_vec16(a.in)) return -1;
+    for (int k = 0; k < n; ++k)
+        if (out[k].dt != a.in.dt || !nhwc_vec16(out[k]) || out[k].shape[1] != H || out[k].shape[2] != W ||
+            out[k].shape[3] != a.in.shape[3])
+            return -1;
+    const int vec = a.in.dt == BF16 ? 8 : 4;
+    const int G = (int)(a.in.shape[3] / vec);
+    const int64_t per_cell = 2 * H * W * 16;
+    int lg = -1;
+    for (int l = 4; l >= 0; --l)
+        if (G % (1 << l) == 0 && per_cell * (1 << l) <= 48 * 1024) { lg = l; break; }
+    // keep at least two CTAs per SM busy
+    while (lg > 0 && (G >> lg) * a.batch < 296) --lg;
+    return lg;
+}
+
+bool maxpool_chain_supported(const Pool2dArgs& a, const TView* out, int n) {
+    return maxpool_chain_cells_log2(a, out, n) >= 0;
+}
+
+bool launch_maxpool_chain(const Pool2dArgs& a, const TView* out, int n, cudaStream_t s) {
+    const int lg = maxpool_chain_cells_log2(a, out, n);
+    if (lg < 0) return false;
+    const int64_t H = a.in.shape[1], W = a.in.shape[2];
+    const int G = (int)(a.in.shape[3] / (a.in.dt == BF16 ? 8 : 4));
+    const int64_t per_cell = 2 * H * W * 16;
+    PoolChainArgs P;
+    P.a = a;
+    for (int k = 0; k < n; ++k) P.out[k] = out[k];
+    P.n = n;
+    P.gc_log2 = lg;
+    P.w_magic = (uint32_t)((65536 + W - 1) / W);
+    const dim3 grid((unsigned)(G >> lg), (unsigned)a.batch);
+    const size_t smem = (size_t)per_cell << lg;
+    if (a.in.dt == BF16) maxpool_chain_kernel<true><<<grid, 256, smem, s>>>(P);
+    else maxpool_chain_kernel<false><<<grid, 256, smem, s>>>(P);
+    PB_CUDA(cudaGetLastError());
+    return true;
 }
 
 void launch_resize_nearest(const TView& in, const TView& out, int64_t batch, cudaStream_t s) {

@@ -1245,6 +1245,37 @@ struct PlanBuilder {
             a.mode = (n.op == Op::MaxPool2d ? 0 : 1) + (nt.mode == 1 ? 2 : 0);
             a.batch = B;
             kind("pool");
+            // SPPF: the next two max pools with the same parameters that each read the
+            // previous one's output run in the same launch (the input is read once); they
+            // are not emitted again
+            std::vector<int> chain;
+            if (a.mode == 0) {
+                int cur = ni;
+                for (size_t j = (size_t)ni + 1; j < nodes.size() && chain.size() < 2; ++j) {
+                    const Node& m = nodes[j];
+                    if (skip[j] || m.op != Op::MaxPool2d || note[j].mode != 0 || m.inputs.empty() ||
+                        m.inputs[0] != nodes[cur].outputs[0] || m.params.kernel_h != n.params.kernel_h ||
+                        m.params.kernel_w != n.params.kernel_w || m.params.stride_h != n.params.stride_h ||
+                        m.params.stride_w != n.params.stride_w || m.params.pad_h != n.params.pad_h ||
+                        m.params.pad_w != n.params.pad_w)
+                        continue;
+                    chain.push_back((int)j);
+                    cur = (int)j;
+                }
+            }
+            if (!chain.empty()) {
+                TView outs[3];
+                outs[0] = a.out;
+                for (size_t k = 0; k < chain.size(); ++k) outs[k + 1] = view(vid[nodes[chain[k]].outputs[0]]);
+                const int cnt = 1 + (int)chain.size();
+                if (maxpool_chain_supported(a, outs, cnt)) {
+                    for (int j : chain) skip[j] = 1;
+                    add_step(n.name, [a, outs, cnt](cudaStream_t s) {
+                        if (!launch_maxpool_chain(a, outs, cnt, s)) fail(ENGINE_ERR_RUNTIME, "max pool chain: layout changed");
+                    });
+                    return;
+                }
+            }
             add_step(n.name, [a](cudaStream_t s) { launch_pool2d(a, s); });
             return;
         }

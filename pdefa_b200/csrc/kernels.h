@@ -61,6 +61,11 @@ struct Pool2dArgs {
     int64_t batch;
 };
 void launch_pool2d(const Pool2dArgs& a, cudaStream_t s);
+// A chain of n <= 3 identical stride-1 'same' max pools (SPPF: y1 = pool(x), y2 =
+// pool(y1), y3 = pool(y2)) in one launch: x is read once, every y_k written to out[k].
+// Returns false (nothing launched) when the shapes or layouts do not allow it.
+bool launch_maxpool_chain(const Pool2dArgs& a, const TView* out, int n, cudaStream_t s);
+bool maxpool_chain_supported(const Pool2dArgs& a, const TView* out, int n);
 // Nearest resize: out(h,w) = in(min(floor(h*Hin/H), Hin-1), ...) (session_ops_shape.inc:182-196).
 void launch_resize_nearest(const TView& in, const TView& out, int64_t batch, cudaStream_t s);
 
