@@ -434,6 +434,13 @@ __device__ __forceinline__ bool group_bar_or(int grp, bool pred) {
 // accumulator wait, with the first residual chunk; TMEM is read two chunks per
 // wait. With tma_store each group stages its chunks in shared memory and one of its
 // threads TMA-stores them (full, coalesced rows; the tensor map clips rows past M).
+// Hands the accumulator back to the MMA warp once this warp's TMEM loads have landed.
+__device__ __forceinline__ void tmem_release(uint64_t* tempty_buf, int lane) {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncwarp();
+    if (lane == 0) mbar_arrive(tempty_buf);
+}
+
 template <int ACT, int EPI>
 __device__ void epilogue_loop(const TcParams& p, const CUtensorMap* tmOut, uint8_t* staging, uint32_t tmem,
                               uint64_t* tfull, uint64_t* tempty, volatile int* abort_flag,
@@ -493,32 +500,55 @@ __device__ void epilogue_loop(const TcParams& p, const CUtensorMap* tmOut, uint8
         }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)buf * p.bufcols;
-        // EPI = 8 reads two chunks per TMEM wait; EPI = 4 reads one (fewer registers,
-        // so four CTAs fit per SM)
-        constexpr int PAIR = EPI == 8 ? 2 : 1;
-        for (int c = grp; c < nchunks; c += PAIR * G) {
-            const bool two = PAIR == 2 && c + G < nchunks;
-            uint32_t r0[16], r1[16];
-            tmem_ld16_async(tbase + (uint32_t)(16 * c), r0);
-            if (two) tmem_ld16_async(tbase + (uint32_t)(16 * (c + G)), r1);
-            tmem_wait_ld();
+        // EPI = 4 hands the accumulator back to the MMA warp as soon as this warp's last
+        // TMEM load has landed, before that chunk's math and stores: the next tile's
+        // MMAs then wait for the loads only (3x3 64 -> 80 at 80x80 -9%, 64 -> 64 -4%).
+        if (EPI == 8) {
+            // two chunks per TMEM wait
+            for (int c = grp; c < nchunks; c += 2 * G) {
+                const bool two = c + G < nchunks;
+                uint32_t r0[16], r1[16];
+                tmem_ld16_async(tbase + (uint32_t)(16 * c), r0);
+                if (two) tmem_ld16_async(tbase + (uint32_t)(16 * (c + G)), r1);
+                tmem_wait_ld();
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                if (h == 1 && !two) break;
-                const int cc = c + G * h;           // chunk index
-                const uint4 rc[4] = {rn[0], rn[1], rn[2], rn[3]};
-                if (p.res && live && cc + G < nchunks) load_res_chunk(p, rb + 16 * (cc + G), rn);
+                for (int h = 0; h < 2; ++h) {
+                    if (h == 1 && !two) break;
+                    const int cc = c + G * h;           // chunk index
+                    const uint4 rc[4] = {rn[0], rn[1], rn[2], rn[3]};
+                    if (p.res && live && cc + G < nchunks) load_res_chunk(p, rb + 16 * (cc + G), rn);
+                    float v[16];
+#pragma unroll
+                    for (int k = 0; k < 16; ++k) v[k] = __uint_as_float(h ? r1[k] : r0[k]);
+                    epilogue_math<ACT>(p, v, rc, n0 + 16 * cc);
+                    if (p.tma_store) store_chunk_staging(p, v, staging + cc * chunk_bytes, row);
+                    else if (live) store_chunk_global(p, v, ob + 16 * cc);
+                }
+            }
+        } else {
+            // one chunk per TMEM wait (EPI = 4: fewer registers, so four CTAs fit per SM);
+            // the last chunk is peeled so the release sits outside the loop
+            auto chunk = [&](int cc, bool last) {
+                uint32_t r0[16];
+                tmem_ld16_async(tbase + (uint32_t)(16 * cc), r0);
+                tmem_wait_ld();
+                if (last) tmem_release(tempty + buf, lane);
                 float v[16];
 #pragma unroll
-                for (int k = 0; k < 16; ++k) v[k] = __uint_as_float(h ? r1[k] : r0[k]);
+                for (int k = 0; k < 16; ++k) v[k] = __uint_as_float(r0[k]);
+                const uint4 rc[4] = {rn[0], rn[1], rn[2], rn[3]};
+                if (p.res && live && cc + G < nchunks) load_res_chunk(p, rb + 16 * (cc + G), rn);
                 epilogue_math<ACT>(p, v, rc, n0 + 16 * cc);
                 if (p.tma_store) store_chunk_staging(p, v, staging + cc * chunk_bytes, row);
                 else if (live) store_chunk_global(p, v, ob + 16 * cc);
-            }
+            };
+            int cc = grp;
+            for (; cc + G < nchunks; cc += G) chunk(cc, false);
+            if (cc < nchunks) chunk(cc, true);
         }
-        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty[buf]);
+        // EPI = 8 releases after its loop (an earlier release there cost the 1x1 convs
+        // 5-12% in register spills); a group without columns releases here too
+        if (EPI == 8 || grp >= nchunks) tmem_release(tempty + buf, lane);
         if (p.tma_store) {
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             group_bar(grp);
@@ -950,15 +980,25 @@ void launch_conv_tc(const ConvArgs& a, int op_dt, int* err, cudaStream_t s) {
     while (p.bufcols < (uint32_t)bn) p.bufcols <<= 1;
     p.nbuf = 2;
     p.tmem_cols = 2 * (int)p.bufcols;                   // two accumulators (four when TMEM allows, below)
+    int dev = 0;
+    PB_CUDA(cudaGetDevice(&dev));
+    static int sm_count[64] = {};
+    int sms = 148;
+    if (dev < 64) {
+        if (!sm_count[dev]) PB_CUDA(cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev));
+        sms = sm_count[dev];
+    }
     {
         // Multi-tap convs with 64 < Cout < 128 (80 for the YOLO class branches) round
         // an accumulator up to 128 columns, so two of them cap TMEM at two CTAs per
-        // SM. One accumulator per CTA allows four CTAs, which measured faster on B200
-        // (128 -> 80 at 40x40: 0.178 -> 0.146 ms, 256 -> 80 at 20x20: 0.097 -> 0.080 ms,
-        // batch 256). For Cout = 128, which fills its columns, two accumulators stay
-        // faster.
+        // SM. One accumulator per CTA allows four CTAs but makes every tile's MMAs wait
+        // for the previous tile's whole epilogue. Measured on B200 (batch 256): the one
+        // layer with at least 8 tiles per CTA slot at four CTAs per SM, 80 -> 80 3x3 at
+        // 80x80, runs 0.480 ms with one accumulator against 0.521 with two; the smaller
+        // ones are faster with two (128 -> 80 at 40x40 0.117 -> 0.108 ms, 256 -> 80 at
+        // 20x20 0.064 -> 0.059, 80 -> 80 at 20x20 0.044 -> 0.040).
         const bool one_ = a.kh == 1 && a.kw == 1 && a.sh == 1 && a.sw == 1 && a.ph == 0 && a.pw == 0;
-        if (!one_ && bn > 64 && bn < 128) {
+        if (!one_ && bn > 64 && bn < 128 && (M + BM - 1) / BM >= (int64_t)8 * 4 * sms) {
             p.nbuf = 1;
             p.tmem_cols = (int)p.bufcols;
         }
@@ -1173,14 +1213,6 @@ void launch_conv_tc(const ConvArgs& a, int op_dt, int* err, cudaStream_t s) {
     p.div_wo = make_fastdiv((uint32_t)Wo);
     const size_t smem = (size_t)stages * stage2 + p.staging_bytes + (size_t)p.hstages * p.halo_bytes + p.bres_bytes +
                         1024 + kBarrierBytes;
-    int dev = 0;
-    PB_CUDA(cudaGetDevice(&dev));
-    static int sm_count[64] = {};
-    int sms = 148;
-    if (dev < 64) {
-        if (!sm_count[dev]) PB_CUDA(cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev));
-        sms = sm_count[dev];
-    }
     const int64_t tiles = p.m_tiles * p.n_tiles;
     dim3 grid((unsigned)std::min<int64_t>(tiles, (int64_t)sms * ctas));
     static bool attr[10][64] = {};
