@@ -182,6 +182,97 @@ __global__ void __launch_bounds__(kHeadAnchors) yolo_head_tile_kernel(YoloHeadAr
     }
 }
 
+// BF16 variant as a persistent kernel: each thread owns one anchor slot of the
+// 64-anchor tiles its CTA walks (tile = blockIdx.x + n*gridDim.x) and prefetches its
+// own anchor's next row (chunks x 16-byte cp.async; the row is contiguous in NHWC)
+// into the other half of a double buffer while it computes the current one. No
+// thread reads another's row, so there are no block barriers, and the HBM reads of
+// tile n+1 overlap the special-function work of tile n (which the one-tile-per-CTA
+// kernel above serialises with its own loads). Same arithmetic as its BF16 path.
+__device__ __forceinline__ void head_cp16(uint4* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+                 : "memory");
+}
+
+__global__ void __launch_bounds__(kHeadAnchors) yolo_head_stream_kernel(YoloHeadArgs a, int tiles, int chunks,
+                                                                        int row_chunks, int total_tiles) {
+    constexpr int kReg = 16;
+    constexpr int kPer = 8;                            // bf16 values per 16-byte chunk
+    extern __shared__ uint4 rows[];                    // [2][kHeadAnchors][row_chunks]
+    const int j = threadIdx.x;
+    const int64_t A = a.A;
+    // this thread's anchor of tile t: image b, index i; false past the last anchor
+    auto anchor_of = [&](int t, int64_t& b, int64_t& i) {
+        const int bt = t / tiles;
+        b = bt;
+        i = (int64_t)(t - bt * tiles) * kHeadAnchors + j;
+        return i < A;
+    };
+    auto issue = [&](int t, uint4* dst) {
+        int64_t b, i;
+        if (!anchor_of(t, b, i)) return;
+        int lvl = 0;
+        int64_t li = i;
+        while (lvl < a.nlevels - 1 && li >= a.level_anchors[lvl]) { li -= a.level_anchors[lvl]; ++lvl; }
+        const TView& v = a.level[lvl];
+        const int W = (int)v.shape[2];
+        const int h = (int)li / W, w = (int)li - h * W;
+        const uint4* src = reinterpret_cast<const uint4*>(static_cast<const char*>(v.ptr) +
+                                                          (b * v.img_stride + h * v.stride[1] + w * v.stride[2]) * 2);
+        for (int q = 0; q < chunks; ++q) head_cp16(dst + q, src + q);
+    };
+    // this thread's row in buffer k is rows + (k * kHeadAnchors + j) * row_chunks
+    int k = 0;
+    if ((int)blockIdx.x < total_tiles) issue(blockIdx.x, rows + j * row_chunks);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, k ^= 1) {
+        const int tn = t + (int)gridDim.x;
+        if (tn < total_tiles) issue(tn, rows + ((k ^ 1) * kHeadAnchors + j) * row_chunks);
+        // one group per tile (possibly empty), so "all but the newest" is tile t's row
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        asm volatile("cp.async.wait_group 1;" ::: "memory");
+        int64_t b, i;
+        if (!anchor_of(t, b, i)) continue;
+        const uint4* const row = rows + (k * kHeadAnchors + j) * row_chunks;
+        float dist[4];
+#pragma unroll
+        for (int side = 0; side < 4; ++side) {
+            float x[kReg];
+#pragma unroll
+            for (int c = 0; c < kReg / kPer; ++c) unpack8<true>(row[side * (kReg / kPer) + c], x + c * kPer);
+            float mx = -1e30f;
+#pragma unroll
+            for (int q = 0; q < kReg; ++q) mx = fmaxf(mx, x[q]);
+            float sum = 0.0f;
+#pragma unroll
+            for (int q = 0; q < kReg; ++q) { x[q] = __expf(x[q] - mx); sum += x[q]; }
+            const float inv = sum > 0.0f ? head_rcp(sum) : 0.0f;
+            float d = 0.0f;
+#pragma unroll
+            for (int q = 0; q < kReg; ++q) d = fmaf(x[q] * inv, a.dfl_w[q], d);
+            dist[side] = d;
+        }
+        const float ax = a.anchors[i], ay = a.anchors[A + i], st = a.strides[i];
+        const float x1 = __fsub_rn(ax, dist[0]), y1 = __fsub_rn(ay, dist[1]);
+        const float x2 = __fadd_rn(ax, dist[2]), y2 = __fadd_rn(ay, dist[3]);
+        const float cx = __fdiv_rn(__fadd_rn(x1, x2), 2.0f), cy = __fdiv_rn(__fadd_rn(y1, y2), 2.0f);
+        const float bw = __fsub_rn(x2, x1), bh = __fsub_rn(y2, y1);
+        float* o = a.out + b * (int64_t)(4 + a.nc) * A + i;
+        o[0] = __fmul_rn(cx, st);
+        o[A] = __fmul_rn(cy, st);
+        o[2 * A] = __fmul_rn(bw, st);
+        o[3 * A] = __fmul_rn(bh, st);
+        const int cls_chunks = a.nc / kPer;
+        for (int c = 0; c < cls_chunks; ++c) {
+            float z[kPer];
+            unpack8<true>(row[4 * kReg / kPer + c], z);
+#pragma unroll
+            for (int e = 0; e < kPer; ++e) o[(4 + c * kPer + e) * A] = fmaf(0.5f, head_tanh(0.5f * z[e]), 0.5f);
+        }
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+}
+
 bool head_tileable(const YoloHeadArgs& a) {
     if (a.reg_max != 16 || a.nlevels < 1 || a.nlevels > 3) return false;
     const int dt = a.level[0].dt;
@@ -210,6 +301,27 @@ void launch_yolo_head(const YoloHeadArgs& a, cudaStream_t s) {
         const int tiles = (int)((a.A + kHeadAnchors - 1) / kHeadAnchors);
         const int64_t blocks = (int64_t)tiles * a.batch;
         const size_t smem = (size_t)kHeadAnchors * row_chunks * 16;
+        if (bf && blocks < (int64_t(1) << 31) && 2 * smem <= 48 * 1024) {
+            // persistent grid: as many CTAs as fit on the device at once
+            int dev = 0;
+            PB_CUDA(cudaGetDevice(&dev));
+            static int per_sm[64] = {}, sms[64] = {};
+            int ps = 4, ns = 148;
+            if (dev >= 0 && dev < 64) {
+                if (!sms[dev]) {
+                    PB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm[dev], yolo_head_stream_kernel,
+                                                                          kHeadAnchors, 2 * smem));
+                    PB_CUDA(cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev));
+                }
+                ps = per_sm[dev] > 0 ? per_sm[dev] : 1;
+                ns = sms[dev];
+            }
+            const int64_t grid = std::min<int64_t>(blocks, (int64_t)ps * ns);
+            yolo_head_stream_kernel<<<(unsigned)grid, kHeadAnchors, 2 * smem, s>>>(a, tiles, chunks, row_chunks,
+                                                                                   (int)blocks);
+            PB_CUDA(cudaGetLastError());
+            return;
+        }
         if (blocks < (int64_t(1) << 31) && smem <= 48 * 1024) {
             if (bf) yolo_head_tile_kernel<true><<<(unsigned)blocks, kHeadAnchors, smem, s>>>(a, tiles, chunks, row_chunks);
             else yolo_head_tile_kernel<false><<<(unsigned)blocks, kHeadAnchors, smem, s>>>(a, tiles, chunks, row_chunks);
