@@ -922,6 +922,18 @@ bool pixel_dense(const TView& v) {
 
 }  // namespace
 
+bool encode_f32_box_map(void* map, const void* ptr, const uint64_t dims[4], const uint64_t strides_bytes[3],
+                        const uint32_t box[4]) {
+    load_driver_fns();
+    cuuint64_t d[4] = {dims[0], dims[1], dims[2], dims[3]};
+    cuuint64_t st[3] = {strides_bytes[0], strides_bytes[1], strides_bytes[2]};
+    cuuint32_t bx[4] = {box[0], box[1], box[2], box[3]};
+    cuuint32_t es[4] = {1, 1, 1, 1};
+    return g_tiled(static_cast<CUtensorMap*>(map), CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<void*>(ptr), d, st,
+                   bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 bool conv_tc_supported(const ConvArgs& a, int op_dt, const char** why) {
     const int esz = op_dt == BF16 ? 2 : 4;
     auto no = [&](const char* m) { if (why) *why = m; return false; };
