@@ -345,7 +345,11 @@ __device__ __forceinline__ void stem_region_load(const StemTileParams& P, int64_
 // = 108 bytes, as 27 pieces of 4 bytes; W % 4 == 0 and the region starts at a multiple
 // of 4 pixels, so each group of three pieces (four pixels) is all in or all out.
 constexpr int kRegU8Row = kRegW * 3;                       // 108 bytes
-constexpr int kRegU8Bytes = (kRegH * kRegU8Row + 15) & ~15;
+// In shared memory a region row sits at pitch 112 and byte offset 4: the layout of a
+// TMA box that starts 4 bytes earlier, at a 16-byte boundary (see stem_region_tma_u8)
+constexpr int kRegU8Pitch = 112;
+constexpr int kRegU8Off = 4;
+constexpr int kRegU8Bytes = (kRegH * kRegU8Pitch + 127) & ~127;
 
 __device__ __forceinline__ void cp_async4_u8(uint32_t dst, const void* src, bool in) {
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(in ? 4 : 0) : "memory");
@@ -362,7 +366,7 @@ __device__ __forceinline__ void stem_region_load_u8(const StemTileParams& P, int
         const int hi = h0 + row, px = c0 + 4 * (j / 3);
         const bool ok = hi >= 0 && hi < H && px >= 0 && px < W;
         const uint8_t* src = ok ? img + ((int64_t)hi * W + c0) * 3 + 4 * j : P.u8;
-        cp_async4_u8(smem_u32(dst + row * kRegU8Row + 4 * j), src, ok);
+        cp_async4_u8(smem_u32(dst + row * kRegU8Pitch + kRegU8Off + 4 * j), src, ok);
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
 }
@@ -382,6 +386,23 @@ __device__ __forceinline__ void stem_region_tma(const StemTileParams& P, const C
         "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], [%2];"
         ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(h0), "r"(0),
           "r"((int)b)
+        : "memory");
+}
+
+// The 8-bit frames' region as one 3-D TMA box [112 bytes, 17 rows, 1 image] of the
+// [N, H, W*3] byte view: the region's 108 bytes start at byte 96*tw - 12, so the box
+// starts 4 bytes earlier, at 96*tw - 16 (a 16-byte boundary, as TMA requires of the
+// innermost coordinate; negative at the left edge, where it reads zeros).
+__device__ __forceinline__ void stem_region_tma_u8(const StemTileParams& P, const CUtensorMap* map, uint64_t* bar,
+                                                   uint8_t* dst, int64_t t) {
+    const uint32_t b = stem_div((uint32_t)t, P.div_img);
+    const int r = (int)((uint32_t)t - b * P.div_img.d);
+    const int th = (int)stem_div((uint32_t)r, P.div_tw), tw = r - th * P.tiles_w;
+    const int h0 = th * (2 * kTileH) - 1, x0 = (tw * (2 * kTileW) - 4) * 3 - kRegU8Off;
+    mbar_expect_tx(bar, kRegH * kRegU8Pitch);
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];"
+        ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x0), "r"(h0), "r"((int)b)
         : "memory");
 }
 
@@ -406,7 +427,7 @@ __global__ void __launch_bounds__(128, 8) conv_stem_tile_kernel(const StemTilePa
     volatile int* const abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     float* const sBias = reinterpret_cast<float*>(mbar + 2);     // [cout], 16-byte aligned
     uint64_t* const rbar = reinterpret_cast<uint64_t*>(sBias + ((cout + 3) & ~3));   // [2] region slots (TMA)
-    const bool tma = !U8 && P.tma_region;
+    const bool tma = P.tma_region != 0;
 
     const int tid = threadIdx.x, warp = tid >> 5;
     if (tid == 0) *abort_flag = *reinterpret_cast<volatile int*>(P.err) != 0;
@@ -422,9 +443,16 @@ __global__ void __launch_bounds__(128, 8) conv_stem_tile_kernel(const StemTilePa
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if ((int64_t)blockIdx.x < P.tiles) {
-        if (U8) stem_region_load_u8(P, blockIdx.x, reinterpret_cast<uint8_t*>(sR0), H, W);
-        else if (tma) { if (tid == 0) stem_region_tma(P, &tmR, &rbar[0], sR0, blockIdx.x); }
-        else stem_region_load(P, blockIdx.x, sR0, H, W);
+        if (tma) {
+            if (tid == 0) {
+                if (U8) stem_region_tma_u8(P, &tmR, &rbar[0], reinterpret_cast<uint8_t*>(sR0), blockIdx.x);
+                else stem_region_tma(P, &tmR, &rbar[0], sR0, blockIdx.x);
+            }
+        } else if (U8) {
+            stem_region_load_u8(P, blockIdx.x, reinterpret_cast<uint8_t*>(sR0), H, W);
+        } else {
+            stem_region_load(P, blockIdx.x, sR0, H, W);
+        }
         r_issued = tma ? 1 : 0;
     }
 
@@ -467,16 +495,17 @@ __global__ void __launch_bounds__(128, 8) conv_stem_tile_kernel(const StemTilePa
         float* const cur = (it & 1) ? sR1 : sR0;
         float* const nxt = (it & 1) ? sR0 : sR1;
         if (tn < P.tiles) {
-            if (U8) {
-                stem_region_load_u8(P, tn, reinterpret_cast<uint8_t*>(nxt), H, W);
-            } else if (tma) {
+            if (tma) {
                 if (tid == 0) {
                     // the slot's previous region was read (generic proxy) before the
                     // last barrier; order those reads before the async-proxy write
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                    stem_region_tma(P, &tmR, &rbar[r_issued & 1], nxt, tn);
+                    if (U8) stem_region_tma_u8(P, &tmR, &rbar[r_issued & 1], reinterpret_cast<uint8_t*>(nxt), tn);
+                    else stem_region_tma(P, &tmR, &rbar[r_issued & 1], nxt, tn);
                 }
                 ++r_issued;
+            } else if (U8) {
+                stem_region_load_u8(P, tn, reinterpret_cast<uint8_t*>(nxt), H, W);
             } else {
                 stem_region_load(P, tn, nxt, H, W);
             }
@@ -499,14 +528,15 @@ __global__ void __launch_bounds__(128, 8) conv_stem_tile_kernel(const StemTilePa
             float v[32];
             if (U8) {
                 // pixel * scale: the identity letterbox's value, bit for bit
-                const uint8_t* cu = reinterpret_cast<const uint8_t*>(cur) + 2 * py * kRegU8Row + (2 * px + 3) * 3;
+                const uint8_t* cu =
+                    reinterpret_cast<const uint8_t*>(cur) + 2 * py * kRegU8Pitch + kRegU8Off + (2 * px + 3) * 3;
 #pragma unroll
                 for (int kr = 0; kr < 3; ++kr)
 #pragma unroll
                     for (int ks = 0; ks < 3; ++ks)
 #pragma unroll
                         for (int c = 0; c < 3; ++c)
-                            v[(kr * 3 + ks) * 3 + c] = __fmul_rn((float)cu[kr * kRegU8Row + ks * 3 + c], P.u8_scale);
+                            v[(kr * 3 + ks) * 3 + c] = __fmul_rn((float)cu[kr * kRegU8Pitch + ks * 3 + c], P.u8_scale);
             } else {
 #pragma unroll
                 for (int c = 0; c < 3; ++c)
@@ -680,7 +710,14 @@ void launch_conv_stem_tc(const ConvArgs& a, int* err, cudaStream_t s) {
             const uint64_t st[3] = {(uint64_t)(a.in.stride[1] * esz_in), (uint64_t)(a.in.stride[3] * esz_in),
                                     (uint64_t)(a.in.img_stride * esz_in)};
             const uint32_t box[4] = {(uint32_t)kRegW, (uint32_t)kRegH, 3, 1};
-            T.tma_region = encode_f32_box_map(&tmR, a.in.ptr, dims, st, box) ? 1 : 0;
+            T.tma_region = encode_box_map(&tmR, 4, 4, a.in.ptr, dims, st, box) ? 1 : 0;
+        } else if (((uintptr_t)a.in_u8 % 16) == 0 && (a.in.shape[2] * 3) % 16 == 0) {
+            // [N, H, W*3] bytes: rows of W*3 bytes (a multiple of 16), images of H*W*3
+            const int64_t Wb = a.in.shape[2] * 3, Hh = a.in.shape[1];
+            const uint64_t dims[3] = {(uint64_t)Wb, (uint64_t)Hh, (uint64_t)a.batch};
+            const uint64_t st[2] = {(uint64_t)Wb, (uint64_t)(Wb * Hh)};
+            const uint32_t box[3] = {(uint32_t)kRegU8Pitch, (uint32_t)kRegH, 1};
+            T.tma_region = encode_box_map(&tmR, 1, 3, a.in_u8, dims, st, box) ? 1 : 0;
         }
         const size_t rbytes = u8 ? (size_t)kRegU8Bytes : (size_t)((3 * kRegPlane * 4 + 127) & ~127);
         // tail: barrier, TMEM slot, flag (16 B), the biases (cout floats), the two

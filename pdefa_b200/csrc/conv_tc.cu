@@ -922,15 +922,17 @@ bool pixel_dense(const TView& v) {
 
 }  // namespace
 
-bool encode_f32_box_map(void* map, const void* ptr, const uint64_t dims[4], const uint64_t strides_bytes[3],
-                        const uint32_t box[4]) {
+bool encode_box_map(void* map, int elem_bytes, int rank, const void* ptr, const uint64_t* dims,
+                    const uint64_t* strides_bytes, const uint32_t* box) {
+    if (rank < 1 || rank > 5 || (elem_bytes != 1 && elem_bytes != 4)) return false;
     load_driver_fns();
-    cuuint64_t d[4] = {dims[0], dims[1], dims[2], dims[3]};
-    cuuint64_t st[3] = {strides_bytes[0], strides_bytes[1], strides_bytes[2]};
-    cuuint32_t bx[4] = {box[0], box[1], box[2], box[3]};
-    cuuint32_t es[4] = {1, 1, 1, 1};
-    return g_tiled(static_cast<CUtensorMap*>(map), CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<void*>(ptr), d, st,
-                   bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+    cuuint64_t d[5], st[4];
+    cuuint32_t bx[5], es[5];
+    for (int i = 0; i < rank; ++i) { d[i] = dims[i]; bx[i] = box[i]; es[i] = 1; }
+    for (int i = 0; i + 1 < rank; ++i) st[i] = strides_bytes[i];
+    return g_tiled(static_cast<CUtensorMap*>(map),
+                   elem_bytes == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, (cuuint32_t)rank,
+                   const_cast<void*>(ptr), d, st, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 

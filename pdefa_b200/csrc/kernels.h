@@ -104,11 +104,11 @@ void launch_conv_direct(const ConvArgs& a, cudaStream_t s);
 // tcgen05 stem conv (BF16): kh*kw*Cin <= 32, Cout % 16 == 0 (<= 256), bf16 output, no
 // residual; threads gather im2col rows into shared memory. weight: as launch_conv_simt.
 // err: device error word for bounded waits.
-// 4-D fp32 TMA tensor map (dims innermost first, byte strides of dims 1-3, box), no
-// swizzle, zero fill out of bounds; `map` is a 64-byte-aligned CUtensorMap. False when
-// the driver refuses the parameters.
-bool encode_f32_box_map(void* map, const void* ptr, const uint64_t dims[4], const uint64_t strides_bytes[3],
-                        const uint32_t box[4]);
+// TMA tensor map over uint8 (elem_bytes 1) or fp32 (4) data of `rank` dims (innermost
+// first; byte strides of dims 1..rank-1), no swizzle, zero fill out of bounds; `map`
+// is a 64-byte-aligned CUtensorMap. False when the driver refuses the parameters.
+bool encode_box_map(void* map, int elem_bytes, int rank, const void* ptr, const uint64_t* dims,
+                    const uint64_t* strides_bytes, const uint32_t* box);
 bool conv_stem_tc_supported(const ConvArgs& a);
 void launch_conv_stem_tc(const ConvArgs& a, int* err, cudaStream_t s);
 
