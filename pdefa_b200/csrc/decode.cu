@@ -1,7 +1,8 @@
 // Batched YOLO decode + class-wise greedy NMS, bit-exact with the reference's
 // pure-Python decode_yolo / _nms / _iou (pdefa/python/src/pdefa/_bindings.py:1095-1212).
 //
-// A grid-wide pass evaluates every anchor, then one CTA (1024 threads) per image:
+// A grid-wide pass evaluates every anchor, then one CTA per image (512 threads, two
+// CTAs per SM, when its keys fit half an SM's shared memory; else 1024 threads):
 //  1. candidates in anchor order: class argmax (strict '>', first maximum wins),
 //     skip when best < conf; box (cx - w*0.5, cy - h*0.5, cx + w*0.5, cy + h*0.5) in
 //     float64; optional letterbox unmap (v - pad) * (1.0 / ratio) clamped to
@@ -32,18 +33,42 @@ namespace pb {
 
 namespace {
 
-constexpr int kThreads = 1024;
-constexpr int kWarps = kThreads / 32;
 constexpr int kMaxKeys = 16384;
 constexpr int kMaxClasses = 1024;
-constexpr int kSub = 256;          // boxes settled per greedy sub-block
-constexpr int kKeptSmem = 512;     // kept boxes mirrored in shared memory
-constexpr int kClsTab = 4096;      // per-class lists of mirrored kept boxes (entries in all)
-// keys | class first/group | raw chunk (kSub) + pending survivors (2 kSub) Det records |
-// kept boxes' float bounds + classes (kKeptSmem) | pending boxes' float bounds (2 kSub) |
-// in-block matrix | survivor flags | per-class kept lists
-constexpr size_t kNmsSmem = kMaxKeys * 8 + 2 * kMaxClasses * 4 + 3 * kSub * 48 + kKeptSmem * 20 +
-                            2 * kSub * 16 + kSub * (kSub / 32) * 4 + 2 * kSub * 4 + kClsTab * 4;
+
+// Shapes of the per-image NMS CTA. Both give the same output (the greedy pass is
+// exact for any sub-block size); the small one takes 512 threads and about half the
+// shared memory, so two CTAs share an SM and a batch of up to 2 x 148 images runs in
+// one wave.
+//   NT   threads (the kept test takes four per box, so SUB = NT / 4)
+//   SUB  boxes settled per greedy sub-block
+//   KEPT kept boxes mirrored in shared memory (float bounds + class)
+//   TAB  entries of the per-class lists of mirrored kept boxes
+template <int NT_, int KEPT_, int TAB_>
+struct NmsShape {
+    static constexpr int NT = NT_, NW = NT_ / 32, SUB = NT_ / 4, KEPT = KEPT_, TAB = TAB_;
+    // dynamic shared memory after the keys and the class arrays: raw chunk (SUB) +
+    // pending survivors (2 SUB) Det records | kept float bounds + classes (KEPT) |
+    // pending float bounds (2 SUB) | in-block matrix | survivor flags | class lists
+    static constexpr size_t kFixedSmem = 3 * SUB * 48 + KEPT * 20 + 2 * SUB * 16 + SUB * (SUB / 32) * 4 +
+                                         2 * SUB * 4 + TAB * 4;
+};
+using NmsBig = NmsShape<1024, 512, 4096>;
+using NmsSmall = NmsShape<512, 320, 2048>;
+
+// keys (key_cap) | class first/group (2 ncp) | the shape's fixed part
+template <class S>
+constexpr size_t nms_smem(int64_t key_cap, int64_t ncp) {
+    return (size_t)key_cap * 8 + (size_t)ncp * 8 + S::kFixedSmem;
+}
+
+// Size R of the sorted prefix (segment 0) of the greedy order: max_det * 8, at least
+// 3968 (a little under a power of two: the sort pads to one), capped so that the
+// product cannot overflow. It only splits the work; the output does not depend on it.
+__host__ __device__ inline int nms_prefix_rank(int max_det) {
+    if (max_det > (1 << 20)) return 1 << 23;
+    return max_det * 8 > 3968 ? max_det * 8 : 3968;
+}
 
 struct Det {
     double x1, y1, x2, y2;
@@ -120,7 +145,9 @@ __device__ __forceinline__ void cmp_swap_reg(unsigned long long& lo, unsigned lo
     if ((lo > hi) == asc) { const unsigned long long t = lo; lo = hi; hi = t; }
 }
 
+template <int kThreads>
 __device__ void bitonic_sort(unsigned long long* keys, int np) {
+    constexpr int kWarps = kThreads / 32;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     if (np < 128) {
         const int half = np >> 1;
@@ -226,10 +253,15 @@ __global__ void decode_candidates_kernel(DecodeArgs p) {
     }
 }
 
-__global__ void __launch_bounds__(kThreads, 1) decode_nms_kernel(DecodeArgs p) {
-    extern __shared__ unsigned long long keys[];                       // kMaxKeys
-    int* first = reinterpret_cast<int*>(keys + kMaxKeys);              // kMaxClasses
-    int* grp = first + kMaxClasses;          // kMaxClasses: group ranks
+// key_cap: capacity of the key array (>= anchors; 16384 for the big shape); ncp: length
+// of each class array (>= the class count, even, so that the records after them stay
+// 16-byte aligned).
+template <class S>
+__global__ void __launch_bounds__(S::NT, 1024 / S::NT) decode_nms_kernel(DecodeArgs p, int key_cap, int ncp) {
+    constexpr int kThreads = S::NT, kWarps = S::NW, kSub = S::SUB, kKeptSmem = S::KEPT, kClsTab = S::TAB;
+    extern __shared__ unsigned long long keys[];                       // key_cap
+    int* first = reinterpret_cast<int*>(keys + key_cap);               // ncp
+    int* grp = first + ncp;                  // ncp: group ranks
     __shared__ int warp_tot[32];
     __shared__ int s_n, s_kept;
 
@@ -240,7 +272,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_nms_kernel(DecodeArgs p) {
     Det* cand = reinterpret_cast<Det*>(p.work) + (int64_t)b * A;
     Det* out = reinterpret_cast<Det*>(p.dets) + (int64_t)b * p.max_det;
 
-    for (int c = tid; c < kMaxClasses; c += kThreads) first[c] = INT_MAX;
+    for (int c = tid; c < ncp; c += kThreads) first[c] = INT_MAX;
     if (tid == 0) { s_n = 0; s_kept = 0; }
     __syncthreads();
 
@@ -306,7 +338,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_nms_kernel(DecodeArgs p) {
                 if (flag[c]) {
                     const int e = c * kWarps + warp;
                     const int k = base + (e ? chunk_tot[e - 1] : 0) + __popc(bal[c] & ((1u << lane) - 1u));
-                    if (k < kMaxKeys) {
+                    if (k < key_cap) {
                         keys[k] = (unsigned long long)(a0 + c * kThreads + tid);
                         if (classes) atomicMin(&first[cls[c]], k);
                     }
@@ -319,7 +351,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_nms_kernel(DecodeArgs p) {
     };
     compact(true);
     const int n = s_n;
-    if (n > kMaxKeys) {
+    if (n > key_cap) {
         if (tid == 0) p.counts[b] = -1;
         return;
     }
@@ -336,7 +368,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_nms_kernel(DecodeArgs p) {
     }
     __syncthreads();
     // the class-first array becomes the per-class kept counts (all zero)
-    for (int c = tid; c < kMaxClasses; c += kThreads) first[c] = 0;
+    for (int c = tid; c < ncp; c += kThreads) first[c] = 0;
     __syncthreads();
 
     // ---- 3. the output order: (conf desc, class group, index) ----
@@ -350,9 +382,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_nms_kernel(DecodeArgs p) {
     __shared__ int hist[256];
     __shared__ unsigned long long s_prefix;
     __shared__ int s_rem, s_sel;
-    // R a little under a power of two (the sort pads to one)
-    const int R = p.max_det * 8 > 3968 ? p.max_det * 8 : 3968;
-    const bool select = n > R && R <= kMaxKeys / 2;
+    const int R = nms_prefix_rank(p.max_det);
+    const bool select = n > R && R <= key_cap / 2;
     unsigned long long T = ~0ull;
     // ---- 4. one greedy pass in output order ----
     // A box's same-class predecessors in the reference's per-class order all come
@@ -367,7 +398,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_nms_kernel(DecodeArgs p) {
     // pending boxes beyond m are tested against the boxes just kept. Boxes suppressed
     // by earlier rounds never reach the matrix, so with heavy suppression the
     // sequential settle runs over few boxes.
-    Det* raw = reinterpret_cast<Det*>(grp + kMaxClasses);              // kSub
+    Det* raw = reinterpret_cast<Det*>(grp + ncp);                      // kSub
     Det* sub = raw + kSub;                                             // 2 * kSub pending
     float4* kept_f = reinterpret_cast<float4*>(sub + 2 * kSub);         // kKeptSmem float bounds
     int* kept_c = reinterpret_cast<int*>(kept_f + kKeptSmem);          // kKeptSmem classes
@@ -543,7 +574,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_nms_kernel(DecodeArgs p) {
     while (np < ns) np <<= 1;
     for (int i = ns + tid; i < np; i += kThreads) keys[i] = ~0ull;
     __syncthreads();
-    bitonic_sort(keys, np);
+    bitonic_sort<kThreads>(keys, np);
 
     if (tid == 0) s_np = 0;
     __syncthreads();
@@ -657,6 +688,40 @@ size_t decode_work_bytes(int64_t batch, int64_t anchors) {
     return (size_t)batch * (size_t)anchors * sizeof(Det);
 }
 
+namespace {
+
+std::once_flag g_nms_once[64];
+int g_nms_small_budget[64];
+
+// Once per device (the opt-in shared-memory sizes are per-device function attributes;
+// runner threads of several devices may get here at the same time): the big shape's
+// opt-in size, and the dynamic shared memory the small shape may take with two CTAs
+// on an SM (half the SM's shared memory less the per-CTA reservation and the
+// kernel's static part), returned.
+int nms_setup(int dev) {
+    if (dev < 0 || dev >= 64) fail(ENGINE_ERR_INVALID_ARG, "decode: device index out of range");
+    std::call_once(g_nms_once[dev], [dev] {
+        PB_CUDA(cudaFuncSetAttribute(decode_nms_kernel<NmsBig>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)nms_smem<NmsBig>(kMaxKeys, kMaxClasses)));
+        int per_sm = 0, reserved = 0;
+        PB_CUDA(cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev));
+        PB_CUDA(cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev));
+        cudaFuncAttributes fa{};
+        PB_CUDA(cudaFuncGetAttributes(&fa, decode_nms_kernel<NmsSmall>));
+        int budget = (per_sm / 2 - reserved - (int)fa.sharedSizeBytes) & ~15;
+        if (budget > 0) {
+            PB_CUDA(cudaFuncSetAttribute(decode_nms_kernel<NmsSmall>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         budget));
+            PB_CUDA(cudaFuncSetAttribute(decode_nms_kernel<NmsSmall>,
+                                         cudaFuncAttributePreferredSharedMemoryCarveout, 100));
+        }
+        g_nms_small_budget[dev] = budget > 0 ? budget : 0;
+    });
+    return g_nms_small_budget[dev];
+}
+
+}  // namespace
+
 void launch_decode_nms(const DecodeArgs& a, cudaStream_t s) {
     if (a.anchors > kMaxKeys) fail(ENGINE_ERR_NOT_IMPL, "decode: more than 16384 anchors per image");
     if (a.channels - 4 > kMaxClasses || a.channels < 5) fail(ENGINE_ERR_INVALID_SHAPE, "decode: bad channel count");
@@ -665,20 +730,31 @@ void launch_decode_nms(const DecodeArgs& a, cudaStream_t s) {
     if (a.batch == 0) return;
     if ((uintptr_t)a.work % 16 || (a.max_det > 0 && (uintptr_t)a.dets % 8))
         fail(ENGINE_ERR_INVALID_ARG, "decode: work must be 16-byte and dets 8-byte aligned");
-    const size_t smem = kNmsSmem;
     int dev = 0;
     PB_CUDA(cudaGetDevice(&dev));
-    // the opt-in shared-memory size is a per-device function attribute, set once
-    // per device (runner threads of several devices may get here at the same time)
-    static std::atomic<bool> set[64] = {};
-    if (dev < 0 || dev >= 64 || !set[dev].load(std::memory_order_acquire)) {
-        PB_CUDA(cudaFuncSetAttribute(decode_nms_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        if (dev >= 0 && dev < 64) set[dev].store(true, std::memory_order_release);
+    const int small_budget = nms_setup(dev);
+    const int ncp = ((int)a.channels - 4 + 1) & ~1;
+    // The small shape's key array must hold every candidate (<= anchors), the padded
+    // sort of segment 0 (< 2 R) and of segment 1 (the power of two >= anchors - R), and
+    // R <= key_cap / 2 so that more than R candidates always take the select.
+    const int64_t R = nms_prefix_rank(a.max_det);
+    int64_t cap = a.anchors > 2 * R ? a.anchors : 2 * R;
+    if (a.anchors > R) {
+        int64_t q = 1;
+        while (q < a.anchors - R) q <<= 1;
+        if (q > cap) cap = q;
     }
+    cap = (cap + 1) & ~int64_t(1);
     int64_t cblocks = (a.batch * a.anchors + 255) / 256;
     if (cblocks > 148 * 16) cblocks = 148 * 16;
     if (cblocks > 0) decode_candidates_kernel<<<(unsigned)cblocks, 256, 0, s>>>(a);
-    decode_nms_kernel<<<(unsigned)a.batch, kThreads, smem, s>>>(a);
+    if (cap <= kMaxKeys && nms_smem<NmsSmall>(cap, ncp) <= (size_t)small_budget) {
+        decode_nms_kernel<NmsSmall><<<(unsigned)a.batch, NmsSmall::NT, nms_smem<NmsSmall>(cap, ncp), s>>>(
+            a, (int)cap, ncp);
+    } else {
+        decode_nms_kernel<NmsBig><<<(unsigned)a.batch, NmsBig::NT, nms_smem<NmsBig>(kMaxKeys, ncp), s>>>(
+            a, kMaxKeys, ncp);
+    }
     PB_CUDA(cudaGetLastError());
 }
 
