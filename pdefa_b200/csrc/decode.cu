@@ -48,10 +48,9 @@ template <int NT_, int KEPT_, int TAB_>
 struct NmsShape {
     static constexpr int NT = NT_, NW = NT_ / 32, SUB = NT_ / 4, KEPT = KEPT_, TAB = TAB_;
     // dynamic shared memory after the keys and the class arrays: raw chunk (SUB) +
-    // pending survivors (2 SUB) Det records | kept float bounds + classes (KEPT) |
-    // pending float bounds (2 SUB) | in-block matrix | survivor flags | class lists
-    static constexpr size_t kFixedSmem = 3 * SUB * 48 + KEPT * 20 + 2 * SUB * 16 + SUB * (SUB / 32) * 4 +
-                                         2 * SUB * 4 + TAB * 4;
+    // pending survivors (2 SUB) Det records | kept bounds + areas + classes (KEPT) |
+    // survivor flags (SUB) | class lists
+    static constexpr size_t kFixedSmem = 3 * SUB * 48 + KEPT * 44 + SUB * 4 + TAB * 4;
 };
 using NmsBig = NmsShape<1024, 512, 4096>;
 using NmsSmall = NmsShape<512, 320, 2048>;
@@ -78,6 +77,10 @@ struct Det {
     int32_t reserved;
 };
 static_assert(sizeof(Det) == 48, "Det must match PdefaDetection");
+// a kept box's bounds and area, mirrored in shared memory for the kept test
+struct Box {
+    double x1, y1, x2, y2, area;
+};
 // the NMS reads a record's tail (conf, cls, anchor, reserved) as one 16-byte load
 static_assert(offsetof(Det, conf) == 32 && offsetof(Det, cls) == 36 && offsetof(Det, anchor) == 40 &&
                   offsetof(Det, reserved) == 44,
@@ -97,7 +100,19 @@ __device__ __forceinline__ uint32_t desc_key(float f) {
 // a double and rounding is monotone). e > 2 ulp(thr) D: q - thr > ulp(thr) even after
 // e's rounding, so rn(q) > thr. Only q within ~2 ulp above thr (and odd inputs:
 // thr outside (0,1), D <= 0 or NaN) take the division.
-__device__ __forceinline__ bool iou_exceeds(const Det& a, const Det& b, double thr, double two_ulp_thr) {
+__device__ __forceinline__ double box_area(double x1, double y1, double x2, double y2) {
+    return __dmul_rn(__dsub_rn(x2, x1), __dsub_rn(y2, y1));
+}
+template <class B>
+__device__ __forceinline__ double box_area(const B& b) {
+    return box_area(b.x1, b.y1, b.x2, b.y2);
+}
+
+// area_a and area_b are box_area(a) and box_area(b), passed in so that a box tested
+// against many others computes its own once.
+template <class BA, class BB>
+__device__ __forceinline__ bool iou_exceeds(const BA& a, double area_a, const BB& b, double area_b, double thr,
+                                            double two_ulp_thr) {
     const double x1 = a.x1 > b.x1 ? a.x1 : b.x1;
     const double y1 = a.y1 > b.y1 ? a.y1 : b.y1;
     const double x2 = a.x2 < b.x2 ? a.x2 : b.x2;
@@ -106,8 +121,6 @@ __device__ __forceinline__ bool iou_exceeds(const Det& a, const Det& b, double t
     const double h = __dsub_rn(y2, y1);
     if (w <= 0.0 || h <= 0.0) return !(0.0 <= thr);
     const double inter = __dmul_rn(w, h);
-    const double area_a = __dmul_rn(__dsub_rn(a.x2, a.x1), __dsub_rn(a.y2, a.y1));
-    const double area_b = __dmul_rn(__dsub_rn(b.x2, b.x1), __dsub_rn(b.y2, b.y1));
     const double D = __dadd_rn(__dsub_rn(__dadd_rn(area_a, area_b), inter), 1e-9);
     if (thr > 0.0 && thr < 1.0 && D > 0.0) {
         const double e = __fma_rn(-thr, D, inter);
@@ -115,18 +128,6 @@ __device__ __forceinline__ bool iou_exceeds(const Det& a, const Det& b, double t
         if (e > __dmul_rn(two_ulp_thr, D)) return true;
     }
     return !(__ddiv_rn(inter, D) <= thr);
-}
-
-// Float bounds of a box, rounded outwards (x1, y1 down; x2, y2 up), and the test that
-// two such boxes cannot overlap: then the exact boxes cannot either (or one is empty),
-// so the reference's IoU is 0. NaN bounds never pass the test.
-__device__ __forceinline__ float4 outer_bounds(const Det& d) {
-    return make_float4(__double2float_rd(d.x1), __double2float_rd(d.y1), __double2float_ru(d.x2),
-                       __double2float_ru(d.y2));
-}
-__device__ __forceinline__ bool apart(const float4& a, const float4& b) {
-    return a.z <= b.x || b.z <= a.x || a.w <= b.y || b.w <= a.y || a.z <= a.x || a.w <= a.y || b.z <= b.x ||
-           b.w <= b.y;
 }
 
 __device__ __forceinline__ double clamp_ref(double v, double hi) {
@@ -390,30 +391,23 @@ __global__ void __launch_bounds__(S::NT, 1024 / S::NT) decode_nms_kernel(DecodeA
     // before it in this order, so deciding boxes in this order keeps exactly the
     // boxes the per-class greedy keeps, and the first max_det kept are the output.
     // Rounds: (a) raw chunks of kSub boxes in order are tested against every box kept
-    // so far (one warp per box, lanes over the kept ones) and the survivors appended,
-    // in order, to a pending list until it holds kSub boxes or the order is exhausted;
-    // (b) the in-block suppression matrix of the first m <= kSub pending boxes (bit i of
-    // row j: box i < j of the same class with IoU not <= thres); (c) one warp settles
-    // them in order with the matrix; (d) kept ones are appended to the output, and the
-    // pending boxes beyond m are tested against the boxes just kept. Boxes suppressed
-    // by earlier rounds never reach the matrix, so with heavy suppression the
-    // sequential settle runs over few boxes.
+    // so far and the survivors appended, in order, to a pending list until it holds
+    // kSub boxes or the order is exhausted; (b) the pending boxes (< 2 kSub, one thread
+    // each) are decided in order: the first one still alive is kept, every later one
+    // of its class with IoU not <= thres dies, and so on, one barrier per kept box.
+    // With heavy suppression most boxes die in (a), against earlier rounds' kept boxes.
     Det* raw = reinterpret_cast<Det*>(grp + ncp);                      // kSub
     Det* sub = raw + kSub;                                             // 2 * kSub pending
-    float4* kept_f = reinterpret_cast<float4*>(sub + 2 * kSub);         // kKeptSmem float bounds
-    int* kept_c = reinterpret_cast<int*>(kept_f + kKeptSmem);          // kKeptSmem classes
-    float4* sub_f = reinterpret_cast<float4*>(kept_c + kKeptSmem);     // 2 * kSub float bounds
-    uint32_t* mask = reinterpret_cast<uint32_t*>(sub_f + 2 * kSub);    // kSub * kSub / 32
-    // non-overlapping pairs skip the float64 IoU when IoU 0 cannot exceed the threshold
-    const bool prefilter = p.iou >= 0.0;
-    int* flag = reinterpret_cast<int*>(mask + kSub * (kSub / 32));     // 2 * kSub
+    Box* kept_b = reinterpret_cast<Box*>(sub + 2 * kSub);              // kKeptSmem kept boxes
+    int* kept_c = reinterpret_cast<int*>(kept_b + kKeptSmem);          // kKeptSmem classes
+    int* flag = kept_c + kKeptSmem;                                    // kSub
     // kept boxes below kKeptSmem listed by class: cls_tab[cls * cap + e], e < cls_cnt[cls]
     // (the class-first array, free once the group ranks exist); a class with more than
     // cap of them is scanned instead
-    int* cls_tab = flag + 2 * kSub;                                    // kClsTab
+    int* cls_tab = flag + kSub;                                        // kClsTab
     int* cls_cnt = first;
     const int cap = kClsTab / (nc > 64 ? nc : 64) < 64 ? kClsTab / (nc > 64 ? nc : 64) : 64;
-    __shared__ uint32_t kbits[kSub / 32];
+    __shared__ uint32_t s_words[2 * (kSub / 16)];
     __shared__ int s_np;
     // 2 ulp(thr) for thr in (0, 1) (used only there)
     const double two_ulp = p.iou > 0.0 && p.iou < 1.0
@@ -421,35 +415,43 @@ __global__ void __launch_bounds__(S::NT, 1024 / S::NT) decode_nms_kernel(DecodeA
     // flag[j] = 1 when box j of `list` (cnt <= kSub boxes) is suppressed by a kept box in
     // [k0, k1). Kept boxes below kKeptSmem: four threads per box (consecutive lanes)
     // split its class's list (or, for a class past its list's capacity, the mirrored
-    // kept range). Kept boxes from kKeptSmem on (max_det above the mirror): lanes take
-    // the boxes (32 per warp) and the warps sharing a group of 32 split that kept range,
-    // so every kept box is read by all lanes at once.
+    // kept range), newest first (the latest kept boxes of a class lie nearest in the
+    // order, so they are the likeliest suppressors), and the four stop together at the
+    // first suppressor any of them finds. Kept boxes from kKeptSmem on (max_det above
+    // the mirror): lanes take the boxes (32 per warp) and the warps sharing a group of
+    // 32 split that kept range, so every kept box is read by all lanes at once.
     auto test_kept = [&](const Det* list, int cnt, int k0, int k1) {
         {
             const int j = tid >> 2, q = tid & 3;
+            const unsigned quad = 0xFu << (lane & ~3);
             const int lim = k1 < kKeptSmem ? k1 : kKeptSmem;
-            bool sup = false;
-            if (j < cnt && k0 < lim) {
-                const Det c = list[j];
-                const float4 cf = outer_bounds(c);
+            bool live = j < cnt && k0 < lim, sup = false, listed = false;
+            Det c;
+            double area_c = 0.0;
+            const int* tab = cls_tab;
+            int e = 0, e_end = 0;
+            if (live) {
+                c = list[j];
+                area_c = box_area(c);
                 const int nk = cls_cnt[c.cls];
-                if (nk <= cap) {
-                    const int* tab = cls_tab + c.cls * cap;
-                    for (int e = q; e < nk && !sup; e += 4) {
-                        const int r = tab[e];
-                        if (r >= k0 && r < lim && !(prefilter && apart(kept_f[r], cf)) &&
-                            iou_exceeds(out[r], c, p.iou, two_ulp))
-                            sup = true;
-                    }
-                } else {
-                    for (int r = k0 + q; r < lim && !sup; r += 4)
-                        if (kept_c[r] == c.cls && !(prefilter && apart(kept_f[r], cf)) &&
-                            iou_exceeds(out[r], c, p.iou, two_ulp))
-                            sup = true;
-                }
+                listed = nk <= cap;
+                tab = cls_tab + c.cls * cap;
+                e = (listed ? nk : lim) - 1 - q;
+                e_end = listed ? 0 : k0;
+                live = e >= e_end;
             }
-            const unsigned bal = __ballot_sync(0xffffffffu, sup);
-            if (q == 0 && j < cnt) flag[j] = ((bal >> (lane & ~3)) & 0xFu) ? 1 : 0;
+            while (__any_sync(0xffffffffu, live)) {
+                bool hit = false;
+                if (live) {
+                    const int r = listed ? tab[e] : e;
+                    hit = (listed ? r >= k0 && r < lim : kept_c[r] == c.cls) &&
+                          iou_exceeds(kept_b[r], kept_b[r].area, c, area_c, p.iou, two_ulp);
+                }
+                if (__ballot_sync(0xffffffffu, hit) & quad) { sup = true; live = false; }
+                e -= 4;
+                if (e < e_end) live = false;
+            }
+            if (q == 0 && j < cnt) flag[j] = sup ? 1 : 0;
         }
         const int s0 = k0 > kKeptSmem ? k0 : kKeptSmem;
         if (k1 > s0) __syncthreads();           // the scan below adds to the results above
@@ -460,14 +462,14 @@ __global__ void __launch_bounds__(S::NT, 1024 / S::NT) decode_nms_kernel(DecodeA
             const int j = gsel * 32 + lane;
             const bool valid = j < cnt && slice < slices;
             Det c;
-            if (valid) c = list[j];
-            const float4 cf = valid ? outer_bounds(c) : make_float4(0.f, 0.f, 0.f, 0.f);
+            double area_c = 0.0;
+            if (valid) { c = list[j]; area_c = box_area(c); }
             bool sup = !valid;
             if (slice < slices) {
                 for (int r = s0 + slice; r < k1; r += slices) {
                     if (!sup) {
                         const Det& o = out[r];
-                        if (o.cls == c.cls && iou_exceeds(o, c, p.iou, two_ulp)) sup = true;
+                        if (o.cls == c.cls && iou_exceeds(o, box_area(o), c, area_c, p.iou, two_ulp)) sup = true;
                     }
                     if (((r - s0) & 7) == 7 && __all_sync(0xffffffffu, sup)) break;
                 }
@@ -493,11 +495,7 @@ __global__ void __launch_bounds__(S::NT, 1024 / S::NT) decode_nms_kernel(DecodeA
             if (lane < kWarps) warp_tot[lane] = v;
         }
         __syncthreads();
-        if (keep) {
-            const int q = dst + (warp ? warp_tot[warp - 1] : 0) + __popc(bal & ((1u << lane) - 1u));
-            sub[q] = d;
-            sub_f[q] = outer_bounds(d);
-        }
+        if (keep) sub[dst + (warp ? warp_tot[warp - 1] : 0) + __popc(bal & ((1u << lane) - 1u))] = d;
         if (tid == 0) s_np = dst + warp_tot[kWarps - 1];
         __syncthreads();
     };
@@ -579,7 +577,7 @@ __global__ void __launch_bounds__(S::NT, 1024 / S::NT) decode_nms_kernel(DecodeA
     if (tid == 0) s_np = 0;
     __syncthreads();
     int cursor = 0;
-    while (s_kept < p.max_det && (cursor < ns || s_np > 0)) {
+    while (s_kept < p.max_det && cursor < ns) {
         // (a) fill the pending list
         while (s_np < kSub && cursor < ns) {
             const int cnt = ns - cursor < kSub ? ns - cursor : kSub;
@@ -590,87 +588,50 @@ __global__ void __launch_bounds__(S::NT, 1024 / S::NT) decode_nms_kernel(DecodeA
             }
             __syncthreads();
             test_kept(raw, cnt, 0, s_kept);
-            __syncthreads();
             append_survivors(raw, cnt, s_np);
             cursor += cnt;
         }
-        const int np = s_np;
-        const int m = np < kSub ? np : kSub;
-        const int kept0 = s_kept;
-        if (tid < kSub / 32) kbits[tid] = 0;
-        // (b) in-block suppression matrix: one warp per row j, a ballot per 32 columns;
-        //     only the words holding some i < j are written (the sweep reads no other)
-        for (int j = warp; j < m; j += kWarps) {
-            const Det c = sub[j];
-            const float4 cf = sub_f[j];
-            for (int w = 0; 32 * w < j; ++w) {
-                const int i = 32 * w + lane;
-                bool sup = false;
-                if (i < j) {
-                    const Det& o = sub[i];
-                    sup = o.cls == c.cls && !(prefilter && apart(sub_f[i], cf)) && iou_exceeds(o, c, p.iou, two_ulp);
-                }
-                const uint32_t bits = __ballot_sync(0xffffffffu, sup);
-                if (lane == 0) mask[j * (kSub / 32) + w] = bits;
-            }
-        }
-        __syncthreads();
-        // (c) settle the boxes in order, one 32-box word at a time (warp 0; lane w < 8
-        //     ends up with the kept bits of word w): every lane first tests its box
-        //     against the boxes kept in earlier words, then the word is resolved in order
-        //     with each box's in-word row bits, broadcast by shuffles.
-        if (warp == 0) {
-            uint32_t kbw = 0;
-            int k = kept0;
-            for (int W = 0; 32 * W < m && k < p.max_det; ++W) {
-                const int q = 32 * W + lane;
-                bool sup = q >= m;
-                for (int w = 0; w < W; ++w) {
-                    const uint32_t kw_w = __shfl_sync(0xffffffffu, kbw, w);
-                    if (!sup && (mask[q * (kSub / 32) + w] & kw_w)) sup = true;
-                }
-                // bits of rows i < q of this word (word W of row q is written when lane > 0)
-                const uint32_t intra = (q < m && lane > 0) ? mask[q * (kSub / 32) + W] : 0u;
-                const uint32_t cand_bits = __ballot_sync(0xffffffffu, !sup);
-                uint32_t kw = 0;
-                for (int bq = 0; bq < 32; ++bq) {
-                    const uint32_t row = __shfl_sync(0xffffffffu, intra, bq);
-                    if (((cand_bits >> bq) & 1u) && !(row & kw) && k < p.max_det) {
-                        kw |= 1u << bq;
-                        ++k;
+        // (b) decide the pending boxes in order (threads below 2 kSub, one box each; a
+        //     named barrier over them): per step the warps post their alive boxes, all
+        //     find the first one, its thread keeps it and the later ones test against
+        //     it. The boxes stay in shared memory (few registers live across the steps).
+        if (tid < 2 * kSub) {
+            const int np = s_np;
+            bool alive = tid < np;
+            const int my_cls = alive ? sub[tid].cls : -1;
+            int k = s_kept;
+            for (int step = 0; k < p.max_det; ++step) {
+                uint32_t* words = s_words + (step & 1) * (kSub / 16);
+                const unsigned bal = __ballot_sync(0xffffffffu, alive);
+                if (lane == 0) words[warp] = bal;
+                asm volatile("bar.sync 1, %0;" ::"r"(2 * kSub) : "memory");
+                const unsigned v = lane < kSub / 16 ? words[lane] : 0u;
+                const unsigned nz = __ballot_sync(0xffffffffu, v != 0u);
+                if (!nz) break;
+                const int w0 = __ffs(nz) - 1;
+                const int j0 = w0 * 32 + __ffs(__shfl_sync(0xffffffffu, v, w0)) - 1;
+                if (tid == j0) {
+                    alive = false;
+                    const Det& me = sub[tid];
+                    out[k] = me;
+                    if (k < kKeptSmem) {
+                        kept_b[k] = Box{me.x1, me.y1, me.x2, me.y2, box_area(me)};
+                        kept_c[k] = my_cls;
+                        const int slot = cls_cnt[my_cls]++;
+                        if (slot < cap) cls_tab[my_cls * cap + slot] = k;
                     }
+                } else if (alive && sub[j0].cls == my_cls) {
+                    const Det& o = sub[j0];
+                    const Det& me = sub[tid];
+                    if (iou_exceeds(o, box_area(o), me, box_area(me), p.iou, two_ulp)) alive = false;
                 }
-                if (lane == W) kbw = kw;
+                ++k;
             }
-            if (lane < kSub / 32) kbits[lane] = kbw;
-            if (lane == 0) s_kept = k;
+            if (tid == 0) s_kept = k;
         }
         __syncthreads();
-        // (d) append the kept boxes
-        if (tid < m && ((kbits[tid >> 5] >> (tid & 31)) & 1u)) {
-            int pos = kept0 + __popc(kbits[tid >> 5] & ((1u << (tid & 31)) - 1u));
-            for (int w = 0; w < (tid >> 5); ++w) pos += __popc(kbits[w]);
-            out[pos] = sub[tid];
-            if (pos < kKeptSmem) {
-                kept_f[pos] = sub_f[tid];
-                kept_c[pos] = sub[tid].cls;
-                const int slot = atomicAdd(&cls_cnt[sub[tid].cls], 1);
-                if (slot < cap) cls_tab[sub[tid].cls * cap + slot] = pos;
-            }
-        }
+        if (tid == 0) s_np = 0;
         __syncthreads();
-        // pending boxes beyond m: test against the boxes kept in this round, keep the rest
-        const int rest = np - m;
-        if (rest > 0 && s_kept < p.max_det) {
-            for (int i = tid; i < rest; i += kThreads) raw[i] = sub[m + i];
-            __syncthreads();
-            test_kept(raw, rest, kept0, s_kept);
-            __syncthreads();
-            append_survivors(raw, rest, 0);
-        } else {
-            if (tid == 0) s_np = 0;
-            __syncthreads();
-        }
     }
     if (!select || s_kept >= p.max_det) break;
     __syncthreads();
