@@ -294,6 +294,10 @@ __device__ __forceinline__ float tc_act(float x, float slope) {
     return apply_act(x, ACT, slope, 0.0f);
 }
 
+__device__ __forceinline__ void prefetch_l2(const void* a) {
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(a));
+}
+
 __device__ __forceinline__ void load_res_chunk(const TcParams& p, int64_t rb, uint4 (&r)[4]) {
     const uint4* src = p.res_dt == BF16
         ? reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(p.res) + rb)
@@ -453,33 +457,49 @@ __device__ void epilogue_loop(const TcParams& p, const CUtensorMap* tmOut, uint8
     const bool leader = (warp & 3) == 2 && lane == 0;   // warp 2 / warp 6, lane 0
     const int nchunks = p.bn >> 4;
     const uint32_t chunk_bytes = p.out_dt == BF16 ? 128u * 32u : 128u * 64u;
-    RingPos acc;
-    for (int64_t t = blockIdx.x; t < total; t += gridDim.x, acc.next(p.nbuf)) {
-        const int buf = acc.slot;
-        const uint32_t use = acc.phase;                  // parity of this buffer's fills before
-        const uint32_t mt = fdiv((uint32_t)t, p.div_ntiles);
-        const int n0 = (int)((uint32_t)t - mt * (uint32_t)p.n_tiles) * p.bn;
-        uint32_t b, ho, wo;
-        bool live;
+    // this thread's output pixel (image b, row ho, column wo) and column base n0 in tile t
+    auto locate = [&](int64_t t, uint32_t& mt, int& n0, uint32_t& b, uint32_t& ho, uint32_t& wo) -> bool {
+        mt = fdiv((uint32_t)t, p.div_ntiles);
+        n0 = (int)((uint32_t)t - mt * (uint32_t)p.n_tiles) * p.bn;
         if (p.a_mode == 2) {
             // row -> padded position P of image b; columns x >= Wo are padding
             b = fdiv(mt, p.div_tpi);
             const uint32_t P = (mt - b * p.div_tpi.d) * (uint32_t)BM + (uint32_t)row;
             ho = fdiv(P, p.div_wp);
             wo = P - ho * p.div_wp.d;
-            live = P < p.Q && (int)wo < p.Wo;
-        } else {
-            const uint32_t m = mt * (uint32_t)BM + (uint32_t)row;
-            live = (int64_t)m < p.M;
-            b = fdiv(m, p.div_hw);
-            const uint32_t r = m - b * p.div_hw.d;
-            ho = fdiv(r, p.div_wo);
-            wo = r - ho * p.div_wo.d;
+            return P < p.Q && (int)wo < p.Wo;
         }
+        const uint32_t m = mt * (uint32_t)BM + (uint32_t)row;
+        b = fdiv(m, p.div_hw);
+        const uint32_t r = m - b * p.div_hw.d;
+        ho = fdiv(r, p.div_wo);
+        wo = r - ho * p.div_wo.d;
+        return (int64_t)m < p.M;
+    };
+    RingPos acc;
+    for (int64_t t = blockIdx.x; t < total; t += gridDim.x, acc.next(p.nbuf)) {
+        const int buf = acc.slot;
+        const uint32_t use = acc.phase;                  // parity of this buffer's fills before
+        uint32_t mt, b, ho, wo;
+        int n0;
+        const bool live = locate(t, mt, n0, b, ho, wo);
         int64_t ob = 0, rb = 0;
         if (live) {
             ob = (int64_t)b * p.out_img + (int64_t)ho * p.out_sh + (int64_t)wo * p.out_sw + n0;
             rb = (int64_t)b * p.res_img + (int64_t)ho * p.res_sh + (int64_t)wo * p.res_sw + n0;
+        }
+        // The residual loads below run just before the accumulator wait, so a tile whose
+        // accumulator is ready waits for them: bring this thread's residual pixel of its
+        // next tile into L2 now, a tile ahead.
+        if (p.res && t + gridDim.x < total) {
+            uint32_t mt2, b2, ho2, wo2;
+            int n2;
+            if (locate(t + gridDim.x, mt2, n2, b2, ho2, wo2)) {
+                const int64_t rb2 = (int64_t)b2 * p.res_img + (int64_t)ho2 * p.res_sh + (int64_t)wo2 * p.res_sw + n2;
+                const char* a = static_cast<const char*>(p.res) + rb2 * (p.res_dt == BF16 ? 2 : 4);
+                const int bytes = p.bn * (p.res_dt == BF16 ? 2 : 4);
+                for (int o = 0; o < bytes; o += 128) prefetch_l2(a + o);
+            }
         }
         uint4 rn[4] = {};
         if (p.res && live && grp < nchunks) load_res_chunk(p, rb + 16 * grp, rn);
